@@ -1,0 +1,90 @@
+// Shared helpers for the anemll_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/anemll_b200.h"
+
+namespace anemll {
+
+// ---------------------------------------------------------------- errors ----
+void set_error(const char* fmt, ...);
+
+#define ANEMLL_REQUIRE(cond, code, ...)      \
+  do {                                       \
+    if (!(cond)) {                           \
+      ::anemll::set_error(__VA_ARGS__);      \
+      return (code);                         \
+    }                                        \
+  } while (0)
+
+// Map a launch/runtime error to the positive status range.
+int launch_status(const char* what);
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline int dtype_size(int dt) { return dt == ANEMLL_F32 ? 4 : 2; }
+inline bool dtype_ok(int dt) { return dt == ANEMLL_F32 || dt == ANEMLL_F16 || dt == ANEMLL_BF16; }
+
+// ------------------------------------------------------------ conversions --
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// ------------------------------------------------------------ reductions ---
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float softplus(float x) {
+  // log(1 + e^x), evaluated without overflow (same threshold behaviour as torch's softplus, beta=1, threshold=20)
+  return x > 20.0f ? x : log1pf(__expf(x));
+}
+
+}  // namespace anemll
+
+// Dispatch an element type code to a C++ type alias `T`.
+#define ANEMLL_DISPATCH_DTYPE(code, T, ...)                     \
+  [&]() -> int {                                                \
+    switch (code) {                                             \
+      case ANEMLL_F32: { using T = float; return __VA_ARGS__(); }          \
+      case ANEMLL_F16: { using T = __half; return __VA_ARGS__(); }         \
+      case ANEMLL_BF16: { using T = __nv_bfloat16; return __VA_ARGS__(); } \
+      default:                                                  \
+        ::anemll::set_error("unsupported dtype code %d", (int)(code)); \
+        return ANEMLL_EUNSUPPORTED;                             \
+    }                                                           \
+  }()
+
+#define ANEMLL_DISPATCH_HALF(code, T, ...)                      \
+  [&]() -> int {                                                \
+    switch (code) {                                             \
+      case ANEMLL_F16: { using T = __half; return __VA_ARGS__(); }         \
+      case ANEMLL_BF16: { using T = __nv_bfloat16; return __VA_ARGS__(); } \
+      default:                                                  \
+        ::anemll::set_error("dtype code %d unsupported here (f16/bf16 only)", (int)(code)); \
+        return ANEMLL_EUNSUPPORTED;                             \
+    }                                                           \
+  }()

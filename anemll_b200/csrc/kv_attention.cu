@@ -1,0 +1,473 @@
+// Fixed-shape KV-cache attention with the cache write fused in.
+//
+// One launch handles one prefill chunk (S tokens) or one decode step (S = 1)
+// of one layer.  The G = H_q / H_kv query heads of a kv head are packed into
+// the rows of one tile (row r = token r / G, head r % G), so every K/V tile
+// read from HBM serves all G heads (GQA without the reference's repeat_kv
+// copy).  Keys are split across CTAs (split-KV); each CTA runs an online
+// softmax over its key range with fp32 accumulators and either finishes the
+// rows itself (one split) or leaves unnormalised partials plus (max, sum) in
+// the caller's workspace for kv_combine_kernel.  Only the visible key range
+// [key_lo, key_hi) is visited when the mask is derived from positions.
+//
+// The new rows [pos, pos + S) are read straight from k_new / v_new by the CTA
+// whose split contains them, and row-tile-0 CTAs store them into the cache,
+// so no CTA ever reads a cache row that is being written.
+//
+// Reference semantics: anemll/models/qwen_model.py forward_prefill 509-546,
+// forward_regular 469-507, cache writes 669-675 / 733-745; sigmoid gate of
+// transformers 5.5.0 modeling_qwen3_5.py:689.
+#include "common.cuh"
+#include "mma_sync.cuh"
+
+namespace anemll {
+namespace {
+
+constexpr int NB = 32;  // keys per block
+
+struct KvParams {
+  const void* q;
+  const void* k_new;
+  const void* v_new;
+  const void* gate;
+  void* kc;
+  void* vc;
+  long long bs, hs;
+  const void* mask;
+  int mask_dtype;
+  long long mask_ld;
+  void* out;
+  int B, S, Hq, Hkv, ctx, pos, window, aligned, has_new;
+  int key_lo, key_hi, n_splits, ks;
+  float* ws_o;
+  float* ws_ml;
+  float scale_log2;
+};
+
+__device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
+
+template <typename T, int HD>
+__device__ __forceinline__ void load_rows_async(T* smem, int nrows, const T* const* src_rows, int tid, int nthreads) {
+  constexpr int CPR = HD / 8;  // 16-byte chunks per row
+  for (int i = tid; i < nrows * CPR; i += nthreads) {
+    const int r = i / CPR, c = i % CPR;
+    T* dst = smem + r * HD + swz(r, c) * 8;
+    const T* s = src_rows[r];
+    if (s) cp_async16(dst, s + c * 8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <typename T, int HD, int MW>
+__global__ void __launch_bounds__(MW * 32)
+kv_attn_kernel(KvParams p) {
+  constexpr int ROWS = 16 * MW;
+  constexpr int NT = MW * 32;
+  constexpr int NTILE_O = HD / 8;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  T* Qs = reinterpret_cast<T*>(smem_raw);
+  T* Ks = Qs + ROWS * HD;       // [2][NB][HD]
+  T* Vs = Ks + 2 * NB * HD;     // [2][NB][HD]
+  __shared__ const T* rowptr[ROWS > NB ? ROWS : NB];
+  __shared__ const T* vrowptr[NB];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = p.Hq / p.Hkv;
+  const int R = p.S * G;
+  const int bh = blockIdx.z;
+  const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int split = blockIdx.y;
+  const int r0 = blockIdx.x * ROWS;
+  const int k_begin = p.key_lo + split * p.ks;
+  const int k_end = min(p.key_hi, k_begin + p.ks);
+
+  T* Kc = reinterpret_cast<T*>(p.kc) + (long long)b * p.bs + (long long)kvh * p.hs;
+  T* Vc = reinterpret_cast<T*>(p.vc) + (long long)b * p.bs + (long long)kvh * p.hs;
+  const T* kn = p.has_new ? reinterpret_cast<const T*>(p.k_new) + (long long)(b * p.Hkv + kvh) * p.S * HD : nullptr;
+  const T* vn = p.has_new ? reinterpret_cast<const T*>(p.v_new) + (long long)(b * p.Hkv + kvh) * p.S * HD : nullptr;
+
+  // fused cache write of the new rows that fall in this split
+  if (p.has_new && blockIdx.x == 0) {
+    const int w0 = max(p.pos, k_begin), w1 = min(p.pos + p.S, k_end);
+    constexpr int CPR = HD / 8;
+    for (int i = tid; i < (w1 - w0) * CPR * 2; i += NT) {
+      const int which = i / ((w1 - w0) * CPR);
+      const int rem = i % ((w1 - w0) * CPR);
+      const int j = w0 + rem / CPR, c = rem % CPR;
+      const T* src = (which ? vn : kn) + (long long)(j - p.pos) * HD + c * 8;
+      T* dst = (which ? Vc : Kc) + (long long)j * HD + c * 8;
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+    }
+  }
+
+  // Q tile
+  for (int i = tid; i < ROWS; i += NT) {
+    const int r = r0 + i;
+    if (r < R) {
+      const int s = r / G, h = kvh * G + r % G;
+      rowptr[i] = reinterpret_cast<const T*>(p.q) + ((long long)(b * p.Hq + h) * p.S + s) * HD;
+    } else {
+      rowptr[i] = nullptr;
+    }
+  }
+  __syncthreads();
+  load_rows_async<T, HD>(Qs, ROWS, rowptr, tid, NT);
+  cp_async_commit();
+  __syncthreads();
+
+  auto issue_kv = [&](int kb, int buf) {
+    for (int i = tid; i < NB; i += NT) {
+      const int j = kb + i;
+      const T* kp = nullptr;
+      const T* vp = nullptr;
+      if (j < k_end) {
+        if (p.has_new && j >= p.pos && j < p.pos + p.S) {
+          kp = kn + (long long)(j - p.pos) * HD;
+          vp = vn + (long long)(j - p.pos) * HD;
+        } else {
+          kp = Kc + (long long)j * HD;
+          vp = Vc + (long long)j * HD;
+        }
+      }
+      rowptr[i] = kp;
+      vrowptr[i] = vp;
+    }
+    __syncthreads();
+    load_rows_async<T, HD>(Ks + buf * NB * HD, NB, rowptr, tid, NT);
+    load_rows_async<T, HD>(Vs + buf * NB * HD, NB, vrowptr, tid, NT);
+    cp_async_commit();
+    __syncthreads();
+  };
+
+  const int nblk = (k_end - k_begin + NB - 1) / NB;
+  // per-thread row state: rows g and g+8 of this warp's 16
+  const int g = lane >> 2, t4 = lane & 3;
+  const int wr0 = r0 + warp * 16;
+  int rows_s[2], rows_lo[2], rows_hi[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = wr0 + g + h * 8;
+    const int s = r < R ? r / G : 0;
+    rows_s[h] = s;
+    const int pq = p.pos + s;
+    int lo = 0;
+    if (p.window > 0) lo = p.aligned ? max(0, min(p.pos + p.S, p.ctx) - p.window) : pq - p.window + 1;
+    rows_lo[h] = lo;
+    rows_hi[h] = r < R ? pq : -1;  // inclusive; -1 hides everything for padding rows
+  }
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float o_acc[NTILE_O][4];
+#pragma unroll
+  for (int i = 0; i < NTILE_O; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+
+  if (nblk > 0) issue_kv(k_begin, 0);
+  for (int blk = 0; blk < nblk; ++blk) {
+    const int buf = blk & 1;
+    const int kb = k_begin + blk * NB;
+    if (blk + 1 < nblk) {
+      issue_kv(kb + NB, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const T* Kb = Ks + buf * NB * HD;
+    const T* Vb = Vs + buf * NB * HD;
+
+    // S = Q K^T : 16 rows x NB keys per warp
+    float sc[NB / 8][4];
+#pragma unroll
+    for (int n = 0; n < NB / 8; ++n) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      uint32_t a[4];
+      {
+        const int r = warp * 16 + (lane & 15);
+        const int c = kk * 2 + (lane >> 4);
+        ldmatrix_x4(a, Qs + r * HD + swz(r, c) * 8);
+      }
+#pragma unroll
+      for (int n2 = 0; n2 < NB / 16; ++n2) {
+        uint32_t bfr[4];
+        const int r = n2 * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int c = kk * 2 + ((lane >> 3) & 1);
+        ldmatrix_x4(bfr, Kb + r * HD + swz(r, c) * 8);
+        mma_16816<T>(sc[2 * n2], a, bfr[0], bfr[1]);
+        mma_16816<T>(sc[2 * n2 + 1], a, bfr[2], bfr[3]);
+      }
+    }
+    // scale, mask, online softmax (base-2)
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < NB / 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const int j = kb + n * 8 + t4 * 2 + (e & 1);
+        float v = sc[n][e] * p.scale_log2;
+        bool vis = j < k_end;
+        if (p.mask) {
+          if (vis && rows_hi[h] >= 0) {
+            const long long mi = (long long)rows_s[h] * p.mask_ld + j;
+            const float mv = p.mask_dtype == ANEMLL_F32 ? reinterpret_cast<const float*>(p.mask)[mi]
+                           : p.mask_dtype == ANEMLL_F16 ? __half2float(reinterpret_cast<const __half*>(p.mask)[mi])
+                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.mask)[mi]);
+            v += mv * 1.4426950408889634f;
+          } else {
+            vis = false;
+          }
+          if (v == -INFINITY) vis = false;
+        } else {
+          vis = vis && j <= rows_hi[h] && j >= rows_lo[h];
+        }
+        v = vis ? v : -INFINITY;
+        sc[n][e] = v;
+        mx[h] = fmaxf(mx[h], v);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float mnew = fmaxf(m_run[h], mx[h]);
+      const float base = mnew == -INFINITY ? 0.f : mnew;
+      alpha[h] = exp2f(m_run[h] - base);
+      m_run[h] = mnew;
+      mx[h] = base;  // reuse as subtraction base
+    }
+    float rs[2] = {0.f, 0.f};
+    uint32_t pf[NB / 16][4];
+#pragma unroll
+    for (int n = 0; n < NB / 8; ++n) {
+      const float p0 = exp2f(sc[n][0] - mx[0]);
+      const float p1 = exp2f(sc[n][1] - mx[0]);
+      const float p2 = exp2f(sc[n][2] - mx[1]);
+      const float p3 = exp2f(sc[n][3] - mx[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      const int kk = n >> 1, hi = n & 1;
+      pf[kk][hi * 2 + 0] = pack2<T>(p0, p1);
+      pf[kk][hi * 2 + 1] = pack2<T>(p2, p3);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_run[h] = l_run[h] * alpha[h] + rs[h];
+    }
+#pragma unroll
+    for (int i = 0; i < NTILE_O; ++i) {
+      o_acc[i][0] *= alpha[0];
+      o_acc[i][1] *= alpha[0];
+      o_acc[i][2] *= alpha[1];
+      o_acc[i][3] *= alpha[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < NB / 16; ++kk) {
+      // A fragment order: (row g, k lo), (row g+8, k lo), (row g, k hi), (row g+8, k hi)
+      uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#pragma unroll
+      for (int n2 = 0; n2 < HD / 16; ++n2) {
+        uint32_t bfr[4];
+        const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int c = n2 * 2 + (lane >> 4);
+        ldmatrix_x4_trans(bfr, Vb + r * HD + swz(r, c) * 8);
+        mma_16816<T>(o_acc[2 * n2], a, bfr[0], bfr[1]);
+        mma_16816<T>(o_acc[2 * n2 + 1], a, bfr[2], bfr[3]);
+      }
+    }
+    __syncthreads();
+  }
+
+  // epilogue
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = wr0 + g + h * 8;
+    if (r >= R) continue;
+    const int s = r / G, hq = kvh * G + r % G;
+    if (p.n_splits == 1) {
+      const float inv = 1.f / l_run[h];
+      T* orow = reinterpret_cast<T*>(p.out) + ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD;
+      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + s) * p.Hq * HD +
+                                   (long long)hq * HD
+                             : nullptr;
+#pragma unroll
+      for (int i = 0; i < NTILE_O; ++i) {
+        const int d = i * 8 + t4 * 2;
+        float v0 = o_acc[i][h * 2] * inv, v1 = o_acc[i][h * 2 + 1] * inv;
+        if (grow) {
+          v0 *= 1.f / (1.f + __expf(-to_f32(grow[d])));
+          v1 *= 1.f / (1.f + __expf(-to_f32(grow[d + 1])));
+        }
+        *reinterpret_cast<uint32_t*>(orow + d) = pack2<T>(v0, v1);
+      }
+    } else {
+      const long long row_id = ((long long)bh * p.n_splits + split) * R + r;
+      float* wo = p.ws_o + row_id * HD;
+#pragma unroll
+      for (int i = 0; i < NTILE_O; ++i) {
+        const int d = i * 8 + t4 * 2;
+        *reinterpret_cast<float2*>(wo + d) = make_float2(o_acc[i][h * 2], o_acc[i][h * 2 + 1]);
+      }
+      if (t4 == 0) {
+        p.ws_ml[row_id * 2 + 0] = m_run[h];
+        p.ws_ml[row_id * 2 + 1] = l_run[h];
+      }
+    }
+  }
+}
+
+// Merge the split partials of each row: out = sum_i w_i O_i / sum_i w_i l_i, w_i = 2^(m_i - max m).
+template <typename T, int HD>
+__global__ void __launch_bounds__(HD)
+kv_combine_kernel(KvParams p) {
+  const int G = p.Hq / p.Hkv;
+  const int R = p.S * G;
+  const int r = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int d = threadIdx.x;
+  float M = -INFINITY;
+  for (int i = 0; i < p.n_splits; ++i) M = fmaxf(M, p.ws_ml[(((long long)bh * p.n_splits + i) * R + r) * 2]);
+  const float base = M == -INFINITY ? 0.f : M;
+  float acc = 0.f, L = 0.f;
+  for (int i = 0; i < p.n_splits; ++i) {
+    const long long row_id = ((long long)bh * p.n_splits + i) * R + r;
+    const float w = exp2f(p.ws_ml[row_id * 2] - base);
+    L += w * p.ws_ml[row_id * 2 + 1];
+    acc += w * p.ws_o[row_id * HD + d];
+  }
+  const int s = r / G, hq = kvh * G + r % G;
+  const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
+  float v = acc / L;
+  if (p.gate) v *= 1.f / (1.f + __expf(-to_f32(reinterpret_cast<const T*>(p.gate)[o])));
+  reinterpret_cast<T*>(p.out)[o] = from_f32<T>(v);
+}
+
+struct Plan {
+  int key_lo, key_hi, n_splits, ks, mw, row_tiles;
+  int max_splits;  // bound on n_splits over every key range of this shape (workspace sizing)
+};
+
+Plan make_plan(int B, int S, int Hq, int Hkv, int ctx, int pos, int window, int aligned, bool explicit_mask) {
+  Plan pl;
+  if (explicit_mask) {
+    pl.key_lo = 0;
+    pl.key_hi = ctx;
+  } else {
+    pl.key_hi = min(ctx, pos + S);
+    pl.key_lo = 0;
+    if (window > 0) pl.key_lo = max(0, aligned ? min(pos + S, ctx) - window : pos - window + 1);
+    if (pl.key_lo > pl.key_hi) pl.key_lo = pl.key_hi;
+  }
+  const int R = S * (Hq / Hkv);
+  pl.mw = R <= 16 ? 1 : 4;
+  pl.row_tiles = (R + 16 * pl.mw - 1) / (16 * pl.mw);
+  const int L = pl.key_hi - pl.key_lo;
+  const int nblocks = max(1, (L + NB - 1) / NB);
+  const long base = (long)pl.row_tiles * B * Hkv;
+  const int want_raw = (int)((2L * 148 + base - 1) / base);
+  pl.max_splits = max(1, min(want_raw, min((ctx + NB - 1) / NB, 128)));
+  const int want = max(1, min(want_raw, min(nblocks, 128)));
+  const int bps = (nblocks + want - 1) / want;
+  pl.ks = bps * NB;
+  pl.n_splits = max(1, (L + pl.ks - 1) / pl.ks);
+  return pl;
+}
+
+template <typename T, int HD>
+int launch_kv(KvParams& p, const Plan& pl, cudaStream_t st) {
+  dim3 grid(pl.row_tiles, pl.n_splits, p.B * p.Hkv);
+  if (pl.mw == 1) {
+    const size_t smem = (size_t)(16 * HD + 4 * NB * HD) * sizeof(T);
+    auto kern = kv_attn_kernel<T, HD, 1>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 32, smem, st>>>(p);
+  } else {
+    const size_t smem = (size_t)(64 * HD + 4 * NB * HD) * sizeof(T);
+    auto kern = kv_attn_kernel<T, HD, 4>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<grid, 128, smem, st>>>(p);
+  }
+  int rc = launch_status("kv_attention");
+  if (rc) return rc;
+  if (pl.n_splits > 1) {
+    const int R = p.S * (p.Hq / p.Hkv);
+    dim3 g2(R, p.B * p.Hkv);
+    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(p);
+    rc = launch_status("kv_combine");
+  }
+  return rc;
+}
+
+size_t workspace_bytes_for(int n_splits, int B, int S, int Hq, int Hkv, int hd) {
+  if (n_splits <= 1) return 0;
+  const size_t R = (size_t)S * (Hq / Hkv);
+  return (size_t)B * Hkv * n_splits * R * (hd + 2) * sizeof(float);
+}
+
+}  // namespace
+}  // namespace anemll
+
+using namespace anemll;
+
+extern "C" size_t anemll_kv_attention_workspace_size(int B, int S, int H_q, int H_kv, int head_dim, int ctx) {
+  if (B <= 0 || S <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv || ctx <= 0) return 0;
+  // max_splits bounds the split count of every key range this shape can take
+  Plan pl = make_plan(B, S, H_q, H_kv, ctx, 0, 0, 0, true);
+  return workspace_bytes_for(pl.max_splits, B, S, H_q, H_kv, head_dim);
+}
+
+extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, const void* gate,
+                                   void* k_cache, void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                                   const void* mask, int mask_dtype, int64_t mask_row_stride,
+                                   void* out, int dtype,
+                                   int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                                   int current_pos, int window, int window_chunk_aligned,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  ANEMLL_REQUIRE(q && k_cache && v_cache && out, ANEMLL_EINVAL, "kv_attention: null pointer");
+  ANEMLL_REQUIRE((k_new == nullptr) == (v_new == nullptr), ANEMLL_EINVAL,
+                 "kv_attention: k_new and v_new must both be given or both be NULL");
+  ANEMLL_REQUIRE(B > 0 && S > 0 && H_q > 0 && H_kv > 0 && ctx > 0, ANEMLL_EINVAL, "kv_attention: bad sizes");
+  ANEMLL_REQUIRE(H_q % H_kv == 0, ANEMLL_EINVAL, "kv_attention: H_q %% H_kv != 0");
+  ANEMLL_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, ANEMLL_EUNSUPPORTED,
+                 "kv_attention: head_dim must be 64, 128 or 256 (got %d)", head_dim);
+  ANEMLL_REQUIRE(current_pos >= 0 && current_pos + S <= ctx, ANEMLL_EINVAL,
+                 "kv_attention: positions [%d, %d) exceed the cache length %d", current_pos, current_pos + S, ctx);
+  ANEMLL_REQUIRE(!mask || (mask_dtype == ANEMLL_F32 || mask_dtype == ANEMLL_F16 || mask_dtype == ANEMLL_BF16),
+                 ANEMLL_EUNSUPPORTED, "kv_attention: bad mask dtype");
+  ANEMLL_REQUIRE(!mask || mask_row_stride >= ctx, ANEMLL_EINVAL, "kv_attention: mask row stride < ctx");
+  ANEMLL_REQUIRE(aligned(q, 16) && (!k_new || (aligned(k_new, 16) && aligned(v_new, 16))) && aligned(k_cache, 16) &&
+                     aligned(v_cache, 16) && aligned(out, 4) && (!gate || aligned(gate, 4)),
+                 ANEMLL_EALIGN, "kv_attention: q/k_new/v_new/caches must be 16-byte aligned");
+  ANEMLL_REQUIRE(cache_batch_stride % 8 == 0 && cache_head_stride % 8 == 0, ANEMLL_EALIGN,
+                 "kv_attention: cache strides must be multiples of 8 elements");
+  Plan pl = make_plan(B, S, H_q, H_kv, ctx, current_pos, window, window_chunk_aligned, mask != nullptr);
+  const size_t need = workspace_bytes_for(pl.n_splits, B, S, H_q, H_kv, head_dim);
+  ANEMLL_REQUIRE(workspace_bytes >= need && (need == 0 || workspace), ANEMLL_EWORKSPACE,
+                 "kv_attention: workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  ANEMLL_REQUIRE(!workspace || aligned(workspace, 16), ANEMLL_EALIGN, "kv_attention: workspace must be 16-byte aligned");
+
+  KvParams p;
+  p.q = q; p.k_new = k_new; p.v_new = v_new; p.gate = gate; p.kc = k_cache; p.vc = v_cache;
+  p.bs = cache_batch_stride; p.hs = cache_head_stride;
+  p.mask = mask; p.mask_dtype = mask_dtype; p.mask_ld = mask_row_stride;
+  p.out = out;
+  p.B = B; p.S = S; p.Hq = H_q; p.Hkv = H_kv; p.ctx = ctx;
+  p.pos = current_pos; p.window = window; p.aligned = window_chunk_aligned; p.has_new = k_new != nullptr;
+  p.key_lo = pl.key_lo; p.key_hi = pl.key_hi; p.n_splits = pl.n_splits; p.ks = pl.ks;
+  const size_t R = (size_t)S * (H_q / H_kv);
+  p.ws_o = reinterpret_cast<float*>(workspace);
+  p.ws_ml = p.ws_o ? p.ws_o + (size_t)B * H_kv * pl.n_splits * R * head_dim : nullptr;
+  p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  cudaStream_t st = (cudaStream_t)stream;
+  return ANEMLL_DISPATCH_HALF(dtype, T, [&] {
+    switch (head_dim) {
+      case 64: return launch_kv<T, 64>(p, pl, st);
+      case 128: return launch_kv<T, 128>(p, pl, st);
+      default: return launch_kv<T, 256>(p, pl, st);
+    }
+  });
+}

@@ -1,0 +1,213 @@
+"""Gated delta-rule (GDN) ops and the drop-in layer, on the sm_100a kernels.
+
+Functional ops mirror the third-party interface the Qwen3.5 layer calls
+(transformers 5.5.0 ``modeling_qwen3_5.py``; the reference snapshot has no GDN
+code): ``recurrent_gated_delta_rule`` (314-353), ``causal_conv1d_update`` +
+gates (210-226, 453-496) and ``Qwen3_5RMSNormGated`` (175-190), with the
+same argument names and meaning.  Differences, all deliberate:
+
+* ``query``/``key`` may stay at ``H_qk`` heads (value head ``j`` reads key
+  head ``j // (H_v/H_qk)``), so the ``repeat_interleave`` copy of
+  ``modeling_qwen3_5.py:495-496`` is never materialised;
+* the ``*_`` variants update ``state`` in place (the caller owns it, like the
+  reference's mutable cache buffers); the plain variants clone first and
+  return the final state, as the third-party functions do.
+
+Every op runs a CUDA kernel from ``libanemll_b200.so``; there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+__all__ = [
+    "recurrent_gated_delta_rule",
+    "recurrent_gated_delta_rule_",
+    "gdn_prologue",
+    "gated_rmsnorm",
+    "GatedDeltaNet",
+]
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("anemll_b200 ops take CUDA tensors (no CPU path)")
+
+
+def _need_contig(name, t):
+    if t is not None and not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def recurrent_gated_delta_rule_(query, key, value, g, beta, state, scale=None,
+                                use_qk_l2norm_in_kernel=False, out=None, out_dtype=None):
+    """Token-by-token delta rule, updating ``state`` [B,H_v,d_k,d_v] fp32 in place.
+
+    ``query, key`` [B,T,H_qk,d_k]; ``value`` [B,T,H_v,d_v]; ``g, beta`` [B,T,H_v] fp32.
+    Returns ``out`` [B,T,H_v,d_v] (dtype ``out_dtype``, default ``query.dtype``).
+    """
+    _need_cuda(query, key, value, g, beta, state)
+    for n, t in (("query", query), ("key", key), ("value", value), ("g", g), ("beta", beta), ("state", state)):
+        _need_contig(n, t)
+    if g.dtype != torch.float32 or beta.dtype != torch.float32 or state.dtype != torch.float32:
+        raise TypeError("g, beta and state must be float32")
+    if query.dtype != key.dtype or key.dtype != value.dtype:
+        raise TypeError("query, key and value must share a dtype")
+    B, T, H_qk, d_k = query.shape
+    H_v, d_v = value.shape[2], value.shape[3]
+    if key.shape != query.shape or value.shape[:2] != (B, T) or tuple(state.shape) != (B, H_v, d_k, d_v):
+        raise ValueError("shape mismatch between query/key/value/state")
+    if tuple(g.shape) != (B, T, H_v) or tuple(beta.shape) != (B, T, H_v):
+        raise ValueError("g and beta must be [B, T, H_v]")
+    out_dtype = out_dtype or query.dtype
+    if out is None:
+        out = torch.empty(B, T, H_v, d_v, dtype=out_dtype, device=query.device)
+    rc = _lib.load().anemll_gdn_recurrent(
+        _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), _lib.dtype_code(query.dtype), _lib.ptr(g), _lib.ptr(beta),
+        _lib.ptr(state), _lib.ptr(out), _lib.dtype_code(out.dtype), B, T, H_qk, H_v, d_k, d_v,
+        float(scale) if scale is not None else 0.0, int(bool(use_qk_l2norm_in_kernel)), _lib.stream_ptr(query.device))
+    _lib.check(rc, "anemll_gdn_recurrent")
+    return out
+
+
+def recurrent_gated_delta_rule(query, key, value, g, beta, initial_state=None, output_final_state=False,
+                               use_qk_l2norm_in_kernel=False, scale=None):
+    """Functional form with the third-party signature; returns ``(out, final_state or None)``."""
+    B, T, _, d_k = query.shape
+    H_v, d_v = value.shape[2], value.shape[3]
+    if initial_state is None:
+        state = torch.zeros(B, H_v, d_k, d_v, dtype=torch.float32, device=query.device)
+    else:
+        state = initial_state.to(torch.float32).clone()
+    out = recurrent_gated_delta_rule_(query, key, value, g.float().contiguous(), beta.float().contiguous(), state,
+                                      scale, use_qk_l2norm_in_kernel)
+    return out, (state if output_final_state else None)
+
+
+def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k_heads, num_v_heads,
+                 head_k_dim=128, head_v_dim=128, use_state=True, out_dtype=torch.float16):
+    """conv1d(+SiLU) over ``mixed_qkv`` [B,T,C], split, l2-normalise q/k, gates.
+
+    ``conv_weight`` [C, K] fp32; ``conv_state`` [B, C, K] (dtype of ``mixed_qkv``)
+    is read as history when ``use_state`` and always receives the last K raw
+    inputs.  Returns ``q, k`` [B,T,H_qk,d_k], ``v`` [B,T,H_v,d_v] (``out_dtype``),
+    ``g, beta`` [B,T,H_v] fp32.
+    """
+    _need_cuda(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias)
+    for n, t in (("mixed_qkv", mixed_qkv), ("conv_weight", conv_weight), ("conv_state", conv_state),
+                 ("a", a), ("b", b), ("A_log", A_log)):
+        _need_contig(n, t)
+    B, T, C = mixed_qkv.shape
+    K = conv_weight.shape[1]
+    if C != 2 * num_k_heads * head_k_dim + num_v_heads * head_v_dim:
+        raise ValueError("mixed_qkv width does not match the head configuration")
+    if conv_state.dtype != mixed_qkv.dtype or tuple(conv_state.shape) != (B, C, K):
+        raise ValueError("conv_state must be [B, C, K] in the dtype of mixed_qkv")
+    if conv_weight.dtype != torch.float32 or A_log.dtype != torch.float32:
+        raise TypeError("conv_weight and A_log must be float32")
+    if a.dtype != b.dtype:
+        raise TypeError("a and b must share a dtype")
+    dev = mixed_qkv.device
+    q = torch.empty(B, T, num_k_heads, head_k_dim, dtype=out_dtype, device=dev)
+    k = torch.empty_like(q)
+    v = torch.empty(B, T, num_v_heads, head_v_dim, dtype=out_dtype, device=dev)
+    g = torch.empty(B, T, num_v_heads, dtype=torch.float32, device=dev)
+    beta = torch.empty_like(g)
+    dtb = None if dt_bias is None else dt_bias.float().contiguous()
+    rc = _lib.load().anemll_gdn_prologue(
+        _lib.ptr(mixed_qkv), _lib.dtype_code(mixed_qkv.dtype), _lib.ptr(conv_weight), _lib.ptr(conv_state),
+        _lib.ptr(a), _lib.ptr(b), _lib.dtype_code(a.dtype), _lib.ptr(A_log), _lib.ptr(dtb),
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(out_dtype), _lib.ptr(g), _lib.ptr(beta),
+        B, T, num_k_heads, num_v_heads, head_k_dim, head_v_dim, K, int(bool(use_state)), _lib.stream_ptr(dev))
+    _lib.check(rc, "anemll_gdn_prologue")
+    return q, k, v, g, beta
+
+
+def gated_rmsnorm(x, z, weight, eps=1e-6, out_dtype=None):
+    """``weight * x * rsqrt(mean(x^2)+eps) * silu(z)`` over the last dim."""
+    _need_cuda(x, z, weight)
+    _need_contig("x", x)
+    _need_contig("z", z)
+    d = x.shape[-1]
+    if z.shape != x.shape or weight.shape != (d,):
+        raise ValueError("gated_rmsnorm: shape mismatch")
+    w = weight.float().contiguous()
+    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    rc = _lib.load().anemll_gated_rmsnorm(_lib.ptr(x), _lib.dtype_code(x.dtype), _lib.ptr(z), _lib.dtype_code(z.dtype),
+                                          _lib.ptr(w), _lib.ptr(out), _lib.dtype_code(out.dtype), x.numel() // d, d,
+                                          float(eps), _lib.stream_ptr(x.device))
+    _lib.check(rc, "anemll_gated_rmsnorm")
+    return out
+
+
+class GatedDeltaNet(nn.Module):
+    """Drop-in Qwen3.5 gated-DeltaNet layer (``Qwen3_5GatedDeltaNet``, modeling_qwen3_5.py:356-533).
+
+    Same parameters and projections; the state lives in caller-owned tensors
+    that ``forward`` mutates in place (the reference's mutable-buffer
+    convention): ``conv_state`` [B, C, K] in the activation dtype and
+    ``recurrent_state`` [B, H_v, d_k, d_v] fp32.  ``use_precomputed_states``
+    selects decode semantics (history read from the states), otherwise the
+    call is a fresh prefill that overwrites them.
+    """
+
+    def __init__(self, hidden_size=2048, num_k_heads=16, num_v_heads=32, head_k_dim=128, head_v_dim=128,
+                 conv_kernel=4, eps=1e-6, dtype=torch.bfloat16, core_dtype=torch.float16, chunk_size=64,
+                 device=None):
+        super().__init__()
+        self.hidden_size = hidden_size
+        self.num_k_heads, self.num_v_heads = num_k_heads, num_v_heads
+        self.head_k_dim, self.head_v_dim = head_k_dim, head_v_dim
+        self.key_dim = num_k_heads * head_k_dim
+        self.value_dim = num_v_heads * head_v_dim
+        self.conv_dim = 2 * self.key_dim + self.value_dim
+        self.conv_kernel = conv_kernel
+        self.eps = eps
+        self.core_dtype = core_dtype
+        self.chunk_size = chunk_size
+        fk = dict(device=device, dtype=dtype)
+        self.in_proj_qkv = nn.Linear(hidden_size, self.conv_dim, bias=False, **fk)
+        self.in_proj_z = nn.Linear(hidden_size, self.value_dim, bias=False, **fk)
+        self.in_proj_b = nn.Linear(hidden_size, num_v_heads, bias=False, **fk)
+        self.in_proj_a = nn.Linear(hidden_size, num_v_heads, bias=False, **fk)
+        self.conv_weight = nn.Parameter(torch.zeros(self.conv_dim, conv_kernel, device=device, dtype=torch.float32))
+        self.dt_bias = nn.Parameter(torch.zeros(num_v_heads, device=device, dtype=torch.float32))
+        self.A_log = nn.Parameter(torch.zeros(num_v_heads, device=device, dtype=torch.float32))
+        self.norm_weight = nn.Parameter(torch.ones(head_v_dim, device=device, dtype=torch.float32))
+        self.out_proj = nn.Linear(self.value_dim, hidden_size, bias=False, **fk)
+
+    def new_states(self, batch_size, device=None, dtype=None):
+        device = device or self.in_proj_qkv.weight.device
+        dtype = dtype or self.in_proj_qkv.weight.dtype
+        conv = torch.zeros(batch_size, self.conv_dim, self.conv_kernel, device=device, dtype=dtype)
+        rec = torch.zeros(batch_size, self.num_v_heads, self.head_k_dim, self.head_v_dim, device=device,
+                          dtype=torch.float32)
+        return conv, rec
+
+    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states):
+        """Everything between the input and output projections (the hot path)."""
+        B, T, _ = mixed_qkv.shape
+        if not use_precomputed_states:
+            recurrent_state.zero_()
+        q, k, v, g, beta = gdn_prologue(mixed_qkv.contiguous(), self.conv_weight, conv_state, a.contiguous(),
+                                        b.contiguous(), self.A_log, self.dt_bias, self.num_k_heads,
+                                        self.num_v_heads, self.head_k_dim, self.head_v_dim,
+                                        use_state=use_precomputed_states, out_dtype=self.core_dtype)
+        o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
+        normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim).contiguous(), self.norm_weight,
+                               self.eps, out_dtype=mixed_qkv.dtype)
+        return o, normed
+
+    def forward(self, hidden_states, conv_state, recurrent_state, use_precomputed_states=False):
+        B, T, _ = hidden_states.shape
+        mixed_qkv = self.in_proj_qkv(hidden_states)
+        z = self.in_proj_z(hidden_states)
+        b = self.in_proj_b(hidden_states)
+        a = self.in_proj_a(hidden_states)
+        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states)
+        return self.out_proj(normed.reshape(B, T, self.value_dim))

@@ -1,0 +1,353 @@
+"""Benchmark of the B200 attention hot path (one JSON line on rank 0).
+
+Default workload (the headline): gated delta-rule recurrent decode, batch 64,
+H_qk=16, H_v=32, d_k=d_v=128, fp32 state [64,32,128,128] (128 MiB) updated in
+place, bf16 q/k/v, 256 distinct token inputs cycled.  One step = one decode
+step of the whole batch = one kernel launch.  Weak scaling: every rank owns
+its own batch of 64 sequences; no collective on the data path.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config gdn_decode|gdn_prefill|kv_attention]
+
+``--impl reference`` times the CPU oracle of the same path on the host cores
+(the reference has no GPU implementation of this path), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+# ------------------------------------------------------------------ clocks --
+class ClockSampler:
+    """Polls NVML (read-only) every few ms while the timed region runs."""
+
+    def __init__(self, device_index=0, period_s=0.005):
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._idx = device_index
+        self._thread = None
+        self._nvml = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            try:
+                pr = torch.cuda.get_device_properties(self._idx)
+                bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(self._idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+            return self
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def _run(self):
+        nv = self._nvml
+        names = {
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for n, bit in names.items():
+                    if r & bit:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------- dist utils --
+def init_dist(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return ws, rank, local  # host-only arm: rank 0 works, the others exit
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def barrier(ws):
+    if ws > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x, ws, device):
+    if ws == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------- GDN decode ---
+DECODE_B, DECODE_STEPS = 64, 256
+H_QK, H_V, DK, DV = 16, 32, 128, 128
+
+
+def decode_bytes_per_step(B=DECODE_B):
+    state = 2 * B * H_V * DK * DV * 4
+    qk = 2 * B * H_QK * DK * 2
+    v = B * H_V * DV * 2
+    out = B * H_V * DV * 2
+    gb = 2 * B * H_V * 4
+    return state + qk + v + out + gb
+
+
+def cpu_decode_sample(n_steps, threads):
+    """Oracle decode steps at the full batch on the host cores; returns steps/s."""
+    from anemll_b200 import inputs
+    from oracle import gdn as og
+    torch.set_num_threads(threads)
+    w = inputs.gdn_decode(B=DECODE_B, steps=min(n_steps, DECODE_STEPS))
+    S = w["state"]
+    # warm one step
+    og.recurrent_gated_delta_rule(w["q"][0], w["k"][0], w["v"][0], w["g"][0], w["beta"][0], S)
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        t = i % w["q"].shape[0]
+        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+    dt = time.perf_counter() - t0
+    return n_steps / dt
+
+
+def bench_gdn_decode(args, ws, rank, local):
+    from anemll_b200 import _lib, gdn, inputs
+    dev = torch.device("cuda", local)
+    w = inputs.gdn_decode(seed=1 + 1000 * rank, B=DECODE_B, steps=DECODE_STEPS)
+    state = w["state"].to(dev)
+    q, k, v, g, beta = (w[n].to(dev) for n in ("q", "k", "v", "g", "beta"))
+    out = torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sp = _lib.stream_ptr(dev)
+    # pre-resolved raw pointers: the timed loop is one C call per step
+    ptrs = [(_lib.ptr(q[t]), _lib.ptr(k[t]), _lib.ptr(v[t]), _lib.ptr(g[t]), _lib.ptr(beta[t]))
+            for t in range(DECODE_STEPS)]
+    sptr, optr = _lib.ptr(state), _lib.ptr(out)
+
+    def step(i):
+        pq, pk, pv, pg, pb = ptrs[i % DECODE_STEPS]
+        rc = lib.anemll_gdn_recurrent(pq, pk, pv, _lib.BF16, pg, pb, sptr, optr, _lib.BF16,
+                                      DECODE_B, 1, H_QK, H_V, DK, DV, 0.0, 0, sp)
+        if rc:
+            _lib.check(rc, "anemll_gdn_recurrent")
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(ws)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, ws, dev)
+
+    # end to end through the public op with host buffers: H2D of the step's
+    # inputs from pinned memory, the kernel, D2H of the step's output
+    hq, hk, hv, hg, hb = (w[n].pin_memory() for n in ("q", "k", "v", "g", "beta"))
+    dq, dk_, dv_, dg, db = (torch.empty_like(x[0], device=dev) for x in (hq, hk, hv, hg, hb))
+    hout = torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16).pin_memory()
+    h2d = sum(x[0].numel() * x.element_size() for x in (hq, hk, hv, hg, hb))
+    d2h = hout.numel() * hout.element_size()
+
+    def e2e_step(i):
+        t = i % DECODE_STEPS
+        dq.copy_(hq[t], non_blocking=True)
+        dk_.copy_(hk[t], non_blocking=True)
+        dv_.copy_(hv[t], non_blocking=True)
+        dg.copy_(hg[t], non_blocking=True)
+        db.copy_(hb[t], non_blocking=True)
+        gdn.recurrent_gated_delta_rule_(dq, dk_, dv_, dg, db, state, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
+
+    pk, how = peaks()
+    per_launch_s = ms / 1e3 / args.steps
+    achieved = decode_bytes_per_step() / per_launch_s / 1e9
+    res = {
+        "metric": "gdn_decode_steps_per_s",
+        "value": ws * args.steps / (ms_max / 1e3),
+        "unit": "steps/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 state, bf16 q/k/v/out",
+        "data": "synthetic (seeded; state ~N(0,0.01), q/k l2-normalised N(0,1), v ~N(0,1))",
+        "config": {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
+                   "d_k": DK, "d_v": DV, "state_bytes": DECODE_B * H_V * DK * DV * 4,
+                   "tokens_cycled": DECODE_STEPS, "l2": "no flush: the 128 MiB state exceeds the 126 MB L2",
+                   "parallelism": f"weak, {ws} independent batch shards"},
+        "tokens_per_s": ws * args.steps * DECODE_B / (ms_max / 1e3),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "peak_source": how,
+                     "algorithmic_bytes_per_launch": decode_bytes_per_step(), "traffic": None},
+        "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+    }
+    res["clocks"] = clk.summary()
+    return res
+
+
+def traffic_from_profiles(name):
+    """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(name)
+    except (OSError, ValueError):
+        return None
+
+
+def reference_arm(args, ws, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from anemll_b200 import inputs
+    from oracle import gdn as og
+    w = inputs.gdn_decode(B=DECODE_B, steps=DECODE_STEPS)
+    S = w["state"]
+    for i in range(args.warmup):
+        t = i % DECODE_STEPS
+        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        t = i % DECODE_STEPS
+        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    return {
+        "impl": "reference",
+        "metric": "gdn_decode_steps_per_s",
+        "value": v,
+        "unit": "steps/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
+                   "d_k": DK, "d_v": DV},
+        "cpu_baseline": {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} full-batch decode steps of the fp32 torch CPU oracle "
+                                   "(the reference has no implementation of this path)"},
+        "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2560)
+    ap.add_argument("--warmup", type=int, default=32)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode"])
+    ap.add_argument("--cpu-baseline-steps", type=int, default=8)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    ws, rank, local = init_dist(args)
+    try:
+        if args.impl == "reference":
+            res = reference_arm(args, ws, rank)
+        else:
+            res = bench_gdn_decode(args, ws, rank, local)
+            res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
+            if rank == 0:
+                if ws == 1:
+                    threads = os.cpu_count() or 1
+                    v = cpu_decode_sample(args.cpu_baseline_steps, threads)
+                    res["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
+                                           "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode steps of "
+                                                     "the fp32 torch CPU oracle"}
+                else:
+                    res["cpu_baseline"] = None
+        if rank == 0 and res is not None:
+            print(json.dumps(res), flush=True)
+    finally:
+        if ws > 1 and torch.distributed.is_initialized():
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

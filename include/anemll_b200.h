@@ -1,0 +1,133 @@
+/*
+ * anemll_b200 — C ABI of the B200 (sm_100a) attention hot path.
+ *
+ * Plain pointers and sizes only.  Every tensor pointer is device memory owned
+ * by the caller; nothing here allocates persistent memory.  `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  All calls are
+ * asynchronous and stream-ordered.
+ *
+ * Return value: 0 = success; negative = invalid argument (shape, dtype,
+ * alignment, null pointer — nothing was launched); positive = a CUDA error
+ * code from the launch.  anemll_last_error() returns a message for the last
+ * failing call on the calling host thread.
+ *
+ * Layouts (row-major, contiguous unless a stride argument says otherwise):
+ *   GDN   q, k        [B, T, H_qk, d_k]     value head j reads key head j / (H_v / H_qk)
+ *         v, out      [B, T, H_v,  d_v]
+ *         g, beta     [B, T, H_v]           fp32; g is the log-decay (<= 0)
+ *         state       [B, H_v, d_k, d_v]    fp32, updated in place
+ *         mixed_qkv   [B, T, 2*H_qk*d_k + H_v*d_v]   (q | k | v channels)
+ *         conv_state  [B, 2*H_qk*d_k + H_v*d_v, conv_k]  same dtype as mixed_qkv
+ *   KV    q           [B, H_q, S, hd]
+ *         k_new,v_new [B, H_kv, S, hd]
+ *         gate        [B, S, H_q*hd]        sigmoid-gate pre-activation (may be NULL)
+ *         out         [B, S, H_q*hd]        attention output before o_proj
+ *         k/v_cache   [B, H_kv, ctx, hd] with explicit batch/head element strides
+ *                     (token stride = hd); one layer of the reference's unified
+ *                     cache [2L, H_kv, ctx, hd] is batch_stride = 0,
+ *                     head_stride = ctx*hd.
+ */
+#ifndef ANEMLL_B200_H
+#define ANEMLL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define ANEMLL_F32 0
+#define ANEMLL_F16 1
+#define ANEMLL_BF16 2
+
+/* status */
+#define ANEMLL_OK 0
+#define ANEMLL_EINVAL (-1)
+#define ANEMLL_EUNSUPPORTED (-2)
+#define ANEMLL_EALIGN (-3)
+#define ANEMLL_EWORKSPACE (-4)
+
+const char* anemll_last_error(void);
+int anemll_version(void);
+
+/*
+ * Gated delta rule, token-by-token form: decode (T == 1) and recurrent prefill.
+ * Replaces the recurrent core called from Qwen3_5GatedDeltaNet.forward
+ * (third-party transformers 5.5.0, modeling_qwen3_5.py:314-353,
+ * torch_recurrent_gated_delta_rule; the reference snapshot has no GDN code).
+ * scale <= 0 selects 1/sqrt(d_k).  qk_l2norm != 0 l2-normalises q and k
+ * (eps 1e-6) first, as use_qk_l2norm_in_kernel=True does there.
+ * qkv_dtype / out_dtype: ANEMLL_F32, ANEMLL_F16 or ANEMLL_BF16.  d_k == 128,
+ * d_v % 32 == 0, H_v % H_qk == 0.
+ */
+int anemll_gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
+                         const float* g, const float* beta, float* state,
+                         void* out, int out_dtype,
+                         int B, int T, int H_qk, int H_v, int d_k, int d_v,
+                         float scale, int qk_l2norm, void* stream);
+
+/*
+ * Fused GDN prologue: depthwise causal conv1d (conv_k taps) + SiLU over the
+ * mixed q|k|v channels, split, l2-normalise q and k (eps 1e-6), and the gates
+ * beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias).
+ * Replaces the conv/split/gate part of Qwen3_5GatedDeltaNet.forward
+ * (modeling_qwen3_5.py:453-496, torch_causal_conv1d_update 210-226).
+ * use_state == 0: history is zero (fresh prefill); != 0: history is read from
+ * conv_state.  conv_state always receives the last conv_k raw inputs.
+ * conv_w [C, conv_k] fp32; A_log, dt_bias [H_v] fp32 (dt_bias may be NULL);
+ * a, b [B, T, H_v] in ab_dtype.  q/k/v outputs in out_dtype, g/beta fp32.
+ */
+int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const float* conv_w, void* conv_state,
+                        const void* a, const void* b, int ab_dtype,
+                        const float* A_log, const float* dt_bias,
+                        void* q_out, void* k_out, void* v_out, int out_dtype,
+                        float* g_out, float* beta_out,
+                        int B, int T, int H_qk, int H_v, int d_k, int d_v, int conv_k,
+                        int use_state, void* stream);
+
+/*
+ * Gated RMSNorm: out = weight * x * rsqrt(mean(x^2) + eps) * silu(z) over rows
+ * of length d.  Replaces Qwen3_5RMSNormGated (modeling_qwen3_5.py:175-190).
+ */
+int anemll_gated_rmsnorm(const void* x, int x_dtype, const void* z, int z_dtype,
+                         const float* weight, void* out, int out_dtype,
+                         int64_t rows, int d, float eps, void* stream);
+
+/*
+ * KV-cache attention with the cache write fused in (one call = one prefill
+ * chunk of S tokens or one decode step, S == 1).  Writes k_new/v_new at
+ * positions [current_pos, current_pos + S) of k_cache / v_cache (for the
+ * reference's unified cache: k_cache = kv_cache[layer_idx], v_cache =
+ * kv_cache[layer_idx + num_layers], get_kv_cache_idx qwen_model.py:88-93),
+ * then attends each query at position current_pos + i over keys 0..ctx-1.
+ * k_new and v_new may both be NULL: the caller already wrote the cache (the
+ * reference's own order: process_layer_* writes, then forward_* attends).
+ * Replaces QwenAttention.forward_prefill (anemll/models/qwen_model.py:509-546)
+ * plus the write at 669-675, and forward_regular (469-507) plus the write at
+ * 733-745, with the Qwen3.5 sigmoid gate (modeling_qwen3_5.py:689).
+ * Visibility: if `mask` is non-NULL it is the reference's additive mask
+ * ([S, mask_row_stride] elements of mask_dtype; -inf hides a key).  Otherwise
+ * key j is visible to position p iff j <= p and, when window > 0, j > p - window
+ * (window_chunk_aligned != 0: j >= max(0, min(current_pos + S, ctx) - window)
+ * for the whole chunk, gemma3_model.py:923-926).
+ * dtype: ANEMLL_F16 or ANEMLL_BF16 for q, k_new, v_new, gate, cache and out.
+ * workspace: device scratch of at least anemll_kv_attention_workspace_size()
+ * bytes (may be NULL when that size is 0).
+ */
+size_t anemll_kv_attention_workspace_size(int B, int S, int H_q, int H_kv, int head_dim, int ctx);
+
+int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, const void* gate,
+                        void* k_cache, void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                        const void* mask, int mask_dtype, int64_t mask_row_stride,
+                        void* out, int dtype,
+                        int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                        int current_pos, int window, int window_chunk_aligned,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANEMLL_B200_H */

@@ -1,0 +1,188 @@
+"""GPU parity of the gated delta-rule kernels against the CPU oracle (through the C ABI)."""
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from anemll_b200 import gdn, inputs
+from oracle import gdn as og
+from tests.conftest import GOLDEN
+from tests.tolerance import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return torch.load(os.path.join(GOLDEN, "gdn.pt"))["gdn"]
+
+
+def test_recurrent_prefill_matches_golden(gold):
+    d = gold
+    state = d["S0"].to(DEV).contiguous()
+    out = gdn.recurrent_gated_delta_rule_(d["q"].to(DEV), d["k"].to(DEV), d["v"].to(DEV), d["g"].to(DEV),
+                                          d["beta"].to(DEV), state, use_qk_l2norm_in_kernel=True,
+                                          out_dtype=torch.float32)
+    assert_close(out, d["out_recurrent"], "out")
+    assert_close(state, d["state_recurrent"], "state")
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_decode_full_batch_few_steps(out_dtype):
+    w = inputs.gdn_decode(B=64, steps=3)
+    S_ref = w["state"].clone()
+    state = w["state"].to(DEV)
+    for t in range(3):
+        q, k, v, g, b = (w[n][t] for n in ("q", "k", "v", "g", "beta"))
+        out = gdn.recurrent_gated_delta_rule_(q.to(DEV), k.to(DEV), v.to(DEV), g.to(DEV), b.to(DEV), state,
+                                              out_dtype=out_dtype)
+        o_ref, S_ref = og.recurrent_gated_delta_rule(q, k, v, g, b, S_ref)
+        if out_dtype == torch.bfloat16:
+            o_ref = o_ref.to(torch.bfloat16).float()  # the output rounding is part of the contract
+            assert_close(out.float(), o_ref, f"out step {t}", rel_l2=5e-3)
+        else:
+            assert_close(out, o_ref, f"out step {t}")
+    assert_close(state, S_ref, "state")
+
+
+def test_decode_256_steps_small_batch():
+    w = inputs.gdn_decode(B=2, steps=256)
+    S_ref = w["state"].clone()
+    state = w["state"].to(DEV)
+    outs, refs = [], []
+    for t in range(256):
+        q, k, v, g, b = (w[n][t] for n in ("q", "k", "v", "g", "beta"))
+        outs.append(gdn.recurrent_gated_delta_rule_(q.to(DEV), k.to(DEV), v.to(DEV), g.to(DEV), b.to(DEV), state,
+                                                    out_dtype=torch.float32))
+    q, k, v, g, b = (w[n].squeeze(2).transpose(0, 1).contiguous() for n in ("q", "k", "v", "g", "beta"))
+    o_ref, S_ref = og.recurrent_gated_delta_rule(q, k, v, g, b, S_ref)
+    assert_close(torch.cat(outs, 1), o_ref, "outputs")
+    assert_close(state, S_ref, "state")
+
+
+def test_multi_token_launch_equals_token_launches_bit_exact():
+    """Size-independent property at the full decode shape: T tokens in one launch
+    (state kept in registers) == T single-token launches (state through HBM)."""
+    w = inputs.gdn_decode(B=64, steps=2)
+    q, k, v, g, b = (w[n].squeeze(2).transpose(0, 1).contiguous().to(DEV) for n in ("q", "k", "v", "g", "beta"))
+    s1 = w["state"].to(DEV)
+    s2 = s1.clone()
+    o1 = gdn.recurrent_gated_delta_rule_(q, k, v, g, b, s1, out_dtype=torch.float32)
+    o2 = torch.cat([gdn.recurrent_gated_delta_rule_(q[:, t:t + 1].contiguous(), k[:, t:t + 1].contiguous(),
+                                                    v[:, t:t + 1].contiguous(), g[:, t:t + 1].contiguous(),
+                                                    b[:, t:t + 1].contiguous(), s2, out_dtype=torch.float32)
+                    for t in range(2)], 1)
+    assert torch.equal(o1, o2)
+    assert torch.equal(s1, s2)
+
+
+def test_zero_write_keeps_state_bit_exact():
+    """beta = 0 and g = 0: the state must come back bit-identical and out = S^T q."""
+    w = inputs.gdn_decode(B=64, steps=1)
+    q, k, v = (w[n][0].to(DEV) for n in ("q", "k", "v"))
+    z = torch.zeros(64, 1, 32, device=DEV)
+    s = w["state"].to(DEV)
+    s0 = s.clone()
+    out = gdn.recurrent_gated_delta_rule_(q, k, v, z, z, s, out_dtype=torch.float32)
+    assert torch.equal(s, s0)
+    qe = q.float().repeat_interleave(2, dim=2)[:, 0] / (128 ** 0.5)
+    ref = torch.einsum("bhkv,bhk->bhv", s0, qe)
+    assert_close(out[:, 0], ref, "S^T q")
+
+
+def test_equal_heads_and_empty_sequence():
+    torch.manual_seed(5)
+    B, T, H = 2, 5, 4
+    q = F.normalize(torch.randn(B, T, H, 128), dim=-1).half()
+    k = F.normalize(torch.randn(B, T, H, 128), dim=-1).half()
+    v = torch.randn(B, T, H, 128).half()
+    g = -F.softplus(torch.randn(B, T, H))
+    b = torch.sigmoid(torch.randn(B, T, H))
+    o, s = gdn.recurrent_gated_delta_rule(q.to(DEV), k.to(DEV), v.to(DEV), g.to(DEV), b.to(DEV),
+                                          output_final_state=True)
+    o_ref, s_ref = og.recurrent_gated_delta_rule(q, k, v, g, b)
+    assert_close(o.float(), o_ref.half().float(), "out", rel_l2=2e-3)
+    assert_close(s, s_ref, "state")
+    st = torch.randn(B, H, 128, 128, device=DEV)
+    st0 = st.clone()
+    gdn.recurrent_gated_delta_rule_(q[:, :0].to(DEV), k[:, :0].to(DEV), v[:, :0].to(DEV), g[:, :0].to(DEV),
+                                    b[:, :0].to(DEV), st)
+    assert torch.equal(st, st0)
+
+
+def test_invalid_arguments_raise():
+    q = torch.zeros(1, 1, 1, 64, device=DEV, dtype=torch.half)
+    with pytest.raises(RuntimeError, match="d_k"):
+        gdn.recurrent_gated_delta_rule_(q, q, q, torch.zeros(1, 1, 1, device=DEV), torch.zeros(1, 1, 1, device=DEV),
+                                        torch.zeros(1, 1, 64, 64, device=DEV))
+
+
+def _prologue_case(B, T, use_state, seed):
+    torch.manual_seed(seed)
+    Hqk, Hv = 16, 32
+    C = 2 * Hqk * 128 + Hv * 128
+    x = torch.randn(B, T, C).bfloat16()
+    w = 0.1 * torch.randn(C, 4)
+    cs = torch.randn(B, C, 4).bfloat16() if use_state else torch.zeros(B, C, 4).bfloat16()
+    a = torch.randn(B, T, Hv).bfloat16()
+    bb = torch.randn(B, T, Hv).bfloat16()
+    A_log = torch.empty(Hv).uniform_(0, 2.77)
+    dtb = 0.1 * torch.randn(Hv)
+    return Hqk, Hv, x, w, cs, a, bb, A_log, dtb
+
+
+@pytest.mark.parametrize("B,T,use_state", [(1, 512, False), (2, 37, True), (3, 1, True), (1, 2, True), (2, 3, False)])
+def test_prologue_matches_oracle(B, T, use_state):
+    Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(B, T, use_state, 10 + T)
+    cs_dev = cs.to(DEV)
+    q, k, v, g, beta = gdn.gdn_prologue(x.to(DEV), w.to(DEV), cs_dev, a.to(DEV), bb.to(DEV), A_log.to(DEV),
+                                        dtb.to(DEV), Hqk, Hv, use_state=use_state, out_dtype=torch.float32)
+    rq, rk, rv, rg, rb, rstate = og.prologue(x, a, bb, w, A_log, dtb, cs if use_state else None, Hqk, Hv, 128, 128)
+    assert_close(q, rq, "q", rel_l2=1e-5, max_abs=1e-5)
+    assert_close(k, rk, "k", rel_l2=1e-5, max_abs=1e-5)
+    assert_close(v, rv, "v", rel_l2=1e-5, max_abs=1e-5)
+    assert_close(g, rg, "g", rel_l2=1e-5, max_abs=1e-4)
+    assert_close(beta, rb, "beta", rel_l2=1e-5, max_abs=1e-5)
+    assert torch.equal(cs_dev.cpu(), rstate.to(torch.bfloat16)), "conv state must be bit-exact"
+
+
+def test_gated_rmsnorm_matches_golden():
+    n = torch.load(os.path.join(GOLDEN, "gdn.pt"))["norm"]
+    y = gdn.gated_rmsnorm(n["x"].to(DEV), n["z"].to(DEV), n["weight"].to(DEV))
+    assert_close(y, n["y"], "gated rmsnorm", rel_l2=1e-5, max_abs=1e-5)
+
+
+def test_gdn_layer_prefill_then_decode_matches_oracle():
+    """Single layer, B=1: 512-token prefill then 64 decode steps; the hot path's
+    inputs are the device's own projection outputs, which the oracle re-uses."""
+    w, hidden = inputs.gdn_layer()
+    layer = gdn.GatedDeltaNet(dtype=torch.bfloat16, device=DEV)
+    with torch.no_grad():
+        for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+            getattr(layer, n).weight.copy_(w[n])
+        layer.conv_weight.copy_(w["conv_w"])
+        layer.A_log.copy_(w["A_log"])
+        layer.dt_bias.copy_(w["dt_bias"])
+        layer.norm_weight.copy_(w["norm_w"])
+    params = dict(conv_w=w["conv_w"], A_log=w["A_log"], dt_bias=w["dt_bias"], norm_w=w["norm_w"])
+    conv_state, rec_state = layer.new_states(1)
+    h = hidden.to(DEV)
+    ref_conv, ref_state = None, None
+    with torch.no_grad():
+        for step, (s, e) in enumerate([(0, 512)] + [(512 + i, 513 + i) for i in range(64)]):
+            x = h[:, s:e]
+            mixed, z, a, b = layer.in_proj_qkv(x), layer.in_proj_z(x), layer.in_proj_a(x), layer.in_proj_b(x)
+            o, normed = layer.core(mixed, z, a, b, conv_state, rec_state, use_precomputed_states=step > 0)
+            if step == 0:
+                ro, rn, ref_conv, ref_state = og.gdn_layer_prefill(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), params,
+                                                                   16, 32, 128, 128)
+            else:
+                ro, rn, ref_conv, ref_state = og.gdn_layer_decode(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), params,
+                                                                  16, 32, 128, 128, ref_conv, ref_state)
+            if step in (0, 1, 64):
+                assert_close(o, ro, f"core output step {step}")
+                assert_close(normed.float(), rn.to(torch.bfloat16).float(), f"normed step {step}", rel_l2=5e-3)
+                assert torch.equal(conv_state.cpu(), ref_conv.to(torch.bfloat16)), "conv state"
+                assert_close(rec_state, ref_state, f"state step {step}")

@@ -1,0 +1,117 @@
+"""GPU parity of the fused KV-cache attention kernel against the oracle (through the C ABI)."""
+import os
+
+import pytest
+import torch
+
+from anemll_b200 import attention, inputs
+from oracle import kv_attention as ok
+from tests.conftest import GOLDEN
+from tests.tolerance import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return torch.load(os.path.join(GOLDEN, "kv_attention.pt"))
+
+
+@pytest.mark.parametrize("use_mask", [True, False])
+def test_matches_reference_golden(gold, use_mask):
+    hd, ctx, Hkv = gold["hd"], gold["ctx"], gold["Hkv"]
+    for c in gold["cases"]:
+        S, pos = c["S"], c["pos"]
+        K = torch.zeros(Hkv, ctx, hd, dtype=torch.half)
+        V = torch.zeros(Hkv, ctx, hd, dtype=torch.half)
+        K[:, :pos + S] = c["K"]
+        V[:, :pos + S] = c["V"]
+        mask = None
+        if use_mask:
+            mask = torch.zeros(1, 1, S, ctx).masked_fill(~c["visible"].view(1, 1, S, ctx), float("-inf")).half()
+            mask = mask.to(DEV)
+        att = attention.QwenAttentionB200(gold["Hq"], Hkv, hd, window=c["window"],
+                                          window_chunk_aligned=c["chunk_aligned"])
+        args = (None, c["q"].to(DEV), (K.to(DEV), V.to(DEV)), mask)
+        if S == 1:
+            out = att.forward_regular(*args, current_pos=pos)
+        else:
+            out = att.forward_prefill(*args, current_pos=pos)
+        assert_close(out.float(), c["out"], c["name"])
+
+
+def test_fused_cache_write_bit_exact_vs_reference():
+    fx = torch.load(os.path.join(GOLDEN, "kv_cache_write.pt"))
+    for w in fx["writes"]:
+        cache = w["before"].to(DEV)
+        L, Hkv, ctx, hd = cache.shape[0] // 2, cache.shape[1], cache.shape[2], cache.shape[3]
+        S = w["S"]
+        q = torch.randn(1, 4, S, hd, dtype=torch.half, device=DEV)
+        att = attention.QwenAttentionB200(4, Hkv, hd)
+        att.process_layer_step(cache, w["layer_idx"], w["num_layers"], q, w["k"].to(DEV), w["v"].to(DEV), w["pos"])
+        assert torch.equal(cache.cpu(), w["after"]), w["name"]
+
+
+@pytest.mark.parametrize("window", [0, 512])
+def test_cfg2_chunked_prefill_and_decode(window):
+    """H_q=16, H_kv=2, hd=256, ctx 4096, fp16: 31 x 64-token chunks at 2048..4031, then
+    64 decode steps at 4032..4095, causal and 512-token sliding window; every
+    output within tolerance, the final cache bit-exact."""
+    d = inputs.kv_attention()
+    cache_dev = d["cache"].clone().to(DEV)  # [2, Hkv, ctx, hd]: a one-layer unified cache
+    cache_ref = d["cache"].float().clone()
+    att = attention.QwenAttentionB200(16, 2, 256, window=window)
+    pos = d["prefill_from"]
+    steps = [(p, 64) for p in range(pos, d["prefill_to"], 64)] + [(p, 1) for p in range(d["prefill_to"], 4096)]
+    worst = 0.0
+    for i, (p, S) in enumerate(steps):
+        j = p - pos
+        q = d["q"][:, :, j:j + S]
+        k = d["k"][:, :, j:j + S]
+        v = d["v"][:, :, j:j + S]
+        gte = d["gate"][:, j:j + S]
+        out = att.process_layer_step(cache_dev, 0, 1, q.to(DEV), k.to(DEV), v.to(DEV), p, gate=gte.to(DEV))
+        if i % 4 == 0 or S == 1 and i % 8 == 0 or i == len(steps) - 1:
+            ref = ok.kv_attention_step(q, k, v, gte, cache_ref, 0, 1, p, window)
+            rel, _ = assert_close(out.float(), ref, f"step {i} pos {p}")
+            worst = max(worst, rel)
+        else:
+            ok.write_cache(cache_ref, k, v, 0, 1, p)
+    assert torch.equal(cache_dev.cpu(), cache_ref.half())
+
+
+def test_batched_cache_and_workspace_errors():
+    torch.manual_seed(7)
+    B, Hq, Hkv, hd, ctx, S, pos = 3, 8, 2, 128, 512, 16, 200
+    kc = torch.randn(B, Hkv, ctx, hd).half()
+    vc = torch.randn(B, Hkv, ctx, hd).half()
+    q = torch.randn(B, Hq, S, hd).half()
+    kn = torch.randn(B, Hkv, S, hd).half()
+    vn = torch.randn(B, Hkv, S, hd).half()
+    kd, vd = kc.to(DEV), vc.to(DEV)
+    out = attention.kv_attention(q.to(DEV), kd, vd, pos, k_new=kn.to(DEV), v_new=vn.to(DEV))
+    kr, vr = kc.float().clone(), vc.float().clone()
+    kr[:, :, pos:pos + S] = kn.float()
+    vr[:, :, pos:pos + S] = vn.float()
+    ref = ok.attend(q, kr, vr, ok.additive_mask(S, ctx, pos))
+    assert_close(out.float(), ref, "batched")
+    assert torch.equal(kd.cpu().float(), kr) and torch.equal(vd.cpu().float(), vr)
+    with pytest.raises(RuntimeError, match="exceed"):
+        attention.kv_attention(q.to(DEV), kd, vd, ctx - 4, k_new=kn.to(DEV), v_new=vn.to(DEV))
+    tiny = torch.empty(16, dtype=torch.uint8, device=DEV)
+    with pytest.raises(RuntimeError, match="workspace"):
+        attention.kv_attention(q[:, :, :1].contiguous().to(DEV), kd, vd, 400, workspace=tiny)
+
+
+def test_bf16_cache():
+    torch.manual_seed(8)
+    Hq, Hkv, hd, ctx, S, pos = 16, 2, 256, 1024, 64, 512
+    kc = torch.randn(Hkv, ctx, hd).bfloat16()
+    vc = torch.randn(Hkv, ctx, hd).bfloat16()
+    q = torch.randn(1, Hq, S, hd).bfloat16()
+    gate = torch.randn(1, S, Hq * hd).bfloat16()
+    out = attention.kv_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos, gate=gate.to(DEV))
+    ref = ok.attend(q, kc.unsqueeze(0), vc.unsqueeze(0), ok.additive_mask(S, ctx, pos), gate)
+    # bf16 probabilities feed the PV product: its 8-bit mantissa sets this bound
+    assert_close(out.float(), ref, "bf16", rel_l2=5e-3, max_abs=1e-2)
