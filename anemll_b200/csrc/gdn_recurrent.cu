@@ -187,7 +187,8 @@ extern "C" int anemll_gdn_recurrent(const void* q, const void* k, const void* v,
                                     void* out, int out_dtype,
                                     int B, int T, int H_qk, int H_v, int d_k, int d_v,
                                     float scale, int qk_l2norm, void* stream) {
-  ANEMLL_REQUIRE(q && k && v && g && beta && state && out, ANEMLL_EINVAL, "gdn_recurrent: null pointer");
+  ANEMLL_REQUIRE(state && (T == 0 || (q && k && v && g && beta && out)), ANEMLL_EINVAL,
+                 "gdn_recurrent: null pointer");
   ANEMLL_REQUIRE(B > 0 && T >= 0 && H_qk > 0 && H_v > 0, ANEMLL_EINVAL,
                  "gdn_recurrent: bad sizes B=%d T=%d H_qk=%d H_v=%d", B, T, H_qk, H_v);
   ANEMLL_REQUIRE(H_v % H_qk == 0, ANEMLL_EINVAL, "gdn_recurrent: H_v (%d) must be a multiple of H_qk (%d)", H_v, H_qk);

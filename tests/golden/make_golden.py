@@ -109,7 +109,7 @@ def make_kv(ref_root):
 
     # ---- cache write through the reference model (bit-exact target) ----
     torch.manual_seed(21)
-    L, Hq, Hkv, hd, ctx = 2, 4, 2, 32, 64
+    L, Hq, Hkv, hd, ctx = 2, 4, 2, 64, 64
     cfg = qm.QwenConfig(hidden_size=128, num_attention_heads=Hq, num_key_value_heads=Hkv, head_dim=hd,
                         context_length=ctx, state_length=ctx, num_hidden_layers=L,
                         intermediate_size=64, vocab_size=32)
