@@ -23,6 +23,9 @@ _SIGS = {
     "anemll_version": ([], _c_int),
     "anemll_gdn_recurrent": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
                               _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp], _c_int),
+    "anemll_gdn_chunked_prefill": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
+                                    _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp], _c_int),
+    "anemll_gdn_chunked_error": ([_c_int], _c_int),
     "anemll_gdn_prologue": ([_vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _vp, _vp,
                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp], _c_int),
     "anemll_gated_rmsnorm": ([_vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_i64, _c_int, _c_float, _vp], _c_int),

@@ -27,6 +27,9 @@ from . import _lib
 __all__ = [
     "recurrent_gated_delta_rule",
     "recurrent_gated_delta_rule_",
+    "chunk_gated_delta_rule",
+    "chunk_gated_delta_rule_",
+    "chunked_device_error",
     "gdn_prologue",
     "gated_rmsnorm",
     "GatedDeltaNet",
@@ -87,6 +90,57 @@ def recurrent_gated_delta_rule(query, key, value, g, beta, initial_state=None, o
     out = recurrent_gated_delta_rule_(query, key, value, g.float().contiguous(), beta.float().contiguous(), state,
                                       scale, use_qk_l2norm_in_kernel)
     return out, (state if output_final_state else None)
+
+
+def chunk_gated_delta_rule_(query, key, value, g, beta, state, scale=None, use_qk_l2norm_in_kernel=False,
+                            chunk_size=64, out=None, out_dtype=None):
+    """Chunked (WY/UT) delta rule on the tensor cores, updating ``state`` in place.
+
+    Same layouts as :func:`recurrent_gated_delta_rule_`; ``query/key/value`` are
+    fp16 or bf16 (converted to fp16 operands inside the kernel).
+    """
+    _need_cuda(query, key, value, g, beta, state)
+    for n, t in (("query", query), ("key", key), ("value", value), ("g", g), ("beta", beta), ("state", state)):
+        _need_contig(n, t)
+    if g.dtype != torch.float32 or beta.dtype != torch.float32 or state.dtype != torch.float32:
+        raise TypeError("g, beta and state must be float32")
+    if query.dtype != key.dtype or key.dtype != value.dtype:
+        raise TypeError("query, key and value must share a dtype")
+    B, T, H_qk, d_k = query.shape
+    H_v, d_v = value.shape[2], value.shape[3]
+    if key.shape != query.shape or value.shape[:2] != (B, T) or tuple(state.shape) != (B, H_v, d_k, d_v):
+        raise ValueError("shape mismatch between query/key/value/state")
+    if tuple(g.shape) != (B, T, H_v) or tuple(beta.shape) != (B, T, H_v):
+        raise ValueError("g and beta must be [B, T, H_v]")
+    out_dtype = out_dtype or query.dtype
+    if out is None:
+        out = torch.empty(B, T, H_v, d_v, dtype=out_dtype, device=query.device)
+    rc = _lib.load().anemll_gdn_chunked_prefill(
+        _lib.ptr(query), _lib.ptr(key), _lib.ptr(value), _lib.dtype_code(query.dtype), _lib.ptr(g), _lib.ptr(beta),
+        _lib.ptr(state), _lib.ptr(out), _lib.dtype_code(out.dtype), B, T, H_qk, H_v, d_k, d_v, int(chunk_size),
+        float(scale) if scale is not None else 0.0, int(bool(use_qk_l2norm_in_kernel)),
+        _lib.stream_ptr(query.device))
+    _lib.check(rc, "anemll_gdn_chunked_prefill")
+    return out
+
+
+def chunk_gated_delta_rule(query, key, value, g, beta, chunk_size=64, initial_state=None, output_final_state=False,
+                           use_qk_l2norm_in_kernel=False, scale=None):
+    """Functional form with the third-party signature; returns ``(out, final_state or None)``."""
+    B, T, _, d_k = query.shape
+    H_v, d_v = value.shape[2], value.shape[3]
+    if initial_state is None:
+        state = torch.zeros(B, H_v, d_k, d_v, dtype=torch.float32, device=query.device)
+    else:
+        state = initial_state.to(torch.float32).clone()
+    out = chunk_gated_delta_rule_(query, key, value, g.float().contiguous(), beta.float().contiguous(), state,
+                                  scale, use_qk_l2norm_in_kernel, chunk_size)
+    return out, (state if output_final_state else None)
+
+
+def chunked_device_error(reset=True) -> int:
+    """Non-zero if a chunked-prefill launch stopped on a bounded wait (synchronous)."""
+    return int(_lib.load().anemll_gdn_chunked_error(int(bool(reset))))
 
 
 def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k_heads, num_v_heads,
@@ -198,7 +252,11 @@ class GatedDeltaNet(nn.Module):
                                         b.contiguous(), self.A_log, self.dt_bias, self.num_k_heads,
                                         self.num_v_heads, self.head_k_dim, self.head_v_dim,
                                         use_state=use_precomputed_states, out_dtype=self.core_dtype)
-        o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
+        if T > 1 and not use_precomputed_states:
+            o = chunk_gated_delta_rule_(q, k, v, g, beta, recurrent_state, chunk_size=self.chunk_size,
+                                        out_dtype=torch.float32)
+        else:
+            o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
         normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim).contiguous(), self.norm_weight,
                                self.eps, out_dtype=mixed_qkv.dtype)
         return o, normed

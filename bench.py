@@ -265,6 +265,78 @@ def bench_gdn_decode(args, ws, rank, local):
     return res
 
 
+PREFILL_B, PREFILL_T, CHUNK = 8, 32768, 64
+PREFILL_FLOP_PER_TOKEN_HEAD = (2 * CHUNK * CHUNK * (3 * DK + 2 * DV) + 6 * CHUNK * DK * DV) // CHUNK  # 180,224
+
+
+def bench_gdn_prefill(args, ws, rank, local):
+    """Chunked prefill, B=8 x 32768 tokens, H_qk=16, H_v=32, d=128, bf16 in, bf16 out.
+
+    Sharding: the 8 sequences are split over the ranks (one launch per rank per
+    step); with more ranks than sequences the value heads are split too (the
+    head pairs that share a key head stay together).  One step = one prefill of
+    this rank's shard; value = all tokens of the job / max-over-ranks time."""
+    from anemll_b200 import gdn, inputs
+    dev = torch.device("cuda", local)
+    if ws <= PREFILL_B:
+        b_loc, hv_loc, hqk_loc = PREFILL_B // ws, H_V, H_QK
+    else:
+        b_loc, hv_loc, hqk_loc = 1, H_V * PREFILL_B // ws, H_QK * PREFILL_B // ws
+    w = inputs.gdn_prefill_device(seed=3 + 1000 * rank, B=b_loc, T=PREFILL_T, device=dev, Hqk=hqk_loc, Hv=hv_loc)
+    state = torch.zeros(b_loc, hv_loc, DK, DV, device=dev)
+    out = torch.empty(b_loc, PREFILL_T, hv_loc, DV, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        gdn.chunk_gated_delta_rule_(w["q"], w["k"], w["v"], w["g"], w["beta"], state, out=out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(ws)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(ms, ws, dev)
+    if gdn.chunked_device_error(reset=True):
+        raise RuntimeError("chunked prefill reported a device-side wait timeout")
+    tokens_local = b_loc * PREFILL_T
+    tokens_job = PREFILL_B * PREFILL_T
+    flop_launch = tokens_local * hv_loc * PREFILL_FLOP_PER_TOKEN_HEAD
+    per_launch_s = ms / 1e3 / args.steps
+    pk, how = peaks()
+    achieved = flop_launch / per_launch_s / 1e12
+    return {
+        "metric": "gdn_prefill_tokens_per_s",
+        "value": tokens_job * args.steps / (ms_max / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16 tensor-core operands, f32 accumulate/state, bf16 in/out",
+        "data": "synthetic (seeded on device; q/k l2-normalised N(0,1), v ~N(0,1))",
+        "config": {"workload": "gdn_chunked_prefill", "batch": PREFILL_B, "seq_len": PREFILL_T, "chunk": CHUNK,
+                   "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV,
+                   "l2": "no flush: 4.3 GB of inputs per step exceed the 126 MB L2",
+                   "parallelism": f"{ws} ranks, sequences x value heads, no collective"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / pk["bf16_tflops"], "peak_source": how,
+                     "algorithmic_flop_per_launch": flop_launch, "traffic": None},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+
+
 def traffic_from_profiles(name):
     """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -322,7 +394,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode"])
+    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode", "gdn_prefill"])
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -331,9 +403,13 @@ def main():
         if args.impl == "reference":
             res = reference_arm(args, ws, rank)
         else:
-            res = bench_gdn_decode(args, ws, rank, local)
-            res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
-            if rank == 0:
+            if args.config == "gdn_prefill":
+                res = bench_gdn_prefill(args, ws, rank, local)
+                res["roofline"]["traffic"] = traffic_from_profiles("gdn_chunked_prefill")
+            else:
+                res = bench_gdn_decode(args, ws, rank, local)
+                res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
+            if rank == 0 and args.config == "gdn_decode":
                 if ws == 1:
                     threads = os.cpu_count() or 1
                     v = cpu_decode_sample(args.cpu_baseline_steps, threads)

@@ -69,6 +69,28 @@ int anemll_gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dt
                          float scale, int qk_l2norm, void* stream);
 
 /*
+ * Gated delta rule, chunked prefill: chunks of chunk_size tokens in the WY/UT
+ * form on the tcgen05 tensor cores (fp16 operands, fp32 accumulators), the
+ * fp32 state carried across chunks in tensor memory.  Replaces
+ * torch_chunk_gated_delta_rule (transformers 5.5.0 modeling_qwen3_5.py:234-311).
+ * q/k/v are ANEMLL_F16 or ANEMLL_BF16; T may be any length (a ragged last
+ * chunk is a shorter chunk).  chunk_size == 64, d_k == d_v == 128.
+ */
+int anemll_gdn_chunked_prefill(const void* q, const void* k, const void* v, int qkv_dtype,
+                               const float* g, const float* beta, float* state,
+                               void* out, int out_dtype,
+                               int B, int T, int H_qk, int H_v, int d_k, int d_v,
+                               int chunk_size, float scale, int qk_l2norm, void* stream);
+
+/*
+ * Device-side status of the chunked kernel: non-zero if a bounded wait on the
+ * tensor core ran out (the kernel then stopped early and its outputs are
+ * invalid).  Synchronous; reset != 0 clears the flag.  Returns -1 on a CUDA
+ * error.  No counterpart in the reference (diagnostics of this build).
+ */
+int anemll_gdn_chunked_error(int reset);
+
+/*
  * Fused GDN prologue: depthwise causal conv1d (conv_k taps) + SiLU over the
  * mixed q|k|v channels, split, l2-normalise q and k (eps 1e-6), and the gates
  * beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias).
