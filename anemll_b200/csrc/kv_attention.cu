@@ -471,3 +471,91 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
     }
   });
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of anemll_kv_attention.
+//
+// Some callers cannot hand us a workspace or allocate one at call time: engines
+// that reserve all device memory when they start and forbid any later
+// cudaMalloc, and loops that cannot afford cudaMalloc/cudaFree because those
+// calls synchronise the whole device.  This entry point takes the split-KV
+// scratch from a fixed array that the library itself owns instead.
+//
+// - Limit: KV_NOALLOC_SCRATCH_BYTES (8 MiB).  Every GPU that loads this
+//   library holds that array until the process exits.  Shapes whose scratch
+//   need exceeds it are rejected (ANEMLL_EWORKSPACE) before anything launches.
+// - Set-up: the first call on a device, with that device current, looks up the
+//   array's device address (cudaGetSymbolAddress) and caches it per device.
+//   Make that first call before any stream capture on the device.
+// - Sharing: all calls share one array.  Each call fully overwrites the part it
+//   reads (every split writes all of its partial rows before the combine reads
+//   them), so nothing has to start at zero, but two calls that overlap on the
+//   GPU (different streams, or different host threads) race on the array.
+// - It never calls cudaMalloc, cudaFree or any allocating library routine.
+#include <mutex>
+
+namespace anemll {
+namespace {
+
+constexpr size_t KV_NOALLOC_SCRATCH_BYTES = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_kv_noalloc_scratch[KV_NOALLOC_SCRATCH_BYTES];
+
+constexpr int KV_NOALLOC_MAX_DEVICES = 64;
+std::mutex g_kv_noalloc_mu;
+void* g_kv_noalloc_ptr[KV_NOALLOC_MAX_DEVICES] = {};
+
+// Device address of the scratch array on the current device (host code may not
+// use the symbol itself: it is only a host-side stand-in for the device array).
+int kv_noalloc_scratch(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("kv_attention_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return (int)e;
+  }
+  ANEMLL_REQUIRE(dev >= 0 && dev < KV_NOALLOC_MAX_DEVICES, ANEMLL_EUNSUPPORTED,
+                 "kv_attention_noalloc: device ordinal %d beyond the supported %d", dev, KV_NOALLOC_MAX_DEVICES);
+  std::lock_guard<std::mutex> lock(g_kv_noalloc_mu);
+  if (!g_kv_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_kv_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("kv_attention_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev, cudaGetErrorString(e));
+      return e != cudaSuccess ? (int)e : ANEMLL_EINVAL;
+    }
+    g_kv_noalloc_ptr[dev] = p;
+  }
+  *out = g_kv_noalloc_ptr[dev];
+  return ANEMLL_OK;
+}
+
+}  // namespace
+}  // namespace anemll
+
+extern "C" size_t anemll_kv_attention_noalloc_max_scratch(void) { return anemll::KV_NOALLOC_SCRATCH_BYTES; }
+
+extern "C" int anemll_kv_attention_noalloc(const void* q, const void* k_new, const void* v_new, const void* gate,
+                                           void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                                           int64_t cache_head_stride,
+                                           const void* mask, int mask_dtype, int64_t mask_row_stride,
+                                           void* out, int dtype,
+                                           int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                                           int current_pos, int window, int window_chunk_aligned, void* stream) {
+  // sizes the plan needs; everything else is validated by anemll_kv_attention
+  ANEMLL_REQUIRE(B > 0 && S > 0 && H_q > 0 && H_kv > 0 && H_q % H_kv == 0 && ctx > 0 && current_pos >= 0,
+                 ANEMLL_EINVAL, "kv_attention_noalloc: bad sizes");
+  ANEMLL_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, ANEMLL_EUNSUPPORTED,
+                 "kv_attention_noalloc: head_dim must be 64, 128 or 256 (got %d)", head_dim);
+  const Plan pl = make_plan(B, S, H_q, H_kv, ctx, current_pos, window, window_chunk_aligned, mask != nullptr);
+  const size_t need = workspace_bytes_for(pl.n_splits, B, S, H_q, H_kv, head_dim);
+  ANEMLL_REQUIRE(need <= KV_NOALLOC_SCRATCH_BYTES, ANEMLL_EWORKSPACE,
+                 "kv_attention_noalloc: this call needs %zu bytes of scratch, above the built-in %zu-byte maximum; "
+                 "use anemll_kv_attention with a caller-provided workspace",
+                 need, KV_NOALLOC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = kv_noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return anemll_kv_attention(q, k_new, v_new, gate, k_cache, v_cache, cache_batch_stride, cache_head_stride, mask,
+                             mask_dtype, mask_row_stride, out, dtype, B, S, H_q, H_kv, head_dim, ctx, current_pos,
+                             window, window_chunk_aligned, scratch, KV_NOALLOC_SCRATCH_BYTES, stream);
+}

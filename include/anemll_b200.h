@@ -148,6 +148,30 @@ int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, con
                         int current_pos, int window, int window_chunk_aligned,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Allocation-free form of anemll_kv_attention (no counterpart in the
+ * reference).  For callers that cannot allocate device memory when they call
+ * in — an engine that reserves all GPU memory at start-up and forbids later
+ * cudaMalloc, or a loop that cannot pay for the device-wide synchronisation
+ * of cudaMalloc/cudaFree — the split-KV scratch comes from a fixed array
+ * inside the library (anemll_kv_attention_noalloc_max_scratch() bytes, 8 MiB,
+ * held on every GPU that loads the library until the process exits).
+ * Same arguments as anemll_kv_attention minus the workspace; calls whose
+ * scratch need exceeds the maximum return ANEMLL_EWORKSPACE without launching.
+ * The first call on a device (with that device current) looks up the array's
+ * device address; make it before any stream capture.  All calls share the
+ * array: calls that overlap on the GPU race.  Allocates nothing.
+ */
+size_t anemll_kv_attention_noalloc_max_scratch(void);
+
+int anemll_kv_attention_noalloc(const void* q, const void* k_new, const void* v_new, const void* gate,
+                                void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                                int64_t cache_head_stride,
+                                const void* mask, int mask_dtype, int64_t mask_row_stride,
+                                void* out, int dtype,
+                                int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                                int current_pos, int window, int window_chunk_aligned, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
