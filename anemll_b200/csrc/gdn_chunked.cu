@@ -8,22 +8,30 @@
 //
 //   D1   = [Q;K] K^T                         (tcgen05, M=128 N=64 K=128)
 //   P    = lower_incl(Q K^T * Gam)           (CUDA cores, fp16 to smem)
-//   A    = strict_lower(diag(beta) K K^T * Gam), T = (I + A)^-1   (CUDA cores)
+//   A    = strict_lower(diag(beta) K K^T * Gam), T = (I + A)^-1   (CUDA cores, fp32, blockwise)
 //   U^T  = V^T (T diag(beta))^T              (tcgen05, M=128 N=64 K=64)
 //   W^T  = K^T (T diag(beta e^G))^T          (tcgen05, M=128 N=64 K=64)
 //   Vn^T = U^T - S^T W^T                     (tcgen05, A negated, accumulates on U)
-//   O^T  = S^T (diag(e^G) Q)^T + Vn^T P^T    (tcgen05, two products, one accumulator)
+//   O1^T = S^T Q^T,  O2^T = Vn^T P^T         (tcgen05; O = diag(e^G) O1 + O2 at readout)
 //   S^T  = e^{G_c} S^T + (diag(e^{G_c - G}) Vn)^T K   (e^{G_c} applied in TMEM, then tcgen05)
 //
 // Every product is arranged so that M = 128 (d_v or d_k on TMEM lanes).  All
 // operands are fp16 in 128-byte-swizzled shared memory; accumulators are fp32
 // in TMEM.  fp16 (10-bit mantissa) operands keep the result within 1e-3
-// relative L2 of an fp32 evaluation; bf16 inputs convert to fp16 on load.  The
-// attention scale multiplies O in fp32 at the end (O is linear in q).
+// relative L2 of an fp32 evaluation; bf16 inputs convert to fp16 on the way in.
+// The attention scale multiplies O in fp32 at the end (O is linear in q).
+//
+// 256 threads: warps w and w+4 read the same TMEM lane quarter and split its
+// columns, so every CUDA-core phase has two warps per scheduler.  The next
+// chunk's raw q/k/v rows and gates are copied with cp.async into a staging
+// buffer while the current chunk computes.  T = (I + A)^-1 is built blockwise:
+// four 16x16 diagonal blocks by forward substitution, then 16 -> 32 -> 64
+// merges T21 = -T22 (A21 T11) as small fp32 matrix products over all threads.
 //
 // Semantics: torch_chunk_gated_delta_rule of transformers 5.5.0
 // (modeling_qwen3_5.py:234-311); chunk (WY/UT) form of Yang et al. (2024).
 #include "common.cuh"
+#include "mma_sync.cuh"
 #include "tcgen05.cuh"
 
 namespace anemll {
@@ -31,26 +39,31 @@ namespace {
 
 constexpr int C = 64;
 constexpr int D = 128;
-constexpr int NT = 128;
-constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t COL_S = 0, COL_O = 128, COL_U = 192;
+constexpr int NT = 256;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_S = 0, COL_O1 = 128, COL_U = 192, COL_O2 = 256, COL_D = 320;
 
-// shared memory map (bytes from a 1024-byte aligned base)
-constexpr int QK_BLK = 128 * 128;            // one 64-column block of a 128-row tile
-constexpr int T64_BLK = 64 * 128;            // one 64-column block of a 64-row tile
-constexpr int OFF_QK = 0;                    // [2][128 rows][128 B]: rows 0-63 Q, 64-127 K
-constexpr int OFF_QT = OFF_QK + 2 * QK_BLK;  // diag(e^G) Q: [2][64][128 B]
-constexpr int OFF_V = OFF_QT + 2 * T64_BLK;  // V [2][64][128 B]; later Vn^T [128][128 B]
-constexpr int OFF_VD = OFF_V + 2 * T64_BLK;  // (dec * Vn)^T [128][128 B]
-constexpr int OFF_P = OFF_VD + 128 * 128;    // P [64][128 B]
-constexpr int OFF_T1 = OFF_P + 64 * 128;     // T diag(beta)
-constexpr int OFF_T2 = OFF_T1 + 64 * 128;    // T diag(beta e^G)
-constexpr int OFF_W = OFF_T2 + 64 * 128;     // W [2][64][128 B]
-constexpr int OFF_ST = OFF_W + 2 * T64_BLK;  // S^T [2][128][128 B]
-constexpr int OFF_A = OFF_ST + 2 * QK_BLK;   // fp32 A [64][A_LD]
-constexpr int A_LD = 68;                     // row pitch: conflict-free float4 row stores
-constexpr int OFF_MISC = OFF_A + 64 * A_LD * 4;
-constexpr int SMEM_BYTES = OFF_MISC + 6 * 64 * 4 + 64 + 1024;
+// shared memory map (bytes from a 1024-byte aligned base); lifetimes in a chunk:
+//   QK  [prep .. S update]     V: V [prep .. U/W] -> Vn^T [Vn .. S update] -> O staging [O out]
+//   VD: (dec Vn)^T [Vn .. S update]
+//   R1: A fp32 [P/A .. T] -> T1,T2 [T .. U/W] -> W [W out .. V'/O1]
+constexpr int QK_BLK = 128 * 128;  // one 64-column block of a 128-row tile
+constexpr int T64_BLK = 64 * 128;  // one 64-column block of a 64-row tile
+constexpr int LDF = 68;            // fp32 row pitch (floats) of A and T
+constexpr int OFF_QK = 0;
+constexpr int OFF_V = OFF_QK + 2 * QK_BLK;
+constexpr int OFF_VD = OFF_V + 2 * T64_BLK;
+constexpr int OFF_P = OFF_VD + 2 * T64_BLK;
+constexpr int OFF_ST = OFF_P + T64_BLK;
+constexpr int OFF_R1 = OFF_ST + 2 * QK_BLK;
+constexpr int OFF_T1 = OFF_R1, OFF_T2 = OFF_R1 + T64_BLK, OFF_W = OFF_R1;
+constexpr int OFF_T = OFF_R1 + 64 * LDF * 4;
+constexpr int OFF_STG = OFF_T + 64 * LDF * 4;      // raw next-chunk rows: q, k, v [64][256 B] each
+constexpr int OFF_STG_G = OFF_STG + 3 * 64 * 256;  // raw g[64], beta[64]
+constexpr int OFF_MISC = OFF_STG_G + 2 * 64 * 4;   // G, beta, e^G, dec [64] each, gamma
+constexpr int SMEM_BYTES = OFF_MISC + 4 * 64 * 4 + 16 + 1024;
+static_assert(OFF_STG % 1024 == 0 && OFF_R1 % 1024 == 0, "tile alignment");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 __device__ int g_chunked_error = 0;
 
@@ -59,8 +72,7 @@ __device__ __forceinline__ uint32_t sw(int r, int ch) { return (uint32_t)(r * 12
 __device__ __forceinline__ uint32_t sw_elem(int r, int c) { return sw(r, c >> 3) + (uint32_t)((c & 7) << 1); }
 
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, float* f) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
   const T* h = reinterpret_cast<const T*>(&u);
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = to_f32(h[i]);
@@ -74,6 +86,37 @@ __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   return u;
 }
 
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
+}
+
+// Issue the copies of chunk `c` (rows < nvalid) into the staging buffer.
+template <typename TIn>
+__device__ __forceinline__ void prefetch_chunk(uint8_t* sm, const TIn* q, const TIn* k, const TIn* v, const float* g,
+                                               const float* beta, int b, int hk, int hv, int T, int Hqk, int Hv,
+                                               int c, int tid) {
+  const int t0 = c * C;
+  const int nvalid = min(C, T - t0);
+#pragma unroll 4
+  for (int i = tid; i < 3 * 64 * 16; i += NT) {
+    const int which = i >> 10, r = (i >> 4) & 63, ch = i & 15;
+    if (r >= nvalid) continue;
+    const size_t tok = (size_t)b * T + t0 + r;
+    const TIn* src = which == 0 ? q + (tok * Hqk + hk) * D : which == 1 ? k + (tok * Hqk + hk) * D
+                                                                        : v + (tok * Hv + hv) * D;
+    cp_async16(sm + OFF_STG + which * 64 * 256 + r * 256 + ch * 16, src + ch * 8);
+  }
+  if (tid < 128) {
+    const int r = tid & 63;
+    if (r < nvalid) {
+      const size_t idx = ((size_t)b * T + t0 + r) * Hv + hv;
+      cp_async4(sm + OFF_STG_G + (tid >> 6) * 256 + r * 4, (tid >> 6) ? beta + idx : g + idx);
+    }
+  }
+  cp_async_commit();
+}
+
 template <typename TIn, typename TOut>
 __global__ void __launch_bounds__(NT, 1)
 gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
@@ -85,18 +128,25 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   float* sBeta = sG + 64;
   float* sEG = sG + 128;
   float* sDec = sG + 192;
-  float* sA = reinterpret_cast<float*>(sm + OFF_A);
+  float* sGamma = sG + 256;
+  float* sA = reinterpret_cast<float*>(sm + OFF_R1);
+  float* sT = reinterpret_cast<float*>(sm + OFF_T);
+  const float* stgG = reinterpret_cast<const float*>(sm + OFF_STG_G);
   __shared__ uint64_t mbar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row = tid & 127;   // TMEM lane this thread reads (warps w and w+4 share a lane quarter)
+  const int half = tid >> 7;   // which half of the columns it reads
   const int bh = blockIdx.x;
   const int b = bh / Hv, hv = bh % Hv;
   const int hk = hv / (Hv / Hqk);
   const uint32_t sbase = tc::smem_u32(sm);
   const uint32_t bar = tc::smem_u32(&mbar);
+  const int nchunks = (T + C - 1) / C;
 
+  prefetch_chunk(sm, q, k, v, g, beta, b, hk, hv, T, Hqk, Hv, 0, tid);
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, TMEM_COLS);
     tc::tmem_relinquish();
@@ -110,18 +160,19 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM sub-partition
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
   uint32_t phase = 0;
 
-  // ---- initial state: thread d holds column d of S (row d of S^T) ----
+  // ---- initial state: thread (row d, half) holds S[half*64 .. +64, d] (row d of S^T) ----
   float* Sg = state + (size_t)bh * D * D;
   {
     float buf[32];
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int k0 = half * 64 + j * 32;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) buf[i] = Sg[(size_t)(j * 32 + i) * D + tid];
-      tc::tmem_st32(lane_addr + COL_S + j * 32, buf);
+      for (int i = 0; i < 32; ++i) buf[i] = Sg[(size_t)(k0 + i) * D + row];
+      tc::tmem_st32(lane_addr + COL_S + k0, buf);
     }
     tc::tmem_wait_st();
   }
@@ -137,18 +188,25 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     tc::fence_after();
     return ok;
   };
+  auto sync_smem_for_mma = [&]() {
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+  };
 
-  const int nchunks = (T + C - 1) / C;
+#pragma unroll 1
   for (int c = 0; c < nchunks && !abort_flag; ++c) {
     const int t0 = c * C;
     const int nvalid = min(C, T - t0);
+    cp_async_wait<0>();
+    __syncthreads();
+
     // ---------------- gates: cumulative log decay (padding tokens: g = beta = 0) ----------------
     if (warp == 0) {
-      float g0 = 0.f, g1 = 0.f, b0 = 0.f, b1 = 0.f;
       const int i0 = 2 * lane, i1 = 2 * lane + 1;
-      const size_t base = ((size_t)b * T + t0) * Hv + hv;
-      if (i0 < nvalid) { g0 = g[base + (size_t)i0 * Hv]; b0 = beta[base + (size_t)i0 * Hv]; }
-      if (i1 < nvalid) { g1 = g[base + (size_t)i1 * Hv]; b1 = beta[base + (size_t)i1 * Hv]; }
+      const float g0 = i0 < nvalid ? stgG[i0] : 0.f, g1 = i1 < nvalid ? stgG[i1] : 0.f;
+      const float b0 = i0 < nvalid ? stgG[64 + i0] : 0.f, b1 = i1 < nvalid ? stgG[64 + i1] : 0.f;
       float s = g0 + g1;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -156,33 +214,30 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         if (lane >= o) s += n;
       }
       const float G1 = s, G0 = s - g1;
+      const float Glast = __shfl_sync(0xffffffffu, G1, 31);
       sG[i0] = G0;
       sG[i1] = G1;
       sBeta[i0] = b0;
       sBeta[i1] = b1;
-      const float Glast = __shfl_sync(0xffffffffu, G1, 31);
       sEG[i0] = __expf(G0);
       sEG[i1] = __expf(G1);
       sDec[i0] = __expf(Glast - G0);
       sDec[i1] = __expf(Glast - G1);
-      if (lane == 0) sG[256] = __expf(Glast);  // gamma, after the four 64-float arrays
+      if (lane == 0) *sGamma = __expf(Glast);
     }
-    __syncthreads();
 
-    // ---------------- tiles: Q, diag(e^G) Q, K, V (fp16, swizzled) ----------------
+    // ---------------- tiles: Q, K, V (fp16, swizzled) from the staging buffer ----------------
     {
       const int ch = tid & 15;  // 16-byte chunk of the 256-byte row
       const int blk = ch >> 3, cb = ch & 7;
 #pragma unroll 2
-      for (int it = 0; it < 8; ++it) {
-        const int r = (tid >> 4) + it * 8;  // token row 0..63
-        const bool valid = r < nvalid;
-        const size_t tok = (size_t)b * T + t0 + r;
+      for (int it = 0; it < 4; ++it) {
+        const int r = (tid >> 4) + it * 16;  // token row 0..63
         float fq[8], fk[8], fv[8];
-        if (valid) {
-          load8(q + (tok * Hqk + hk) * D + ch * 8, fq);
-          load8(k + (tok * Hqk + hk) * D + ch * 8, fk);
-          load8(v + (tok * Hv + hv) * D + ch * 8, fv);
+        if (r < nvalid) {
+          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + r * 256 + ch * 16), fq);
+          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + 64 * 256 + r * 256 + ch * 16), fk);
+          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + 128 * 256 + r * 256 + ch * 16), fv);
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) fq[i] = fk[i] = fv[i] = 0.f;
@@ -203,18 +258,11 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         *reinterpret_cast<uint4*>(sm + OFF_QK + blk * QK_BLK + sw(r, cb)) = pack8_f16(fq);
         *reinterpret_cast<uint4*>(sm + OFF_QK + blk * QK_BLK + sw(64 + r, cb)) = pack8_f16(fk);
         *reinterpret_cast<uint4*>(sm + OFF_V + blk * T64_BLK + sw(r, cb)) = pack8_f16(fv);
-        const float e = sEG[r];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) fq[i] *= e;
-        *reinterpret_cast<uint4*>(sm + OFF_QT + blk * T64_BLK + sw(r, cb)) = pack8_f16(fq);
       }
     }
-    tc::fence_async_smem();
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
+    sync_smem_for_mma();
 
-    // ---------------- D1 = [Q;K] K^T ----------------
+    // ---------------- D1 = [Q;K] K^T ; prefetch the next chunk ----------------
     if (tid == 0) {
       constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
 #pragma unroll
@@ -222,90 +270,154 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         const uint32_t koff = (uint32_t)((s >> 2) * QK_BLK + (s & 3) * 32);
         const uint64_t ad = tc::sdesc_sw128(sbase + OFF_QK + koff, 16, 1024);
         const uint64_t bd = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + koff, 16, 1024);
-        tc::mma_f16(tmem + COL_O, ad, bd, id, s > 0);
+        tc::mma_f16(tmem + COL_D, ad, bd, id, s > 0);
       }
       tc::commit(bar);
     }
-    if (!sync_mma()) break;
+    if (c + 1 < nchunks) prefetch_chunk(sm, q, k, v, g, beta, b, hk, hv, T, Hqk, Hv, c + 1, tid);
 
-    // ---------------- P, A; state readout ----------------
+    // state readout (independent of D1): S^T row -> fp16 operand, then scale the accumulator by gamma
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_O, r0);
-      tc::tmem_ld32(lane_addr + COL_O + 32, r1);
-      tc::tmem_wait_ld();
-      if (tid < 64) {
-        const int i = tid;
-        const float Gi = sG[i];
-        float p[64];
+      const float gamma = *sGamma;
+#pragma unroll 1
+      for (int j = 0; j < 2; ++j) {
+        const int k0 = half * 64 + j * 32;
+        float s32[32];
+        tc::tmem_ld32(lane_addr + COL_S + k0, s32);
+        tc::tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 64; ++j) {
-          const float x = j < 32 ? r0[j] : r1[j - 32];
-          p[j] = j <= i ? x * __expf(Gi - sG[j]) : 0.f;
+        for (int cb = 0; cb < 4; ++cb) {
+          const int kc = (k0 >> 3) + cb;  // 16-byte chunk index 0..15 along d_k
+          *reinterpret_cast<uint4*>(sm + OFF_ST + (kc >> 3) * QK_BLK + sw(row, kc & 7)) = pack8_f16(s32 + cb * 8);
         }
 #pragma unroll
-        for (int cb = 0; cb < 8; ++cb)
-          *reinterpret_cast<uint4*>(sm + OFF_P + sw(i, cb)) = pack8_f16(p + cb * 8);
-      } else {
-        const int i = tid - 64;
-        const float Gi = sG[i], bi = sBeta[i];
-        float* arow = sA + i * A_LD;
+        for (int e = 0; e < 32; ++e) s32[e] *= gamma;
+        tc::tmem_st32(lane_addr + COL_S + k0, s32);
+      }
+      tc::tmem_wait_st();
+    }
+    if (!sync_mma()) break;
+
+    // ---------------- P (rows 0-63), A (rows 64-127): each thread 32 columns ----------------
+    {
+      const int i = row & 63;
+      const float Gi = sG[i];
+      float r32[32];
+      tc::tmem_ld32(lane_addr + COL_D + half * 32, r32);
+      tc::tmem_wait_ld();
+      if (row < 64) {
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
+        for (int cb = 0; cb < 4; ++cb) {
+          float p8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int j = half * 32 + cb * 8 + e;
+            p8[e] = j <= i ? r32[cb * 8 + e] * __expf(Gi - sG[j]) : 0.f;
+          }
+          *reinterpret_cast<uint4*>(sm + OFF_P + sw(i, half * 4 + cb)) = pack8_f16(p8);
+        }
+      } else {
+        const float bi = sBeta[i];
+        float* arow = sA + i * LDF + half * 32;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
           float a4[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int j = j4 * 4 + e;
-            const float x = j < 32 ? r0[j] : r1[j - 32];
-            a4[e] = j < i ? bi * x * __expf(Gi - sG[j]) : 0.f;
+            const int j = half * 32 + j4 * 4 + e;
+            a4[e] = j < i ? bi * r32[j4 * 4 + e] * __expf(Gi - sG[j]) : 0.f;
           }
           *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(a4[0], a4[1], a4[2], a4[3]);
         }
       }
-      // S^T row (lane = d_v index) -> fp16 operand; then scale the accumulator by gamma
-      const float gamma = sG[256];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float s32[32];
-        tc::tmem_ld32(lane_addr + COL_S + j * 32, s32);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          const int kc = j * 4 + cb;  // 16-byte chunk index 0..15 along d_k
-          *reinterpret_cast<uint4*>(sm + OFF_ST + (kc >> 3) * QK_BLK + sw(tid, kc & 7)) = pack8_f16(s32 + cb * 8);
-        }
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s32[i] *= gamma;
-        tc::tmem_st32(lane_addr + COL_S + j * 32, s32);
-      }
-      tc::tmem_wait_st();
     }
     tc::fence_before();
     __syncthreads();
 
-    // ---------------- T = (I + A)^-1 by forward substitution (thread j: column j) ----------------
+    // ---------------- T = (I + A)^-1, blockwise ----------------
+    // (1) diagonal 16x16 blocks: thread (blk, j) solves column j by right-looking substitution
     if (tid < 64) {
-      const int j = tid;
-      float t[64];
+      const int o = (tid >> 4) * 16, j = tid & 15;
+      float x[16];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        float acc = (i == j) ? 1.f : 0.f;
-        const float* arow = sA + i * A_LD;
+      for (int i = 0; i < 16; ++i) x[i] = i == j ? 1.f : 0.f;
 #pragma unroll
-        for (int kk = 0; kk < i; ++kk) acc -= arow[kk] * t[kk];
-        t[i] = acc;
+      for (int kk = 0; kk < 15; ++kk) {
+        const float xk = x[kk];
+#pragma unroll
+        for (int i = kk + 1; i < 16; ++i) x[i] -= sA[(o + i) * LDF + o + kk] * xk;
       }
-      const float bj = sBeta[j], bej = sBeta[j] * sEG[j];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        *reinterpret_cast<__half*>(sm + OFF_T1 + sw_elem(i, j)) = __float2half_rn(t[i] * bj);
-        *reinterpret_cast<__half*>(sm + OFF_T2 + sw_elem(i, j)) = __float2half_rn(t[i] * bej);
+      for (int i = 0; i < 16; ++i) sT[(o + i) * LDF + o + j] = x[i];
+    }
+    __syncthreads();
+    // (2) 16 -> 32: X = A_{r,c} T_{c,c} (kept in A's unused upper block), T_{r,c} = -T_{r,r} X
+    {
+      const int m = tid >> 7, idx = tid & 127, r = idx >> 3, c0 = (idx & 7) * 2;
+      const int ro = m ? 48 : 16, co = m ? 32 : 0;  // block rows ro.., block cols co..
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        const float a = sA[(ro + r) * LDF + co + kk];
+        const float2 t2 = *reinterpret_cast<const float2*>(sT + (co + kk) * LDF + co + c0);
+        a0 += a * t2.x;
+        a1 += a * t2.y;
+      }
+      *reinterpret_cast<float2*>(sA + (ro - 16 + r) * LDF + co + 16 + c0) = make_float2(a0, a1);
+      __syncthreads();
+      a0 = a1 = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        const float t = sT[(ro + r) * LDF + ro + kk];
+        const float2 x2 = *reinterpret_cast<const float2*>(sA + (ro - 16 + kk) * LDF + co + 16 + c0);
+        a0 += t * x2.x;
+        a1 += t * x2.y;
+      }
+      *reinterpret_cast<float2*>(sT + (ro + r) * LDF + co + c0) = make_float2(-a0, -a1);
+    }
+    __syncthreads();
+    // (3) 32 -> 64: Y = A[32:64, 0:32] T[0:32, 0:32] (kept in A[0:32, 32:64]); T[32:64, 0:32] = -T[32:64, 32:64] Y
+    {
+      const int r = tid >> 3, c0 = (tid & 7) * 4;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int k_lo = c0 >= 16 ? 16 : 0;  // T[0:16, 16:32] is the (zero) upper block
+#pragma unroll 4
+      for (int kk = k_lo; kk < 32; ++kk) {
+        const float a = sA[(32 + r) * LDF + kk];
+        const float4 t4 = *reinterpret_cast<const float4*>(sT + kk * LDF + c0);
+        acc[0] += a * t4.x; acc[1] += a * t4.y; acc[2] += a * t4.z; acc[3] += a * t4.w;
+      }
+      *reinterpret_cast<float4*>(sA + r * LDF + 32 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      __syncthreads();
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+      const int k_hi = r < 16 ? 16 : 32;  // T[32:48, 48:64] is the (zero) upper block
+#pragma unroll 4
+      for (int kk = 0; kk < k_hi; ++kk) {
+        const float t = sT[(32 + r) * LDF + 32 + kk];
+        const float4 y4 = *reinterpret_cast<const float4*>(sA + kk * LDF + 32 + c0);
+        acc[0] += t * y4.x; acc[1] += t * y4.y; acc[2] += t * y4.z; acc[3] += t * y4.w;
+      }
+      *reinterpret_cast<float4*>(sT + (32 + r) * LDF + c0) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
+    }
+    __syncthreads();
+    // T1 = T diag(beta), T2 = T diag(beta e^G): fp16, swizzled, over A's (now dead) storage
+    {
+      const int r = tid >> 2, cq = (tid & 3) * 2;  // two 8-column chunks per thread
+#pragma unroll
+      for (int cb = 0; cb < 2; ++cb) {
+        float t1[8], t2[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int cc = (cq + cb) * 8 + e;
+          const float t = cc <= r ? sT[r * LDF + cc] : 0.f;
+          t1[e] = t * sBeta[cc];
+          t2[e] = t1[e] * sEG[cc];
+        }
+        *reinterpret_cast<uint4*>(sm + OFF_T1 + sw(r, cq + cb)) = pack8_f16(t1);
+        *reinterpret_cast<uint4*>(sm + OFF_T2 + sw(r, cq + cb)) = pack8_f16(t2);
       }
     }
-    tc::fence_async_smem();
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
+    sync_smem_for_mma();
 
     // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T ----------------
     if (tid == 0) {
@@ -317,32 +429,25 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         tc::mma_f16(tmem + COL_U, av, b1, id, s > 0);
         const uint64_t ak = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
         const uint64_t b2 = tc::sdesc_sw128(sbase + OFF_T2 + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_O, ak, b2, id, s > 0);
+        tc::mma_f16(tmem + COL_D, ak, b2, id, s > 0);
       }
       tc::commit(bar);
     }
     if (!sync_mma()) break;
 
-    // ---------------- W readout: lane = d_k index, columns = tokens ----------------
+    // ---------------- W readout: lane = d_k index, 32 token columns per thread ----------------
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_O, r0);
-      tc::tmem_ld32(lane_addr + COL_O + 32, r1);
+      uint8_t* wb = sm + OFF_W + (row >> 6) * T64_BLK;
+      float r32[32];
+      tc::tmem_ld32(lane_addr + COL_D + half * 32, r32);
       tc::tmem_wait_ld();
-      const int d = tid;
-      uint8_t* wb = sm + OFF_W + (d >> 6) * T64_BLK;
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
-        const float x = t < 32 ? r0[t] : r1[t - 32];
-        *reinterpret_cast<__half*>(wb + sw_elem(t, d & 63)) = __float2half_rn(x);
-      }
+      for (int t = 0; t < 32; ++t)
+        *reinterpret_cast<__half*>(wb + sw_elem(half * 32 + t, row & 63)) = __float2half_rn(r32[t]);
     }
-    tc::fence_async_smem();
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
+    sync_smem_for_mma();
 
-    // ---------------- Vn^T = U^T - S^T W^T ; O^T = S^T Qt^T ----------------
+    // ---------------- Vn^T = U^T - S^T W^T ; O1^T = S^T Q^T ----------------
     if (tid == 0) {
       constexpr uint32_t idn = tc::idesc_f16(128, 64, false, false, true);
       constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
@@ -351,39 +456,30 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         const uint64_t as = tc::sdesc_sw128(sbase + OFF_ST + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
         const uint64_t bw = tc::sdesc_sw128(sbase + OFF_W + (s >> 2) * T64_BLK + (s & 3) * 32, 16, 1024);
         tc::mma_f16(tmem + COL_U, as, bw, idn, 1);
-        const uint64_t bq = tc::sdesc_sw128(sbase + OFF_QT + (s >> 2) * T64_BLK + (s & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_O, as, bq, id, s > 0);
+        const uint64_t bq = tc::sdesc_sw128(sbase + OFF_QK + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
+        tc::mma_f16(tmem + COL_O1, as, bq, id, s > 0);
       }
       tc::commit(bar);
     }
     if (!sync_mma()) break;
 
-    // ---------------- Vn readout: lane = d_v index, columns = tokens ----------------
+    // ---------------- Vn readout: lane = d_v index, 32 token columns per thread ----------------
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_U, r0);
-      tc::tmem_ld32(lane_addr + COL_U + 32, r1);
+      float r32[32];
+      tc::tmem_ld32(lane_addr + COL_U + half * 32, r32);
       tc::tmem_wait_ld();
-      const int d = tid;
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        float x[8], y[8];
+      for (int cb = 0; cb < 4; ++cb) {
+        float y[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int t = cb * 8 + e;
-          x[e] = t < 32 ? r0[t] : r1[t - 32];
-          y[e] = x[e] * sDec[t];
-        }
-        *reinterpret_cast<uint4*>(sm + OFF_V + sw(d, cb)) = pack8_f16(x);
-        *reinterpret_cast<uint4*>(sm + OFF_VD + sw(d, cb)) = pack8_f16(y);
+        for (int e = 0; e < 8; ++e) y[e] = r32[cb * 8 + e] * sDec[half * 32 + cb * 8 + e];
+        *reinterpret_cast<uint4*>(sm + OFF_V + sw(row, half * 4 + cb)) = pack8_f16(r32 + cb * 8);
+        *reinterpret_cast<uint4*>(sm + OFF_VD + sw(row, half * 4 + cb)) = pack8_f16(y);
       }
     }
-    tc::fence_async_smem();
-    tc::fence_before();
-    __syncthreads();
-    tc::fence_after();
+    sync_smem_for_mma();
 
-    // ---------------- O^T += Vn^T P^T ; S^T += (dec Vn)^T K ----------------
+    // ---------------- O2^T = Vn^T P^T ; S^T += (dec Vn)^T K ----------------
     if (tid == 0) {
       constexpr uint32_t id64 = tc::idesc_f16(128, 64, false, false);
       constexpr uint32_t id128 = tc::idesc_f16(128, 128, false, true);
@@ -391,7 +487,7 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
       for (int s = 0; s < 4; ++s) {
         const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 32, 16, 1024);
         const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_O, av, bp, id64, 1);
+        tc::mma_f16(tmem + COL_O2, av, bp, id64, s > 0);
         const uint64_t ad = tc::sdesc_sw128(sbase + OFF_VD + s * 32, 16, 1024);
         const uint64_t bk = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
         tc::mma_f16(tmem + COL_S, ad, bk, id128, 1);
@@ -400,18 +496,34 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     }
     if (!sync_mma()) break;
 
-    // ---------------- O readout -> global ----------------
+    // ---------------- O = (e^G O1 + O2) * scale -> global ----------------
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_O, r0);
-      tc::tmem_ld32(lane_addr + COL_O + 32, r1);
+      float o1[32], o2[32];
+      tc::tmem_ld32(lane_addr + COL_O1 + half * 32, o1);
+      tc::tmem_ld32(lane_addr + COL_O2 + half * 32, o2);
       tc::tmem_wait_ld();
-      const int d = tid;
+      if constexpr (sizeof(TOut) == 2) {
+        // stage [token][d_v] in the V region, then write whole 256-byte rows
+        TOut* ost = reinterpret_cast<TOut*>(sm + OFF_V);
 #pragma unroll
-      for (int t = 0; t < 64; ++t) {
-        if (t < nvalid) {
-          const float x = (t < 32 ? r0[t] : r1[t - 32]) * scale;
-          out[(((size_t)b * T + t0 + t) * Hv + hv) * D + d] = from_f32<TOut>(x);
+        for (int t = 0; t < 32; ++t) {
+          const int tt = half * 32 + t;
+          ost[tt * D + row] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int r = (tid >> 4) + it * 16, ch = tid & 15;
+          if (r < nvalid)
+            *reinterpret_cast<uint4*>(out + (((size_t)b * T + t0 + r) * Hv + hv) * D + ch * 8) =
+                *reinterpret_cast<const uint4*>(sm + OFF_V + r * 256 + ch * 16);
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int tt = half * 32 + t;
+          if (tt < nvalid)
+            out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + row] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
         }
       }
     }
@@ -420,15 +532,17 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     tc::fence_after();
   }
 
+  cp_async_wait<0>();
   // ---- final state ----
   if (!abort_flag) {
     float buf[32];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      tc::tmem_ld32(lane_addr + COL_S + j * 32, buf);
+#pragma unroll 1
+    for (int j = 0; j < 2; ++j) {
+      const int k0 = half * 64 + j * 32;
+      tc::tmem_ld32(lane_addr + COL_S + k0, buf);
       tc::tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) Sg[(size_t)(j * 32 + i) * D + tid] = buf[i];
+      for (int i = 0; i < 32; ++i) Sg[(size_t)(k0 + i) * D + row] = buf[i];
     }
   }
   tc::fence_before();
@@ -466,8 +580,9 @@ extern "C" int anemll_gdn_chunked_prefill(const void* q, const void* k, const vo
                  "gdn_chunked_prefill: q/k/v must be f16 or bf16");
   ANEMLL_REQUIRE(dtype_ok(out_dtype), ANEMLL_EUNSUPPORTED, "gdn_chunked_prefill: bad out dtype");
   if (T == 0) return ANEMLL_OK;
-  ANEMLL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16), ANEMLL_EALIGN,
-                 "gdn_chunked_prefill: q/k/v must be 16-byte aligned");
+  ANEMLL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(g, 4) && aligned(beta, 4) &&
+                     (dtype_size(out_dtype) == 4 || aligned(out, 16)),
+                 ANEMLL_EALIGN, "gdn_chunked_prefill: q/k/v (and 2-byte outputs) must be 16-byte aligned");
   if (scale <= 0.f) scale = 1.0f / sqrtf((float)d_k);
   cudaStream_t st = (cudaStream_t)stream;
   return ANEMLL_DISPATCH_HALF(qkv_dtype, TIn, [&] {

@@ -278,13 +278,14 @@ def bench_gdn_prefill(args, ws, rank, local):
     this rank's shard; value = all tokens of the job / max-over-ranks time."""
     from anemll_b200 import gdn, inputs
     dev = torch.device("cuda", local)
-    if ws <= PREFILL_B:
-        b_loc, hv_loc, hqk_loc = PREFILL_B // ws, H_V, H_QK
+    nseq, seqlen = args.prefill_seqs, args.prefill_len
+    if ws <= nseq:
+        b_loc, hv_loc, hqk_loc = nseq // ws, H_V, H_QK
     else:
-        b_loc, hv_loc, hqk_loc = 1, H_V * PREFILL_B // ws, H_QK * PREFILL_B // ws
-    w = inputs.gdn_prefill_device(seed=3 + 1000 * rank, B=b_loc, T=PREFILL_T, device=dev, Hqk=hqk_loc, Hv=hv_loc)
+        b_loc, hv_loc, hqk_loc = 1, H_V * nseq // ws, H_QK * nseq // ws
+    w = inputs.gdn_prefill_device(seed=3 + 1000 * rank, B=b_loc, T=seqlen, device=dev, Hqk=hqk_loc, Hv=hv_loc)
     state = torch.zeros(b_loc, hv_loc, DK, DV, device=dev)
-    out = torch.empty(b_loc, PREFILL_T, hv_loc, DV, dtype=torch.bfloat16, device=dev)
+    out = torch.empty(b_loc, seqlen, hv_loc, DV, dtype=torch.bfloat16, device=dev)
 
     def step():
         gdn.chunk_gated_delta_rule_(w["q"], w["k"], w["v"], w["g"], w["beta"], state, out=out)
@@ -306,8 +307,8 @@ def bench_gdn_prefill(args, ws, rank, local):
     ms_max = max_over_ranks(ms, ws, dev)
     if gdn.chunked_device_error(reset=True):
         raise RuntimeError("chunked prefill reported a device-side wait timeout")
-    tokens_local = b_loc * PREFILL_T
-    tokens_job = PREFILL_B * PREFILL_T
+    tokens_local = b_loc * seqlen
+    tokens_job = nseq * seqlen
     flop_launch = tokens_local * hv_loc * PREFILL_FLOP_PER_TOKEN_HEAD
     per_launch_s = ms / 1e3 / args.steps
     pk, how = peaks()
@@ -325,7 +326,7 @@ def bench_gdn_prefill(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "f16 tensor-core operands, f32 accumulate/state, bf16 in/out",
         "data": "synthetic (seeded on device; q/k l2-normalised N(0,1), v ~N(0,1))",
-        "config": {"workload": "gdn_chunked_prefill", "batch": PREFILL_B, "seq_len": PREFILL_T, "chunk": CHUNK,
+        "config": {"workload": "gdn_chunked_prefill", "batch": nseq, "seq_len": seqlen, "chunk": CHUNK,
                    "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV,
                    "l2": "no flush: 4.3 GB of inputs per step exceed the 126 MB L2",
                    "parallelism": f"{ws} ranks, sequences x value heads, no collective"},
@@ -396,6 +397,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode", "gdn_prefill"])
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
+    ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
+    ap.add_argument("--prefill-len", type=int, default=PREFILL_T, help="gdn_prefill: tokens per sequence")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     ws, rank, local = init_dist(args)
