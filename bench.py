@@ -167,7 +167,8 @@ def cpu_decode_sample(n_steps, threads):
 def bench_gdn_decode(args, ws, rank, local):
     from anemll_b200 import _lib, gdn, inputs
     dev = torch.device("cuda", local)
-    w = inputs.gdn_decode(seed=1 + 1000 * rank, B=DECODE_B, steps=DECODE_STEPS)
+    from anemll_b200 import shard
+    w = inputs.gdn_decode(seed=shard.decode_seed(1, rank), B=DECODE_B, steps=DECODE_STEPS)
     state = w["state"].to(dev)
     q, k, v, g, beta = (w[n].to(dev) for n in ("q", "k", "v", "g", "beta"))
     out = torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16, device=dev)
@@ -276,13 +277,11 @@ def bench_gdn_prefill(args, ws, rank, local):
     step); with more ranks than sequences the value heads are split too (the
     head pairs that share a key head stay together).  One step = one prefill of
     this rank's shard; value = all tokens of the job / max-over-ranks time."""
-    from anemll_b200 import gdn, inputs
+    from anemll_b200 import gdn, inputs, shard
     dev = torch.device("cuda", local)
     nseq, seqlen = args.prefill_seqs, args.prefill_len
-    if ws <= nseq:
-        b_loc, hv_loc, hqk_loc = nseq // ws, H_V, H_QK
-    else:
-        b_loc, hv_loc, hqk_loc = 1, H_V * nseq // ws, H_QK * nseq // ws
+    sh = shard.prefill_shard(ws, rank, nseq, H_QK, H_V)
+    b_loc, hv_loc, hqk_loc = sh.seq_count, sh.v_head_count, sh.k_head_count
     w = inputs.gdn_prefill_device(seed=3 + 1000 * rank, B=b_loc, T=seqlen, device=dev, Hqk=hqk_loc, Hv=hv_loc)
     state = torch.zeros(b_loc, hv_loc, DK, DV, device=dev)
     out = torch.empty(b_loc, seqlen, hv_loc, DV, dtype=torch.bfloat16, device=dev)
