@@ -18,18 +18,27 @@
 // Every product is arranged so that M = 128 (d_v or d_k on TMEM lanes).  All
 // operands are fp16 in 128-byte-swizzled shared memory; accumulators are fp32
 // in TMEM.  fp16 (10-bit mantissa) operands keep the result within 1e-3
-// relative L2 of an fp32 evaluation; bf16 inputs convert to fp16 on the way in.
-// The attention scale multiplies O in fp32 at the end (O is linear in q).
+// relative L2 of an fp32 evaluation; bf16 inputs are converted to fp16 in
+// place.  The attention scale multiplies O in fp32 at the end (O is linear in q).
 //
-// 256 threads: warps w and w+4 read the same TMEM lane quarter and split its
-// columns, so every CUDA-core phase has two warps per scheduler.  The next
-// chunk's raw q/k/v rows and gates are copied with cp.async into a staging
-// buffer while the current chunk computes.  T = (I + A)^-1 is built blockwise:
+// Data movement: q/k/v tiles arrive by TMA (3-D tensor maps over [d, head,
+// token], 64-token x 64-element boxes, 128-byte swizzle done by the copy
+// engine) into two tile buffers: chunk c computes from one while chunk c+1
+// lands in the other; the in-place conversion of chunk c+1 (bf16 -> fp16,
+// optional l2-norm, zeroing of rows past the sequence end) runs while the
+// tensor core works on chunk c.  256 threads: warps w and w+4 read the same
+// TMEM lane quarter and split its columns.  T = (I + A)^-1 is built blockwise:
 // four 16x16 diagonal blocks by forward substitution, then 16 -> 32 -> 64
 // merges T21 = -T22 (A21 T11) as small fp32 matrix products over all threads.
 //
 // Semantics: torch_chunk_gated_delta_rule of transformers 5.5.0
 // (modeling_qwen3_5.py:234-311); chunk (WY/UT) form of Yang et al. (2024).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
 #include "common.cuh"
 #include "mma_sync.cuh"
 #include "tcgen05.cuh"
@@ -44,30 +53,35 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t COL_S = 0, COL_O1 = 128, COL_U = 192, COL_O2 = 256, COL_D = 320;
 
 // shared memory map (bytes from a 1024-byte aligned base); lifetimes in a chunk:
-//   QK  [prep .. S update]     V: V [prep .. U/W] -> Vn^T [Vn .. S update] -> O staging [O out]
-//   VD: (dec Vn)^T [Vn .. S update]
-//   R1: A fp32 [P/A .. T] -> T1,T2 [T .. U/W] -> W [W out .. V'/O1]
+//   QK[x] (TMA)   [prep .. S update]     V[x] (TMA): V [.. U/W] -> Vn^T [Vn .. S update] -> O staging
+//   VD: (dec Vn)^T [Vn .. S update]      R1: A fp32 [P/A .. T] -> T1,T2 [.. U/W] -> W [.. V'/O1]
 constexpr int QK_BLK = 128 * 128;  // one 64-column block of a 128-row tile
 constexpr int T64_BLK = 64 * 128;  // one 64-column block of a 64-row tile
-constexpr int LDF = 68;            // fp32 row pitch (floats) of A and T
-constexpr int OFF_QK = 0;
-constexpr int OFF_V = OFF_QK + 2 * QK_BLK;
-constexpr int OFF_VD = OFF_V + 2 * T64_BLK;
+constexpr int QK_BYTES = 2 * QK_BLK, V_BYTES = 2 * T64_BLK;
+constexpr int LDF = 68;  // fp32 row pitch (floats) of A and T
+constexpr int OFF_QK0 = 0;
+constexpr int OFF_V0 = OFF_QK0 + 2 * QK_BYTES;
+constexpr int OFF_VD = OFF_V0 + 2 * V_BYTES;
 constexpr int OFF_P = OFF_VD + 2 * T64_BLK;
 constexpr int OFF_ST = OFF_P + T64_BLK;
 constexpr int OFF_R1 = OFF_ST + 2 * QK_BLK;
 constexpr int OFF_T1 = OFF_R1, OFF_T2 = OFF_R1 + T64_BLK, OFF_W = OFF_R1;
 constexpr int OFF_T = OFF_R1 + 64 * LDF * 4;
-constexpr int OFF_STG = OFF_T + 64 * LDF * 4;      // raw next-chunk rows: q, k, v [64][256 B] each
-constexpr int OFF_STG_G = OFF_STG + 3 * 64 * 256;  // raw g[64], beta[64]
-constexpr int OFF_MISC = OFF_STG_G + 2 * 64 * 4;   // G, beta, e^G, dec [64] each, gamma
+constexpr int OFF_GB = OFF_T + 64 * LDF * 4;    // raw g, beta per buffer: [2][128] floats
+constexpr int OFF_MISC = OFF_GB + 2 * 128 * 4;  // G, beta, e^G, dec [64] each, gamma
 constexpr int SMEM_BYTES = OFF_MISC + 4 * 64 * 4 + 16 + 1024;
-static_assert(OFF_STG % 1024 == 0 && OFF_R1 % 1024 == 0, "tile alignment");
+constexpr uint32_t TILE_TX_BYTES = QK_BYTES + V_BYTES;  // bytes one chunk's six boxes deliver
+static_assert(OFF_R1 % 1024 == 0 && OFF_ST % 1024 == 0, "tile alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+struct TileMaps {
+  CUtensorMap q, k, v;
+};
 
 __device__ int g_chunked_error = 0;
 
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` inside a 128-byte-row swizzled block
+// (the TMA 128-byte swizzle: chunk index XOR row index mod 8, 1024-byte aligned blocks)
 __device__ __forceinline__ uint32_t sw(int r, int ch) { return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)); }
 __device__ __forceinline__ uint32_t sw_elem(int r, int c) { return sw(r, c >> 3) + (uint32_t)((c & 7) << 1); }
 
@@ -91,37 +105,51 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem));
 }
 
-// Issue the copies of chunk `c` (rows < nvalid) into the staging buffer.
+// Rewrite one chunk's tiles in place as fp16: convert from TIn, l2-normalise q
+// and k rows if asked, zero the rows at and past `nvalid`.
 template <typename TIn>
-__device__ __forceinline__ void prefetch_chunk(uint8_t* sm, const TIn* q, const TIn* k, const TIn* v, const float* g,
-                                               const float* beta, int b, int hk, int hv, int T, int Hqk, int Hv,
-                                               int c, int tid) {
-  const int t0 = c * C;
-  const int nvalid = min(C, T - t0);
-#pragma unroll 4
-  for (int i = tid; i < 3 * 64 * 16; i += NT) {
-    const int which = i >> 10, r = (i >> 4) & 63, ch = i & 15;
-    if (r >= nvalid) continue;
-    const size_t tok = (size_t)b * T + t0 + r;
-    const TIn* src = which == 0 ? q + (tok * Hqk + hk) * D : which == 1 ? k + (tok * Hqk + hk) * D
-                                                                        : v + (tok * Hv + hv) * D;
-    cp_async16(sm + OFF_STG + which * 64 * 256 + r * 256 + ch * 16, src + ch * 8);
-  }
-  if (tid < 128) {
-    const int r = tid & 63;
+__device__ __forceinline__ void convert_tiles(uint8_t* qk, uint8_t* vt, int nvalid, int l2norm, int tid) {
+  const int ch = tid & 15;
+  const int blk = ch >> 3, cb = ch & 7;
+#pragma unroll 1
+  for (int it = 0; it < 4; ++it) {
+    const int r = (tid >> 4) + it * 16;
+    uint4* pq = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(r, cb));
+    uint4* pk = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(64 + r, cb));
+    uint4* pv = reinterpret_cast<uint4*>(vt + blk * T64_BLK + sw(r, cb));
+    float fq[8], fk[8], fv[8];
     if (r < nvalid) {
-      const size_t idx = ((size_t)b * T + t0 + r) * Hv + hv;
-      cp_async4(sm + OFF_STG_G + (tid >> 6) * 256 + r * 4, (tid >> 6) ? beta + idx : g + idx);
+      unpack8<TIn>(*pq, fq);
+      unpack8<TIn>(*pk, fk);
+      unpack8<TIn>(*pv, fv);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) fq[i] = fk[i] = fv[i] = 0.f;
     }
+    if (l2norm) {
+      float sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { sq += fq[i] * fq[i]; sk += fk[i] * fk[i]; }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
+      }
+      const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) { fq[i] *= rq; fk[i] *= rk; }
+    }
+    *pq = pack8_f16(fq);
+    *pk = pack8_f16(fk);
+    *pv = pack8_f16(fv);
   }
-  cp_async_commit();
 }
 
 template <typename TIn, typename TOut>
 __global__ void __launch_bounds__(NT, 1)
-gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
-                   const float* __restrict__ g, const float* __restrict__ beta, float* __restrict__ state,
-                   TOut* __restrict__ out, int T, int Hqk, int Hv, float scale, int l2norm) {
+gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restrict__ g, const float* __restrict__ beta,
+                   float* __restrict__ state, TOut* __restrict__ out, int T, int Hqk, int Hv, float scale,
+                   int l2norm) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* sG = reinterpret_cast<float*>(sm + OFF_MISC);
@@ -131,8 +159,8 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   float* sGamma = sG + 256;
   float* sA = reinterpret_cast<float*>(sm + OFF_R1);
   float* sT = reinterpret_cast<float*>(sm + OFF_T);
-  const float* stgG = reinterpret_cast<const float*>(sm + OFF_STG_G);
-  __shared__ uint64_t mbar;
+  __shared__ uint64_t mbar;       // tensor-core completions
+  __shared__ uint64_t tbar[2];    // TMA arrivals per tile buffer
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -144,24 +172,56 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   const int hk = hv / (Hv / Hqk);
   const uint32_t sbase = tc::smem_u32(sm);
   const uint32_t bar = tc::smem_u32(&mbar);
+  const uint32_t tb0 = tc::smem_u32(&tbar[0]);
   const int nchunks = (T + C - 1) / C;
+  // fp16 inputs without l2-norm need no rewrite except for a ragged last chunk
+  constexpr bool kConvert = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
+  const bool always_convert = kConvert || l2norm;
 
-  prefetch_chunk(sm, q, k, v, g, beta, b, hk, hv, T, Hqk, Hv, 0, tid);
+  // chunk cc -> buffer cc & 1: six TMA boxes plus the gates by cp.async
+  auto issue_loads = [&](int cc) {
+    const int x = cc & 1;
+    const int tok0 = b * T + cc * C;
+    if (tid == 0) {
+      const uint32_t tb = tb0 + 8u * x;
+      tc::mbar_arrive_expect_tx(tb, TILE_TX_BYTES);
+      const uint32_t qk = sbase + OFF_QK0 + x * QK_BYTES, vt = sbase + OFF_V0 + x * V_BYTES;
+      tc::tma_load_3d(qk, &maps.q, 0, hk, tok0, tb);
+      tc::tma_load_3d(qk + QK_BLK, &maps.q, 64, hk, tok0, tb);
+      tc::tma_load_3d(qk + 64 * 128, &maps.k, 0, hk, tok0, tb);
+      tc::tma_load_3d(qk + QK_BLK + 64 * 128, &maps.k, 64, hk, tok0, tb);
+      tc::tma_load_3d(vt, &maps.v, 0, hv, tok0, tb);
+      tc::tma_load_3d(vt + T64_BLK, &maps.v, 64, hv, tok0, tb);
+    }
+    if (tid < 128) {
+      const int r = tid & 63;
+      if (cc * C + r < T) {
+        const size_t idx = ((size_t)b * T + cc * C + r) * Hv + hv;
+        cp_async4(sm + OFF_GB + x * 512 + (tid >> 6) * 256 + r * 4, (tid >> 6) ? beta + idx : g + idx);
+      }
+    }
+    cp_async_commit();
+  };
+
+  if (tid == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&tbar[0], 1);
+    tc::mbar_init(&tbar[1], 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
   if (warp == 0) {
     tc::tmem_alloc(&tmem_slot, TMEM_COLS);
     tc::tmem_relinquish();
   }
-  if (tid == 0) {
-    tc::mbar_init(&mbar, 1);
-    tc::fence_mbar_init();
-    abort_flag = 0;
-  }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
+  issue_loads(0);
   const uint32_t tmem = tmem_slot;
   const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);  // this warp's TMEM lane quarter
   uint32_t phase = 0;
+  int pending_chunk = 0;  // chunk whose tiles were requested and not yet waited for (-1: none)
 
   // ---- initial state: thread (row d, half) holds S[half*64 .. +64, d] (row d of S^T) ----
   float* Sg = state + (size_t)bh * D * D;
@@ -177,15 +237,22 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     tc::tmem_wait_st();
   }
 
+  auto fail = [&]() {
+    atomicExch(&g_chunked_error, 1);
+    abort_flag = 1;
+  };
   auto sync_mma = [&]() -> bool {
     // every thread: wait until the MMAs committed so far have completed
     const bool ok = tc::mbar_wait(bar, phase);
     phase ^= 1u;
-    if (!ok) {
-      atomicExch(&g_chunked_error, 1);
-      abort_flag = 1;
-    }
+    if (!ok) fail();
     tc::fence_after();
+    return ok;
+  };
+  auto wait_tiles = [&](int cc) -> bool {
+    const bool ok = tc::mbar_wait(tb0 + 8u * (cc & 1), (uint32_t)((cc >> 1) & 1));
+    if (!ok) fail();
+    else pending_chunk = -1;
     return ok;
   };
   auto sync_smem_for_mma = [&]() {
@@ -195,18 +262,26 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     tc::fence_after();
   };
 
+  if (wait_tiles(0) && (always_convert || T < C))
+    convert_tiles<TIn>(sm + OFF_QK0, sm + OFF_V0, min(C, T), l2norm, tid);
+
 #pragma unroll 1
   for (int c = 0; c < nchunks && !abort_flag; ++c) {
+    const int x = c & 1;
     const int t0 = c * C;
     const int nvalid = min(C, T - t0);
+    const uint32_t qk_a = sbase + OFF_QK0 + x * QK_BYTES;
+    const uint32_t v_a = sbase + OFF_V0 + x * V_BYTES;
+    const int v_off = OFF_V0 + x * V_BYTES;
     cp_async_wait<0>();
     __syncthreads();
 
     // ---------------- gates: cumulative log decay (padding tokens: g = beta = 0) ----------------
     if (warp == 0) {
+      const float* gb = reinterpret_cast<const float*>(sm + OFF_GB + x * 512);
       const int i0 = 2 * lane, i1 = 2 * lane + 1;
-      const float g0 = i0 < nvalid ? stgG[i0] : 0.f, g1 = i1 < nvalid ? stgG[i1] : 0.f;
-      const float b0 = i0 < nvalid ? stgG[64 + i0] : 0.f, b1 = i1 < nvalid ? stgG[64 + i1] : 0.f;
+      const float g0 = i0 < nvalid ? gb[i0] : 0.f, g1 = i1 < nvalid ? gb[i1] : 0.f;
+      const float b0 = i0 < nvalid ? gb[64 + i0] : 0.f, b1 = i1 < nvalid ? gb[64 + i1] : 0.f;
       float s = g0 + g1;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -225,56 +300,24 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
       sDec[i1] = __expf(Glast - G1);
       if (lane == 0) *sGamma = __expf(Glast);
     }
-
-    // ---------------- tiles: Q, K, V (fp16, swizzled) from the staging buffer ----------------
-    {
-      const int ch = tid & 15;  // 16-byte chunk of the 256-byte row
-      const int blk = ch >> 3, cb = ch & 7;
-#pragma unroll 2
-      for (int it = 0; it < 4; ++it) {
-        const int r = (tid >> 4) + it * 16;  // token row 0..63
-        float fq[8], fk[8], fv[8];
-        if (r < nvalid) {
-          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + r * 256 + ch * 16), fq);
-          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + 64 * 256 + r * 256 + ch * 16), fk);
-          unpack8<TIn>(*reinterpret_cast<const uint4*>(sm + OFF_STG + 128 * 256 + r * 256 + ch * 16), fv);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) fq[i] = fk[i] = fv[i] = 0.f;
-        }
-        if (l2norm) {
-          float sq = 0.f, sk = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) { sq += fq[i] * fq[i]; sk += fk[i] * fk[i]; }
-#pragma unroll
-          for (int o = 1; o < 16; o <<= 1) {
-            sq += __shfl_xor_sync(0xffffffffu, sq, o);
-            sk += __shfl_xor_sync(0xffffffffu, sk, o);
-          }
-          const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) { fq[i] *= rq; fk[i] *= rk; }
-        }
-        *reinterpret_cast<uint4*>(sm + OFF_QK + blk * QK_BLK + sw(r, cb)) = pack8_f16(fq);
-        *reinterpret_cast<uint4*>(sm + OFF_QK + blk * QK_BLK + sw(64 + r, cb)) = pack8_f16(fk);
-        *reinterpret_cast<uint4*>(sm + OFF_V + blk * T64_BLK + sw(r, cb)) = pack8_f16(fv);
-      }
-    }
     sync_smem_for_mma();
+    if (c + 1 < nchunks) {  // the other buffer was released by chunk c-1
+      issue_loads(c + 1);
+      pending_chunk = c + 1;
+    }
 
-    // ---------------- D1 = [Q;K] K^T ; prefetch the next chunk ----------------
+    // ---------------- D1 = [Q;K] K^T ----------------
     if (tid == 0) {
       constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint32_t koff = (uint32_t)((s >> 2) * QK_BLK + (s & 3) * 32);
-        const uint64_t ad = tc::sdesc_sw128(sbase + OFF_QK + koff, 16, 1024);
-        const uint64_t bd = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + koff, 16, 1024);
+        const uint64_t ad = tc::sdesc_sw128(qk_a + koff, 16, 1024);
+        const uint64_t bd = tc::sdesc_sw128(qk_a + 64 * 128 + koff, 16, 1024);
         tc::mma_f16(tmem + COL_D, ad, bd, id, s > 0);
       }
       tc::commit(bar);
     }
-    if (c + 1 < nchunks) prefetch_chunk(sm, q, k, v, g, beta, b, hk, hv, T, Hqk, Hv, c + 1, tid);
 
     // state readout (independent of D1): S^T row -> fp16 operand, then scale the accumulator by gamma
     {
@@ -338,17 +381,17 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
     // (1) diagonal 16x16 blocks: thread (blk, j) solves column j by right-looking substitution
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
-      float x[16];
+      float xs[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = i == j ? 1.f : 0.f;
+      for (int i = 0; i < 16; ++i) xs[i] = i == j ? 1.f : 0.f;
 #pragma unroll
       for (int kk = 0; kk < 15; ++kk) {
-        const float xk = x[kk];
+        const float xk = xs[kk];
 #pragma unroll
-        for (int i = kk + 1; i < 16; ++i) x[i] -= sA[(o + i) * LDF + o + kk] * xk;
+        for (int i = kk + 1; i < 16; ++i) xs[i] -= sA[(o + i) * LDF + o + kk] * xk;
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) sT[(o + i) * LDF + o + j] = x[i];
+      for (int i = 0; i < 16; ++i) sT[(o + i) * LDF + o + j] = xs[i];
     }
     __syncthreads();
     // (2) 16 -> 32: X = A_{r,c} T_{c,c} (kept in A's unused upper block), T_{r,c} = -T_{r,r} X
@@ -424,10 +467,10 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
       constexpr uint32_t id = tc::idesc_f16(128, 64, true, false);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 2048, T64_BLK, 1024);
+        const uint64_t av = tc::sdesc_sw128(v_a + s * 2048, T64_BLK, 1024);
         const uint64_t b1 = tc::sdesc_sw128(sbase + OFF_T1 + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_U, av, b1, id, s > 0);
-        const uint64_t ak = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
+        const uint64_t ak = tc::sdesc_sw128(qk_a + 64 * 128 + s * 2048, QK_BLK, 1024);
         const uint64_t b2 = tc::sdesc_sw128(sbase + OFF_T2 + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_D, ak, b2, id, s > 0);
       }
@@ -456,10 +499,16 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         const uint64_t as = tc::sdesc_sw128(sbase + OFF_ST + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
         const uint64_t bw = tc::sdesc_sw128(sbase + OFF_W + (s >> 2) * T64_BLK + (s & 3) * 32, 16, 1024);
         tc::mma_f16(tmem + COL_U, as, bw, idn, 1);
-        const uint64_t bq = tc::sdesc_sw128(sbase + OFF_QK + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
+        const uint64_t bq = tc::sdesc_sw128(qk_a + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
         tc::mma_f16(tmem + COL_O1, as, bq, id, s > 0);
       }
       tc::commit(bar);
+    }
+    // while the tensor core works: land and rewrite the next chunk's tiles
+    if (c + 1 < nchunks) {
+      const int nv1 = min(C, T - (c + 1) * C);
+      if (wait_tiles(c + 1) && (always_convert || nv1 < C))
+        convert_tiles<TIn>(sm + OFF_QK0 + (x ^ 1) * QK_BYTES, sm + OFF_V0 + (x ^ 1) * V_BYTES, nv1, l2norm, tid);
     }
     if (!sync_mma()) break;
 
@@ -473,7 +522,7 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
         float y[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) y[e] = r32[cb * 8 + e] * sDec[half * 32 + cb * 8 + e];
-        *reinterpret_cast<uint4*>(sm + OFF_V + sw(row, half * 4 + cb)) = pack8_f16(r32 + cb * 8);
+        *reinterpret_cast<uint4*>(sm + v_off + sw(row, half * 4 + cb)) = pack8_f16(r32 + cb * 8);
         *reinterpret_cast<uint4*>(sm + OFF_VD + sw(row, half * 4 + cb)) = pack8_f16(y);
       }
     }
@@ -485,11 +534,11 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
       constexpr uint32_t id128 = tc::idesc_f16(128, 128, false, true);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 32, 16, 1024);
+        const uint64_t av = tc::sdesc_sw128(v_a + s * 32, 16, 1024);
         const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_O2, av, bp, id64, s > 0);
         const uint64_t ad = tc::sdesc_sw128(sbase + OFF_VD + s * 32, 16, 1024);
-        const uint64_t bk = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
+        const uint64_t bk = tc::sdesc_sw128(qk_a + 64 * 128 + s * 2048, QK_BLK, 1024);
         tc::mma_f16(tmem + COL_S, ad, bk, id128, 1);
       }
       tc::commit(bar);
@@ -503,8 +552,8 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
       tc::tmem_ld32(lane_addr + COL_O2 + half * 32, o2);
       tc::tmem_wait_ld();
       if constexpr (sizeof(TOut) == 2) {
-        // stage [token][d_v] in the V region, then write whole 256-byte rows
-        TOut* ost = reinterpret_cast<TOut*>(sm + OFF_V);
+        // stage [token][d_v] in this chunk's V region, then write whole 256-byte rows
+        TOut* ost = reinterpret_cast<TOut*>(sm + v_off);
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const int tt = half * 32 + t;
@@ -516,7 +565,7 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
           const int r = (tid >> 4) + it * 16, ch = tid & 15;
           if (r < nvalid)
             *reinterpret_cast<uint4*>(out + (((size_t)b * T + t0 + r) * Hv + hv) * D + ch * 8) =
-                *reinterpret_cast<const uint4*>(sm + OFF_V + r * 256 + ch * 16);
+                *reinterpret_cast<const uint4*>(sm + v_off + r * 256 + ch * 16);
         }
       } else {
 #pragma unroll
@@ -533,6 +582,8 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   }
 
   cp_async_wait<0>();
+  // a stopped CTA still lets the tiles it requested land before it leaves (bounded)
+  if (pending_chunk >= 0) tc::mbar_wait(tb0 + 8u * (pending_chunk & 1), (uint32_t)((pending_chunk >> 1) & 1));
   // ---- final state ----
   if (!abort_flag) {
     float buf[32];
@@ -550,13 +601,47 @@ gdn_chunked_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const T
   if (warp == 0) tc::tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ------------------------------------------------------------ tensor maps ----
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// [d = 128, heads, tokens] view of a [B*T, heads, 128] 2-byte tensor; box 64 x 1 x 64, 128-byte swizzle.
+int encode_rows_map(CUtensorMap* m, const void* base, int heads, long long tokens) {
+  auto enc = tensor_map_encoder();
+  ANEMLL_REQUIRE(enc, ANEMLL_EUNSUPPORTED, "gdn_chunked_prefill: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)tokens};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)C};
+  const cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  ANEMLL_REQUIRE(r == CUDA_SUCCESS, ANEMLL_EINVAL, "gdn_chunked_prefill: tensor map encoding failed (%d)", (int)r);
+  return ANEMLL_OK;
+}
+
 template <typename TIn, typename TOut>
 int launch_chunked(const void* q, const void* k, const void* v, const float* g, const float* beta, float* state,
                    void* out, int B, int T, int Hqk, int Hv, float scale, int l2norm, cudaStream_t st) {
+  TileMaps maps;
+  const long long tokens = (long long)B * T;
+  int rc = encode_rows_map(&maps.q, q, Hqk, tokens);
+  if (!rc) rc = encode_rows_map(&maps.k, k, Hqk, tokens);
+  if (!rc) rc = encode_rows_map(&maps.v, v, Hv, tokens);
+  if (rc) return rc;
   auto kern = gdn_chunked_kernel<TIn, TOut>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  kern<<<B * Hv, NT, SMEM_BYTES, st>>>((const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T,
-                                       Hqk, Hv, scale, l2norm);
+  kern<<<B * Hv, NT, SMEM_BYTES, st>>>(maps, g, beta, state, (TOut*)out, T, Hqk, Hv, scale, l2norm);
   return launch_status("gdn_chunked_prefill");
 }
 
