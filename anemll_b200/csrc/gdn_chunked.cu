@@ -11,8 +11,8 @@
 //   A    = strict_lower(diag(beta) K K^T * Gam), T = (I + A)^-1   (CUDA cores, fp32, blockwise)
 //   U^T  = V^T (T diag(beta))^T              (tcgen05, M=128 N=64 K=64)
 //   W^T  = K^T (T diag(beta e^G))^T          (tcgen05, M=128 N=64 K=64)
-//   Vn^T = U^T - S^T W^T                     (tcgen05, A negated, accumulates on U)
-//   O1^T = S^T Q^T,  O2^T = Vn^T P^T         (tcgen05; O = diag(e^G) O1 + O2 at readout)
+//   [X1|X2] = -S^T [W;Q]^T                   (tcgen05, one N=128 product, A negated)
+//   Vn^T = U^T + X1,  O2^T = Vn^T P^T        (O = diag(e^G) (-X2) + O2 at readout)
 //   S^T  = e^{G_c} S^T + (diag(e^{G_c - G}) Vn)^T K   (e^{G_c} applied in TMEM, then tcgen05)
 //
 // Every product is arranged so that M = 128 (d_v or d_k on TMEM lanes).  All
@@ -50,27 +50,30 @@ constexpr int C = 64;
 constexpr int D = 128;
 constexpr int NT = 256;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_S = 0, COL_O1 = 128, COL_U = 192, COL_O2 = 256, COL_D = 320;
+constexpr uint32_t COL_S = 0, COL_U = 128, COL_X = 192, COL_O2 = 320, COL_D = 384;  // X: [X1 | X2]
 
 // shared memory map (bytes from a 1024-byte aligned base); lifetimes in a chunk:
-//   QK[x] (TMA)   [prep .. S update]     V[x] (TMA): V [.. U/W] -> Vn^T [Vn .. S update] -> O staging
-//   VD: (dec Vn)^T [Vn .. S update]      R1: A fp32 [P/A .. T] -> T1,T2 [.. U/W] -> W [.. V'/O1]
-constexpr int QK_BLK = 128 * 128;  // one 64-column block of a 128-row tile
-constexpr int T64_BLK = 64 * 128;  // one 64-column block of a 64-row tile
-constexpr int QK_BYTES = 2 * QK_BLK, V_BYTES = 2 * T64_BLK;
+//   WQK[x]: rows 0-63 W (written per chunk), 64-127 Q and 128-191 K (TMA) [prep .. S update]
+//   V[x] (TMA): V [.. U/W] -> Vn^T [Vn .. S update] -> O staging
+//   VD: (dec Vn)^T [Vn .. S update]      R1: A fp32 [P/A .. T] -> T1,T2 [.. U/W]
+constexpr int QK_BLK = 128 * 128;   // one 64-column block of a 128-row tile (S^T)
+constexpr int WQK_BLK = 192 * 128;  // one 64-column block of the [W;Q;K] tile
+constexpr int T64_BLK = 64 * 128;   // one 64-column block of a 64-row tile
+constexpr int WQK_BYTES = 2 * WQK_BLK, V_BYTES = 2 * T64_BLK;
+constexpr int ROW_Q = 64, ROW_K = 128;
 constexpr int LDF = 68;  // fp32 row pitch (floats) of A and T
-constexpr int OFF_QK0 = 0;
-constexpr int OFF_V0 = OFF_QK0 + 2 * QK_BYTES;
+constexpr int OFF_WQK0 = 0;
+constexpr int OFF_V0 = OFF_WQK0 + 2 * WQK_BYTES;
 constexpr int OFF_VD = OFF_V0 + 2 * V_BYTES;
 constexpr int OFF_P = OFF_VD + 2 * T64_BLK;
 constexpr int OFF_ST = OFF_P + T64_BLK;
 constexpr int OFF_R1 = OFF_ST + 2 * QK_BLK;
-constexpr int OFF_T1 = OFF_R1, OFF_T2 = OFF_R1 + T64_BLK, OFF_W = OFF_R1;
+constexpr int OFF_T1 = OFF_R1, OFF_T2 = OFF_R1 + T64_BLK;
 constexpr int OFF_T = OFF_R1 + 64 * LDF * 4;
 constexpr int OFF_GB = OFF_T + 64 * LDF * 4;    // raw g, beta per buffer: [2][128] floats
 constexpr int OFF_MISC = OFF_GB + 2 * 128 * 4;  // G, beta, e^G, dec [64] each, gamma
 constexpr int SMEM_BYTES = OFF_MISC + 4 * 64 * 4 + 16 + 1024;
-constexpr uint32_t TILE_TX_BYTES = QK_BYTES + V_BYTES;  // bytes one chunk's six boxes deliver
+constexpr uint32_t TILE_TX_BYTES = 2 * 2 * 64 * 128 + V_BYTES;  // bytes one chunk's six boxes deliver
 static_assert(OFF_R1 % 1024 == 0 && OFF_ST % 1024 == 0, "tile alignment");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
@@ -108,14 +111,14 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 // Rewrite one chunk's tiles in place as fp16: convert from TIn, l2-normalise q
 // and k rows if asked, zero the rows at and past `nvalid`.
 template <typename TIn>
-__device__ __forceinline__ void convert_tiles(uint8_t* qk, uint8_t* vt, int nvalid, int l2norm, int tid) {
+__device__ __forceinline__ void convert_tiles(uint8_t* wqk, uint8_t* vt, int nvalid, int l2norm, int tid) {
   const int ch = tid & 15;
   const int blk = ch >> 3, cb = ch & 7;
 #pragma unroll 1
   for (int it = 0; it < 4; ++it) {
     const int r = (tid >> 4) + it * 16;
-    uint4* pq = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(r, cb));
-    uint4* pk = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(64 + r, cb));
+    uint4* pq = reinterpret_cast<uint4*>(wqk + blk * WQK_BLK + sw(ROW_Q + r, cb));
+    uint4* pk = reinterpret_cast<uint4*>(wqk + blk * WQK_BLK + sw(ROW_K + r, cb));
     uint4* pv = reinterpret_cast<uint4*>(vt + blk * T64_BLK + sw(r, cb));
     float fq[8], fk[8], fv[8];
     if (r < nvalid) {
@@ -185,11 +188,11 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     if (tid == 0) {
       const uint32_t tb = tb0 + 8u * x;
       tc::mbar_arrive_expect_tx(tb, TILE_TX_BYTES);
-      const uint32_t qk = sbase + OFF_QK0 + x * QK_BYTES, vt = sbase + OFF_V0 + x * V_BYTES;
-      tc::tma_load_3d(qk, &maps.q, 0, hk, tok0, tb);
-      tc::tma_load_3d(qk + QK_BLK, &maps.q, 64, hk, tok0, tb);
-      tc::tma_load_3d(qk + 64 * 128, &maps.k, 0, hk, tok0, tb);
-      tc::tma_load_3d(qk + QK_BLK + 64 * 128, &maps.k, 64, hk, tok0, tb);
+      const uint32_t w = sbase + OFF_WQK0 + x * WQK_BYTES, vt = sbase + OFF_V0 + x * V_BYTES;
+      tc::tma_load_3d(w + ROW_Q * 128, &maps.q, 0, hk, tok0, tb);
+      tc::tma_load_3d(w + WQK_BLK + ROW_Q * 128, &maps.q, 64, hk, tok0, tb);
+      tc::tma_load_3d(w + ROW_K * 128, &maps.k, 0, hk, tok0, tb);
+      tc::tma_load_3d(w + WQK_BLK + ROW_K * 128, &maps.k, 64, hk, tok0, tb);
       tc::tma_load_3d(vt, &maps.v, 0, hv, tok0, tb);
       tc::tma_load_3d(vt + T64_BLK, &maps.v, 64, hv, tok0, tb);
     }
@@ -263,14 +266,15 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   };
 
   if (wait_tiles(0) && (always_convert || T < C))
-    convert_tiles<TIn>(sm + OFF_QK0, sm + OFF_V0, min(C, T), l2norm, tid);
+    convert_tiles<TIn>(sm + OFF_WQK0, sm + OFF_V0, min(C, T), l2norm, tid);
 
 #pragma unroll 1
   for (int c = 0; c < nchunks && !abort_flag; ++c) {
     const int x = c & 1;
     const int t0 = c * C;
     const int nvalid = min(C, T - t0);
-    const uint32_t qk_a = sbase + OFF_QK0 + x * QK_BYTES;
+    const uint32_t wqk_a = sbase + OFF_WQK0 + x * WQK_BYTES;
+    const int wqk_off = OFF_WQK0 + x * WQK_BYTES;
     const uint32_t v_a = sbase + OFF_V0 + x * V_BYTES;
     const int v_off = OFF_V0 + x * V_BYTES;
     cp_async_wait<0>();
@@ -311,9 +315,9 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
-        const uint32_t koff = (uint32_t)((s >> 2) * QK_BLK + (s & 3) * 32);
-        const uint64_t ad = tc::sdesc_sw128(qk_a + koff, 16, 1024);
-        const uint64_t bd = tc::sdesc_sw128(qk_a + 64 * 128 + koff, 16, 1024);
+        const uint32_t koff = (uint32_t)((s >> 2) * WQK_BLK + (s & 3) * 32);
+        const uint64_t ad = tc::sdesc_sw128(wqk_a + ROW_Q * 128 + koff, 16, 1024);
+        const uint64_t bd = tc::sdesc_sw128(wqk_a + ROW_K * 128 + koff, 16, 1024);
         tc::mma_f16(tmem + COL_D, ad, bd, id, s > 0);
       }
       tc::commit(bar);
@@ -378,7 +382,13 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     __syncthreads();
 
     // ---------------- T = (I + A)^-1, blockwise ----------------
-    // (1) diagonal 16x16 blocks: thread (blk, j) solves column j by right-looking substitution
+    // (1) diagonal 16x16 blocks: thread (blk, j) solves column j by right-looking substitution;
+    //     the upper blocks T[0:16,16:32] and T[32:48,48:64] that the merges read are zeroed
+    {
+      const int z = tid * 2, sel = z >> 8, w = z & 255;
+      const int zr = (sel ? 32 : 0) + (w >> 4), zc = (sel ? 48 : 16) + (w & 15);
+      *reinterpret_cast<float2*>(sT + zr * LDF + zc) = make_float2(0.f, 0.f);
+    }
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
       float xs[16];
@@ -423,9 +433,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     {
       const int r = tid >> 3, c0 = (tid & 7) * 4;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int k_lo = c0 >= 16 ? 16 : 0;  // T[0:16, 16:32] is the (zero) upper block
-#pragma unroll 4
-      for (int kk = k_lo; kk < 32; ++kk) {
+#pragma unroll 8
+      for (int kk = 0; kk < 32; ++kk) {
         const float a = sA[(32 + r) * LDF + kk];
         const float4 t4 = *reinterpret_cast<const float4*>(sT + kk * LDF + c0);
         acc[0] += a * t4.x; acc[1] += a * t4.y; acc[2] += a * t4.z; acc[3] += a * t4.w;
@@ -433,9 +442,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       *reinterpret_cast<float4*>(sA + r * LDF + 32 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
       __syncthreads();
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-      const int k_hi = r < 16 ? 16 : 32;  // T[32:48, 48:64] is the (zero) upper block
-#pragma unroll 4
-      for (int kk = 0; kk < k_hi; ++kk) {
+#pragma unroll 8
+      for (int kk = 0; kk < 32; ++kk) {
         const float t = sT[(32 + r) * LDF + 32 + kk];
         const float4 y4 = *reinterpret_cast<const float4*>(sA + kk * LDF + 32 + c0);
         acc[0] += t * y4.x; acc[1] += t * y4.y; acc[2] += t * y4.z; acc[3] += t * y4.w;
@@ -449,12 +457,19 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 #pragma unroll
       for (int cb = 0; cb < 2; ++cb) {
         float t1[8], t2[8];
+        const int c8 = (cq + cb) * 8;
+        const float4 ta = *reinterpret_cast<const float4*>(sT + r * LDF + c8);
+        const float4 tb = *reinterpret_cast<const float4*>(sT + r * LDF + c8 + 4);
+        const float4 ba = *reinterpret_cast<const float4*>(sBeta + c8), bb = *reinterpret_cast<const float4*>(sBeta + c8 + 4);
+        const float4 ea = *reinterpret_cast<const float4*>(sEG + c8), eb = *reinterpret_cast<const float4*>(sEG + c8 + 4);
+        const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+        const float bv[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
+        const float ev[8] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const int cc = (cq + cb) * 8 + e;
-          const float t = cc <= r ? sT[r * LDF + cc] : 0.f;
-          t1[e] = t * sBeta[cc];
-          t2[e] = t1[e] * sEG[cc];
+          const float t = c8 + e <= r ? tv[e] : 0.f;
+          t1[e] = t * bv[e];
+          t2[e] = t1[e] * ev[e];
         }
         *reinterpret_cast<uint4*>(sm + OFF_T1 + sw(r, cq + cb)) = pack8_f16(t1);
         *reinterpret_cast<uint4*>(sm + OFF_T2 + sw(r, cq + cb)) = pack8_f16(t2);
@@ -470,7 +485,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         const uint64_t av = tc::sdesc_sw128(v_a + s * 2048, T64_BLK, 1024);
         const uint64_t b1 = tc::sdesc_sw128(sbase + OFF_T1 + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_U, av, b1, id, s > 0);
-        const uint64_t ak = tc::sdesc_sw128(qk_a + 64 * 128 + s * 2048, QK_BLK, 1024);
+        const uint64_t ak = tc::sdesc_sw128(wqk_a + ROW_K * 128 + s * 2048, WQK_BLK, 1024);
         const uint64_t b2 = tc::sdesc_sw128(sbase + OFF_T2 + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_D, ak, b2, id, s > 0);
       }
@@ -480,7 +495,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- W readout: lane = d_k index, 32 token columns per thread ----------------
     {
-      uint8_t* wb = sm + OFF_W + (row >> 6) * T64_BLK;
+      uint8_t* wb = sm + wqk_off + (row >> 6) * WQK_BLK;  // rows 0-63 of [W;Q;K]
       float r32[32];
       tc::tmem_ld32(lane_addr + COL_D + half * 32, r32);
       tc::tmem_wait_ld();
@@ -490,17 +505,14 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     }
     sync_smem_for_mma();
 
-    // ---------------- Vn^T = U^T - S^T W^T ; O1^T = S^T Q^T ----------------
+    // ---------------- [X1 | X2] = -S^T [W;Q]^T : one N=128 product ----------------
     if (tid == 0) {
-      constexpr uint32_t idn = tc::idesc_f16(128, 64, false, false, true);
-      constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
+      constexpr uint32_t idn = tc::idesc_f16(128, 128, false, false, true);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint64_t as = tc::sdesc_sw128(sbase + OFF_ST + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
-        const uint64_t bw = tc::sdesc_sw128(sbase + OFF_W + (s >> 2) * T64_BLK + (s & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_U, as, bw, idn, 1);
-        const uint64_t bq = tc::sdesc_sw128(qk_a + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_O1, as, bq, id, s > 0);
+        const uint64_t bwq = tc::sdesc_sw128(wqk_a + (s >> 2) * WQK_BLK + (s & 3) * 32, 16, 1024);
+        tc::mma_f16(tmem + COL_X, as, bwq, idn, s > 0);
       }
       tc::commit(bar);
     }
@@ -508,20 +520,26 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     if (c + 1 < nchunks) {
       const int nv1 = min(C, T - (c + 1) * C);
       if (wait_tiles(c + 1) && (always_convert || nv1 < C))
-        convert_tiles<TIn>(sm + OFF_QK0 + (x ^ 1) * QK_BYTES, sm + OFF_V0 + (x ^ 1) * V_BYTES, nv1, l2norm, tid);
+        convert_tiles<TIn>(sm + OFF_WQK0 + (x ^ 1) * WQK_BYTES, sm + OFF_V0 + (x ^ 1) * V_BYTES, nv1, l2norm, tid);
     }
     if (!sync_mma()) break;
 
     // ---------------- Vn readout: lane = d_v index, 32 token columns per thread ----------------
     {
-      float r32[32];
+      float r32[32], x32[32];
       tc::tmem_ld32(lane_addr + COL_U + half * 32, r32);
+      tc::tmem_ld32(lane_addr + COL_X + half * 32, x32);
       tc::tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; ++e) r32[e] += x32[e];
 #pragma unroll
       for (int cb = 0; cb < 4; ++cb) {
         float y[8];
+        const float4 d0 = *reinterpret_cast<const float4*>(sDec + half * 32 + cb * 8);
+        const float4 d1 = *reinterpret_cast<const float4*>(sDec + half * 32 + cb * 8 + 4);
+        const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) y[e] = r32[cb * 8 + e] * sDec[half * 32 + cb * 8 + e];
+        for (int e = 0; e < 8; ++e) y[e] = r32[cb * 8 + e] * dd[e];
         *reinterpret_cast<uint4*>(sm + v_off + sw(row, half * 4 + cb)) = pack8_f16(r32 + cb * 8);
         *reinterpret_cast<uint4*>(sm + OFF_VD + sw(row, half * 4 + cb)) = pack8_f16(y);
       }
@@ -538,7 +556,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 32, 16, 1024);
         tc::mma_f16(tmem + COL_O2, av, bp, id64, s > 0);
         const uint64_t ad = tc::sdesc_sw128(sbase + OFF_VD + s * 32, 16, 1024);
-        const uint64_t bk = tc::sdesc_sw128(qk_a + 64 * 128 + s * 2048, QK_BLK, 1024);
+        const uint64_t bk = tc::sdesc_sw128(wqk_a + ROW_K * 128 + s * 2048, WQK_BLK, 1024);
         tc::mma_f16(tmem + COL_S, ad, bk, id128, 1);
       }
       tc::commit(bar);
@@ -548,7 +566,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     // ---------------- O = (e^G O1 + O2) * scale -> global ----------------
     {
       float o1[32], o2[32];
-      tc::tmem_ld32(lane_addr + COL_O1 + half * 32, o1);
+      tc::tmem_ld32(lane_addr + COL_X + 64 + half * 32, o1);
       tc::tmem_ld32(lane_addr + COL_O2 + half * 32, o2);
       tc::tmem_wait_ld();
       if constexpr (sizeof(TOut) == 2) {
@@ -557,7 +575,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const int tt = half * 32 + t;
-          ost[tt * D + row] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
+          ost[tt * D + row] = from_f32<TOut>((o2[t] - sEG[tt] * o1[t]) * scale);
         }
         __syncthreads();
 #pragma unroll
@@ -572,7 +590,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         for (int t = 0; t < 32; ++t) {
           const int tt = half * 32 + t;
           if (tt < nvalid)
-            out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + row] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
+            out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + row] = from_f32<TOut>((o2[t] - sEG[tt] * o1[t]) * scale);
         }
       }
     }
