@@ -337,6 +337,115 @@ def bench_gdn_prefill(args, ws, rank, local):
     }
 
 
+def bench_kv_attention(args, ws, rank, local):
+    """Fixed-shape KV-cache attention, H_q=16, H_kv=2, hd=256, ctx 4096, fp16.
+
+    One step = one pass of the layer's attention over the workload: 31 prefill
+    chunks of 64 tokens at positions 2048..4031 then 64 decode steps at
+    4032..4095 (cache write fused in every call).  `--window 512` selects the
+    sliding-window variant.  Ranks beyond the two kv heads are replicas."""
+    from anemll_b200 import attention, inputs, shard
+    dev = torch.device("cuda", local)
+    d = inputs.kv_attention()
+    kv0, nkv = shard.kv_head_shard(ws, rank, 2)
+    hq0, nq = kv0 * 8, nkv * 8
+    cache = d["cache"][:, kv0:kv0 + nkv].contiguous().to(dev)
+    q = d["q"][:, hq0:hq0 + nq].contiguous().to(dev)
+    k = d["k"][:, kv0:kv0 + nkv].contiguous().to(dev)
+    v = d["v"][:, kv0:kv0 + nkv].contiguous().to(dev)
+    gate = d["gate"].view(1, -1, 16, 256)[:, :, hq0:hq0 + nq].reshape(1, -1, nq * 256).contiguous().to(dev)
+    K, V = cache[0], cache[1]
+    pos0, pos1 = d["prefill_from"], d["prefill_to"]
+    calls = []
+    for p in range(pos0, pos1, 64):
+        j = p - pos0
+        calls.append((p, q[:, :, j:j + 64].contiguous(), k[:, :, j:j + 64].contiguous(), v[:, :, j:j + 64].contiguous(),
+                      gate[:, j:j + 64].contiguous()))
+    dec = []
+    for p in range(pos1, 4096):
+        j = p - pos0
+        dec.append((p, q[:, :, j:j + 1].contiguous(), k[:, :, j:j + 1].contiguous(), v[:, :, j:j + 1].contiguous(),
+                    gate[:, j:j + 1].contiguous()))
+    outs = [torch.empty(1, c[1].shape[2], nq * 256, dtype=torch.half, device=dev) for c in calls + dec]
+    ws_buf = torch.empty(attention.kv_attention_workspace_size(1, 64, nq, nkv, 256, 4096), dtype=torch.uint8,
+                         device=dev)
+    window = args.window
+
+    def run(seq):
+        for (p, qq, kk, vv, gg), o in seq:
+            attention.kv_attention(qq, K, V, p, k_new=kk, v_new=vv, gate=gg, window=window, out=o, workspace=ws_buf)
+
+    pre = list(zip(calls, outs[:len(calls)]))
+    dcd = list(zip(dec, outs[len(calls):]))
+    for _ in range(args.warmup):
+        run(pre)
+        run(dcd)
+    torch.cuda.synchronize(dev)
+    # the 31 prefill calls and the 64 decode calls replay as CUDA graphs (as a serving loop would)
+    g_pre, g_dec = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_pre):
+        run(pre)
+    with torch.cuda.graph(g_dec):
+        run(dcd)
+    g_pre.replay()
+    g_dec.replay()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    stream = torch.cuda.current_stream(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    pre_ms = dec_ms = 0.0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            e[0].record(stream)
+            g_pre.replay()
+            e[1].record(stream)
+            g_dec.replay()
+            e[2].record(stream)
+            torch.cuda.synchronize(dev)
+            pre_ms += e[0].elapsed_time(e[1])
+            dec_ms += e[1].elapsed_time(e[2])
+    barrier(ws)
+    tot_ms = max_over_ranks(pre_ms + dec_ms, ws, dev)
+    pre_ms_max = max_over_ranks(pre_ms, ws, dev)
+    dec_ms_max = max_over_ranks(dec_ms, ws, dev)
+    # algorithmic work: 4*hd*H_q FLOP per visible (query, key) pair in prefill; K+V bytes of visible keys in decode
+    vis_pre = sum(min(p + i + 1, window) if window else p + i + 1 for p in range(pos0, pos1, 64) for i in range(64))
+    flop_pre = 4 * 256 * nq * vis_pre
+    bytes_dec = sum((min(p + 1, window) if window else p + 1) * nkv * 256 * 2 * 2 + 3 * nq * 256 * 2 + 2 * nkv * 256 * 2
+                    for p in range(pos1, 4096))
+    pk, how = peaks()
+    tflops = flop_pre / (pre_ms / args.steps / 1e3) / 1e12
+    gbs = bytes_dec / (dec_ms / args.steps / 1e3) / 1e9
+    n_tok = (pos1 - pos0) + (4096 - pos1)
+    return {
+        "metric": "kv_attention_tokens_per_s",
+        "value": n_tok * args.steps / (tot_ms / 1e3) * (1 if ws <= 2 else ws / 2),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong" if ws <= 2 else "strong up to 2 (kv heads), replicas beyond",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded; cache prefilled N(0,1) at 0..2047)",
+        "config": {"workload": "kv_cache_attention", "H_q": 16, "H_kv": 2, "head_dim": 256, "ctx": 4096,
+                   "prefill_chunks": len(calls), "chunk": 64, "decode_steps": len(dec), "window": window,
+                   "l2": "K/V of one layer (8 MiB) stay L2-resident across calls, as in serving",
+                   "parallelism": f"{ws} ranks, kv heads {kv0}..{kv0 + nkv - 1}"},
+        "prefill_us_per_chunk": pre_ms_max / args.steps / len(calls) * 1e3,
+        "decode_us_per_step": dec_ms_max / args.steps / len(dec) * 1e3,
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk["bf16_tflops"], "peak_source": how,
+                     "algorithmic_flop_per_pass": flop_pre, "traffic": None,
+                     "decode": {"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                                "algorithmic_bytes_per_pass": bytes_dec}},
+        "gpu_launches": args.steps * (len(calls) + len(dec)) * 2,
+        "clocks": clk.summary(),
+    }
+
+
 def traffic_from_profiles(name):
     """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
@@ -394,7 +503,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode", "gdn_prefill"])
+    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode", "gdn_prefill", "kv_attention"])
+    ap.add_argument("--window", type=int, default=0, help="kv_attention: sliding window (0 = causal)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
     ap.add_argument("--prefill-len", type=int, default=PREFILL_T, help="gdn_prefill: tokens per sequence")
@@ -405,7 +515,9 @@ def main():
         if args.impl == "reference":
             res = reference_arm(args, ws, rank)
         else:
-            if args.config == "gdn_prefill":
+            if args.config == "kv_attention":
+                res = bench_kv_attention(args, ws, rank, local)
+            elif args.config == "gdn_prefill":
                 res = bench_gdn_prefill(args, ws, rank, local)
                 res["roofline"]["traffic"] = traffic_from_profiles("gdn_chunked_prefill")
             else:
