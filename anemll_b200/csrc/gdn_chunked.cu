@@ -239,7 +239,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   };
   auto sync_mma = [&]() -> bool {
     // every thread: wait until the MMAs committed so far have completed
-    const bool ok = tc::mbar_wait(bar, phase);
+    const bool ok = __syncthreads_and(tc::mbar_wait(bar, phase));  // block-uniform outcome
     phase ^= 1u;
     if (!ok) fail();
     tc::fence_after();
@@ -257,7 +257,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     const int t0 = c * C;
     const int nvalid = min(C, T - t0);
     // ---------------- tiles and gates of this chunk ----------------
-    if (!tc::mbar_wait(tb, (uint32_t)(c & 1))) {
+    if (!__syncthreads_and(tc::mbar_wait(tb, (uint32_t)(c & 1)))) {
       fail();
       break;
     }

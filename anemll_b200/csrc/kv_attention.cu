@@ -17,8 +17,15 @@
 // Reference semantics: anemll/models/qwen_model.py forward_prefill 509-546,
 // forward_regular 469-507, cache writes 669-675 / 733-745; sigmoid gate of
 // transformers 5.5.0 modeling_qwen3_5.py:689.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
 #include "common.cuh"
 #include "mma_sync.cuh"
+#include "tcgen05.cuh"
 
 namespace anemll {
 namespace {
@@ -408,6 +415,399 @@ size_t workspace_bytes_for(int n_splits, int B, int S, int Hq, int Hkv, int hd) 
   return (size_t)B * Hkv * n_splits * R * (hd + 2) * sizeof(float);
 }
 
+
+// ---------------------------------------------------------------------------
+// tcgen05 path for prefill chunks (G = H_q/H_kv = 8 query heads per kv head,
+// head_dim 128 or 256, S >= 16).  A CTA owns a 128-row query tile (8 heads x
+// 16 tokens, rows head-major: row = head * 16 + token) and one key split; K/V
+// blocks of 64 keys arrive by TMA (double-buffered) straight from the cache.
+// Per block: S = Q K^T into TMEM (tcgen05, M=128 N=64 K=hd), an online softmax
+// on CUDA cores (thread = row) writes fp16 P to shared memory, O += P V on the
+// tensor core into TMEM (M=128 N=hd K=64).  The running max is kept stale until
+// it grows by more than 2^8, so O in TMEM is rescaled only then.  The new cache
+// rows are stored by a small copy kernel launched just before.  Partials use the
+// same workspace format and combine kernel as the mma.sync path.
+constexpr int TC_KB = 64;  // keys per block
+
+struct KvTcMaps {
+  CUtensorMap q, k, v;
+};
+
+__device__ int g_kv_tc_error = 0;
+
+template <typename T>
+__global__ void kv_write_kernel(KvParams p, int HD) {
+  // one 16-byte chunk per thread: [b][kvh][s][hd/8] for K and V
+  const int per = HD / 8;
+  const long long n = (long long)p.B * p.Hkv * p.S * per;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < 2 * n; i += (long long)gridDim.x * blockDim.x) {
+    const int which = i >= n;
+    const long long e = which ? i - n : i;
+    const int c = (int)(e % per);
+    const long long rs = e / per;
+    const int s = (int)(rs % p.S);
+    const int bh = (int)(rs / p.S);
+    const int b = bh / p.Hkv, kvh = bh % p.Hkv;
+    const T* src = reinterpret_cast<const T*>(which ? p.v_new : p.k_new) + ((long long)bh * p.S + s) * HD + c * 8;
+    T* dst = reinterpret_cast<T*>(which ? p.vc : p.kc) + (long long)b * p.bs + (long long)kvh * p.hs +
+             (long long)(p.pos + s) * HD + c * 8;
+    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+  }
+}
+
+__device__ __forceinline__ uint32_t swz128(int r, int ch) { return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)); }
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(128, 1)
+kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
+  constexpr int NKB = HD / 64;                 // 64-element column blocks of a row
+  constexpr int Q_BLK = 128 * 128;             // [128 rows][128 B]
+  constexpr int KV_BLK = TC_KB * 128;          // [64 keys][128 B]
+  constexpr int OFF_Q = 0;
+  constexpr int OFF_K = OFF_Q + NKB * Q_BLK;   // [2 buffers][NKB blocks]
+  constexpr int OFF_V = OFF_K + 2 * NKB * KV_BLK;
+  constexpr int OFF_P = OFF_V + 2 * NKB * KV_BLK;
+  constexpr uint32_t COL_SB = 0, COL_O = 256;  // S: two 64-column buffers; O: HD columns
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t mbar, qbar, kvbar[2];
+  __shared__ uint32_t tmem_slot;
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int G = p.Hq / p.Hkv;  // == 8
+  const int bh = blockIdx.z, b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  const int k_begin = p.key_lo + split * p.ks;
+  const int k_end = min(p.key_hi, k_begin + p.ks);
+  const int nblk = k_end > k_begin ? (k_end - k_begin + TC_KB - 1) / TC_KB : 0;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const uint32_t bar = tc::smem_u32(&mbar), qb = tc::smem_u32(&qbar), kvb0 = tc::smem_u32(&kvbar[0]);
+
+  // this thread's row: head g, token s
+  const int g = tid >> 4, s = tile * 16 + (tid & 15);
+  const bool row_valid = s < p.S;
+  const int qpos = p.pos + s;
+  int lo = 0;
+  if (p.window > 0) lo = p.aligned ? max(0, min(p.pos + p.S, p.ctx) - p.window) : qpos - p.window + 1;
+
+  auto issue_kv = [&](int j) {
+    const int buf = j & 1;
+    const uint32_t kb = kvb0 + 8u * buf;
+    tc::mbar_arrive_expect_tx(kb, 2u * NKB * KV_BLK);
+    const int key0 = k_begin + j * TC_KB;
+#pragma unroll
+    for (int c = 0; c < NKB; ++c) {
+      const uint32_t dk = sbase + OFF_K + (buf * NKB + c) * KV_BLK;
+      const uint32_t dv = sbase + OFF_V + (buf * NKB + c) * KV_BLK;
+      if (p.B > 1) {
+        tc::tma_load_4d(dk, &maps.k, c * 64, key0, kvh, b, kb);
+        tc::tma_load_4d(dv, &maps.v, c * 64, key0, kvh, b, kb);
+      } else {
+        tc::tma_load_3d(dk, &maps.k, c * 64, key0, kvh, kb);
+        tc::tma_load_3d(dv, &maps.v, c * 64, key0, kvh, kb);
+      }
+    }
+  };
+
+  if (tid == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&qbar, 1);
+    tc::mbar_init(&kvbar[0], 1);
+    tc::mbar_init(&kvbar[1], 1);
+    tc::fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  if (tid == 0) {
+    tc::mbar_arrive_expect_tx(qb, (uint32_t)(NKB * Q_BLK));
+#pragma unroll
+    for (int c = 0; c < NKB; ++c)
+      tc::tma_load_3d(sbase + OFF_Q + c * Q_BLK, &maps.q, c * 64, tile * 16, b * p.Hq + kvh * G, qb);
+    if (nblk > 0) issue_kv(0);
+  }
+  bool ok = __syncthreads_and(tc::mbar_wait(qb, 0));
+  uint32_t phase = 0;
+  float m_run = -INFINITY, l_run = 0.f;
+  int pending = nblk > 0 ? 0 : -1;  // K/V block requested and not yet waited for
+
+#pragma unroll 1
+  for (int j = 0; j < nblk && ok; ++j) {
+    const int buf = j & 1;
+    if (tid == 0 && j + 1 < nblk) issue_kv(j + 1);  // the other buffer was released by block j-1
+    ok = __syncthreads_and(tc::mbar_wait(kvb0 + 8u * buf, (uint32_t)((j >> 1) & 1)));  // block-uniform
+    if (!ok) break;
+    pending = j + 1 < nblk ? j + 1 : -1;
+    tc::fence_after();
+    // S = Q K^T
+    if (tid == 0) {
+      constexpr uint32_t id = tc::idesc_f16(128, 64, false, false, false, std::is_same<T, __nv_bfloat16>::value);
+#pragma unroll
+      for (int st = 0; st < HD / 16; ++st) {
+        const uint64_t ad = tc::sdesc_sw128(sbase + OFF_Q + (st >> 2) * Q_BLK + (st & 3) * 32, 16, 1024);
+        const uint64_t bd =
+            tc::sdesc_sw128(sbase + OFF_K + (buf * NKB + (st >> 2)) * KV_BLK + (st & 3) * 32, 16, 1024);
+        tc::mma_f16(tmem + COL_SB + buf * 64, ad, bd, id, st > 0);
+      }
+      tc::commit(bar);
+    }
+    ok = __syncthreads_and(tc::mbar_wait(bar, phase));
+    phase ^= 1u;
+    if (!ok) break;
+    tc::fence_after();
+    // online softmax (base 2) of this row's 64 scores
+    float x[64];
+    tc::tmem_ld32(lane_addr + COL_SB + buf * 64, x);
+    tc::tmem_ld32(lane_addr + COL_SB + buf * 64 + 32, x + 32);
+    tc::tmem_wait_ld();
+    const int key0 = k_begin + j * TC_KB;
+    float mb = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+      const int kj = key0 + e;
+      float v = x[e] * p.scale_log2;
+      bool vis = row_valid && kj < k_end;
+      if (p.mask) {
+        if (vis) {
+          const long long mi = (long long)s * p.mask_ld + kj;
+          const float mv = p.mask_dtype == ANEMLL_F32 ? reinterpret_cast<const float*>(p.mask)[mi]
+                         : p.mask_dtype == ANEMLL_F16 ? __half2float(reinterpret_cast<const __half*>(p.mask)[mi])
+                         : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.mask)[mi]);
+          v += mv * 1.4426950408889634f;
+          vis = v != -INFINITY;
+        }
+      } else {
+        vis = vis && kj <= qpos && kj >= lo;
+      }
+      x[e] = vis ? v : -INFINITY;
+      mb = fmaxf(mb, x[e]);
+    }
+    float alpha = 1.f;
+    bool rescale = false;
+    if (mb > m_run + 8.f) {  // also true when m_run is still -inf
+      if (m_run != -INFINITY) {
+        alpha = exp2f(m_run - mb);
+        rescale = true;
+      }
+      m_run = mb;
+    }
+    const float base = m_run == -INFINITY ? 0.f : m_run;
+    float ls = 0.f;
+#pragma unroll
+    for (int cb = 0; cb < 8; ++cb) {
+      float p8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        p8[e] = exp2f(x[cb * 8 + e] - base);
+        ls += p8[e];
+      }
+      uint4 u;
+      T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(p8[e]);
+      *reinterpret_cast<uint4*>(sm + OFF_P + swz128(tid, cb)) = u;
+    }
+    l_run = l_run * alpha + ls;
+    if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM access; alpha = 1 on other lanes
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] *= alpha;
+        tc::tmem_st32(lane_addr + COL_O + c * 32, o);
+      }
+      tc::tmem_wait_st();
+    }
+    tc::fence_async_smem();
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    // O += P V
+    if (tid == 0) {
+      constexpr uint32_t id = tc::idesc_f16(128, HD, false, true, false, std::is_same<T, __nv_bfloat16>::value);
+#pragma unroll
+      for (int st = 0; st < TC_KB / 16; ++st) {
+        const uint64_t ad = tc::sdesc_sw128(sbase + OFF_P + st * 32, 16, 1024);
+        const uint64_t bd = tc::sdesc_sw128(sbase + OFF_V + buf * NKB * KV_BLK + st * 2048, KV_BLK, 1024);
+        tc::mma_f16(tmem + COL_O, ad, bd, id, j > 0 || st > 0);
+      }
+      tc::commit(bar);
+    }
+    ok = __syncthreads_and(tc::mbar_wait(bar, phase));
+    phase ^= 1u;
+    tc::fence_after();
+  }
+  if (!ok) atomicExch(&g_kv_tc_error, 1);
+  if (pending >= 0 && !ok) tc::mbar_wait(kvb0 + 8u * (pending & 1), (uint32_t)((pending >> 1) & 1));
+
+  // ---- epilogue: this thread's row ----
+  if (ok && row_valid) {
+    const int hq = kvh * G + g;
+    if (p.n_splits == 1) {
+      const float inv = nblk > 0 ? 1.f / l_run : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD;
+      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + s) * p.Hq * HD +
+                                   (long long)hq * HD
+                             : nullptr;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        if (nblk > 0) {
+          tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0.f;
+        }
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          uint4 u;
+          T* h = reinterpret_cast<T*>(&u);
+          uint4 gu;
+          if (grow) gu = *reinterpret_cast<const uint4*>(grow + c * 32 + c8 * 8);
+          const T* gh = reinterpret_cast<const T*>(&gu);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float v = o[c8 * 8 + e] * inv;
+            if (grow) v *= 1.f / (1.f + __expf(-to_f32(gh[e])));
+            h[e] = from_f32<T>(v);
+          }
+          *reinterpret_cast<uint4*>(orow + c * 32 + c8 * 8) = u;
+        }
+      }
+    } else {
+      const int R = p.S * G;
+      const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)s * G + g;
+      float* wo = p.ws_o + row_id * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        if (nblk > 0) {
+          tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0.f;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(wo + c * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+      }
+      p.ws_ml[row_id * 2 + 0] = m_run;
+      p.ws_ml[row_id * 2 + 1] = l_run;
+    }
+  } else if (ok && !row_valid) {
+    // padding rows hold no output
+  }
+  // the other warps' epilogue reads of TMEM must finish before the allocation is released
+  __syncwarp();
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, 512);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 kv_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int kv_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+              const cuuint32_t* box) {
+  auto enc = kv_map_encoder();
+  ANEMLL_REQUIRE(enc, ANEMLL_EUNSUPPORTED, "kv_attention: cuTensorMapEncodeTiled unavailable");
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
+                         box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  ANEMLL_REQUIRE(r == CUDA_SUCCESS, ANEMLL_EINVAL, "kv_attention: tensor map encoding failed (%d)", (int)r);
+  return ANEMLL_OK;
+}
+
+bool tc_eligible(int S, int Hq, int Hkv, int hd, long long bs, long long hs, const void* out, const void* gate) {
+  return Hq / Hkv == 8 && (hd == 128 || hd == 256) && S >= 16 && (hs * 2) % 16 == 0 && (bs * 2) % 16 == 0 &&
+         aligned(out, 16) && (!gate || aligned(gate, 16));
+}
+
+template <typename T, int HD>
+int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
+  // key split for 128-row tiles: about one wave, never more splits than the generic plan (workspace bound)
+  const int row_tiles = (p.S + 15) / 16;
+  const int L = p.key_hi - p.key_lo;
+  const int nblocks = max(1, (L + TC_KB - 1) / TC_KB);
+  const long base = (long)row_tiles * p.B * p.Hkv;
+  int want = (int)((148 + base - 1) / base);
+  want = max(1, min(want, min(nblocks, pl0.n_splits)));
+  const int bps = (nblocks + want - 1) / want;
+  const int ks = bps * TC_KB;
+  const int n_splits = max(1, (L + ks - 1) / ks);
+  KvParams q = p;
+  q.n_splits = n_splits;
+  q.ks = ks;
+  if (n_splits > 1) {
+    const size_t R = (size_t)p.S * (p.Hq / p.Hkv);
+    q.ws_ml = q.ws_o + (size_t)p.B * p.Hkv * n_splits * R * HD;
+  }
+  KvTcMaps maps;
+  {
+    const cuuint64_t dq[3] = {(cuuint64_t)HD, (cuuint64_t)p.S, (cuuint64_t)p.B * p.Hq};
+    const cuuint64_t sq[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.S * HD * 2};
+    const cuuint32_t bq[3] = {64, 16, 8};
+    int rc = kv_encode(&maps.q, p.q, 3, dq, sq, bq);
+    if (rc) return rc;
+    const cuuint32_t bk[4] = {64, (cuuint32_t)TC_KB, 1, 1};
+    if (p.B > 1) {
+      const cuuint64_t dk[4] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv, (cuuint64_t)p.B};
+      const cuuint64_t sk[3] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2, (cuuint64_t)p.bs * 2};
+      rc = kv_encode(&maps.k, p.kc, 4, dk, sk, bk);
+      if (!rc) rc = kv_encode(&maps.v, p.vc, 4, dk, sk, bk);
+    } else {
+      const cuuint64_t dk[3] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv};
+      const cuuint64_t sk[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2};
+      rc = kv_encode(&maps.k, p.kc, 3, dk, sk, bk);
+      if (!rc) rc = kv_encode(&maps.v, p.vc, 3, dk, sk, bk);
+    }
+    if (rc) return rc;
+  }
+  if (p.has_new) {
+    const long long n = 2LL * p.B * p.Hkv * p.S * (HD / 8);
+    const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    kv_write_kernel<T><<<blocks, 256, 0, st>>>(q, HD);
+    const int rc = launch_status("kv_cache_write");
+    if (rc) return rc;
+  }
+  constexpr int NKB = HD / 64;
+  const size_t smem = (size_t)NKB * 128 * 128 + 4 * (size_t)NKB * TC_KB * 128 + 128 * 128 + 1024;
+  auto kern = kv_attn_tc_kernel<T, HD>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(row_tiles, n_splits, p.B * p.Hkv);
+  kern<<<grid, 128, smem, st>>>(maps, q);
+  int rc = launch_status("kv_attention_tc");
+  if (rc) return rc;
+  if (n_splits > 1) {
+    const int R = p.S * (p.Hq / p.Hkv);
+    dim3 g2(R, p.B * p.Hkv);
+    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(q);
+    rc = launch_status("kv_combine");
+  }
+  return rc;
+}
+
 }  // namespace
 }  // namespace anemll
 
@@ -463,11 +863,12 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
   p.ws_ml = p.ws_o ? p.ws_o + (size_t)B * H_kv * pl.n_splits * R * head_dim : nullptr;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
   cudaStream_t st = (cudaStream_t)stream;
+  const bool use_tc = tc_eligible(S, H_q, H_kv, head_dim, cache_batch_stride, cache_head_stride, out, gate);
   return ANEMLL_DISPATCH_HALF(dtype, T, [&] {
     switch (head_dim) {
       case 64: return launch_kv<T, 64>(p, pl, st);
-      case 128: return launch_kv<T, 128>(p, pl, st);
-      default: return launch_kv<T, 256>(p, pl, st);
+      case 128: return use_tc ? launch_kv_tc<T, 128>(p, pl, st) : launch_kv<T, 128>(p, pl, st);
+      default: return use_tc ? launch_kv_tc<T, 256>(p, pl, st) : launch_kv<T, 256>(p, pl, st);
     }
   });
 }

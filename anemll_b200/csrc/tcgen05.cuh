@@ -26,11 +26,13 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
   return d;
 }
 
-// Instruction descriptor, kind::f16 with fp16 A/B and fp32 accumulate.
+// Instruction descriptor, kind::f16 with fp16 (or, with bf16 = true, bf16) A and
+// B — always the same type — and fp32 accumulate.
 // a_mn / b_mn: operand is MN-major (else K-major); a_neg negates A.
-__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn, bool a_neg = false) {
-  return (1u << 4)                       // D format f32
-         | (0u << 7) | (0u << 10)        // A, B format f16
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool a_mn, bool b_mn, bool a_neg = false,
+                                                 bool bf16 = false) {
+  return (1u << 4)                                            // D format f32
+         | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B format: 0 f16, 1 bf16
          | ((a_neg ? 1u : 0u) << 13)
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
          | ((uint32_t)(N >> 3) << 17)
@@ -134,6 +136,15 @@ __device__ __forceinline__ void tma_load_3d(uint32_t smem_dst, const void* tmap,
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::
           "r"(smem_dst),
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t smem_dst, const void* tmap, int x, int y, int z, int w,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];\n" ::"r"(smem_dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
       : "memory");
 }
 
