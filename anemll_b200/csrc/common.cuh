@@ -58,6 +58,14 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// 2^x with the hardware approximation instruction (PTX ex2.approx.ftz.f32;
+// relative error about 2^-22, -inf -> 0): the softmax exponent.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float softplus(float x) {
   // log(1 + e^x), evaluated without overflow (same threshold behaviour as torch's softplus, beta=1, threshold=20)
   return x > 20.0f ? x : log1pf(__expf(x));

@@ -239,7 +239,7 @@ kv_attn_kernel(KvParams p) {
       mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
       const float mnew = fmaxf(m_run[h], mx[h]);
       const float base = mnew == -INFINITY ? 0.f : mnew;
-      alpha[h] = exp2f(m_run[h] - base);
+      alpha[h] = fast_exp2(m_run[h] - base);
       m_run[h] = mnew;
       mx[h] = base;  // reuse as subtraction base
     }
@@ -247,10 +247,10 @@ kv_attn_kernel(KvParams p) {
     uint32_t pf[NB / 16][4];
 #pragma unroll
     for (int n = 0; n < NB / 8; ++n) {
-      const float p0 = exp2f(sc[n][0] - mx[0]);
-      const float p1 = exp2f(sc[n][1] - mx[0]);
-      const float p2 = exp2f(sc[n][2] - mx[1]);
-      const float p3 = exp2f(sc[n][3] - mx[1]);
+      const float p0 = fast_exp2(sc[n][0] - mx[0]);
+      const float p1 = fast_exp2(sc[n][1] - mx[0]);
+      const float p2 = fast_exp2(sc[n][2] - mx[1]);
+      const float p3 = fast_exp2(sc[n][3] - mx[1]);
       rs[0] += p0 + p1;
       rs[1] += p2 + p3;
       const int kk = n >> 1, hi = n & 1;
@@ -336,16 +336,47 @@ kv_combine_kernel(KvParams p) {
   const int bh = blockIdx.y;
   const int b = bh / p.Hkv, kvh = bh % p.Hkv;
   const int d = threadIdx.x;
-  float M = -INFINITY;
-  for (int i = 0; i < p.n_splits; ++i) M = fmaxf(M, p.ws_ml[(((long long)bh * p.n_splits + i) * R + r) * 2]);
+  constexpr int NW = HD / 32;
+  __shared__ float s_w[128];  // n_splits <= 128
+  __shared__ float s_red[NW];
+  // (max, sum) of the splits in parallel: thread d holds splits d, d + HD, ...
+  const int ns = p.n_splits;
+  const long long row0 = (long long)bh * ns * R + r;  // row id of split 0; split i adds i * R
+  float mloc = -INFINITY;
+  for (int i = d; i < ns; i += HD) mloc = fmaxf(mloc, p.ws_ml[(row0 + (long long)i * R) * 2]);
+  float M = warp_max(mloc);
+  if ((d & 31) == 0) s_red[d >> 5] = M;
+  __syncthreads();
+  M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) M = fmaxf(M, s_red[w]);
   const float base = M == -INFINITY ? 0.f : M;
-  float acc = 0.f, L = 0.f;
-  for (int i = 0; i < p.n_splits; ++i) {
-    const long long row_id = ((long long)bh * p.n_splits + i) * R + r;
-    const float w = exp2f(p.ws_ml[row_id * 2] - base);
-    L += w * p.ws_ml[row_id * 2 + 1];
-    acc += w * p.ws_o[row_id * HD + d];
+  float lloc = 0.f;
+  for (int i = d; i < ns; i += HD) {
+    const float wi = fast_exp2(p.ws_ml[(row0 + (long long)i * R) * 2] - base);
+    s_w[i] = wi;
+    lloc += wi * p.ws_ml[(row0 + (long long)i * R) * 2 + 1];
   }
+  __syncthreads();  // every s_w written, every s_red read
+  float Lp = warp_sum(lloc);
+  if ((d & 31) == 0) s_red[d >> 5] = Lp;
+  __syncthreads();
+  float L = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) L += s_red[w];
+  // weighted sum of the partial rows, eight independent loads in flight
+  const float* po = p.ws_o + row0 * HD + d;
+  const long long step = (long long)R * HD;
+  float acc = 0.f;
+  int i = 0;
+  for (; i + 8 <= ns; i += 8) {
+    float v8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v8[u] = po[(long long)(i + u) * step];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc += s_w[i + u] * v8[u];
+  }
+  for (; i < ns; ++i) acc += s_w[i] * po[(long long)i * step];
   const int s = r / G, hq = kvh * G + r % G;
   const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
   float v = acc / L;
@@ -377,7 +408,9 @@ Plan make_plan(int B, int S, int Hq, int Hkv, int ctx, int pos, int window, int 
   const long base = (long)pl.row_tiles * B * Hkv;
   const int want_raw = (int)((2L * 148 + base - 1) / base);
   pl.max_splits = max(1, min(want_raw, min((ctx + NB - 1) / NB, 128)));
-  const int want = max(1, min(want_raw, min(nblocks, 128)));
+  // single-warp CTAs (decode): at most 64 splits, so each CTA reads at least two key blocks
+  const int cap = pl.mw == 1 ? 64 : 128;
+  const int want = max(1, min(want_raw, min(nblocks, cap)));
   const int bps = (nblocks + want - 1) / want;
   pl.ks = bps * NB;
   pl.n_splits = max(1, (L + pl.ks - 1) / pl.ks);
@@ -568,12 +601,21 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     tc::tmem_wait_ld();
     const int key0 = k_begin + j * TC_KB;
     float mb = -INFINITY;
+    if (!p.mask) {
+      // keys visible to this row form one interval of the block: [vlo, vhi]
+      const int vlo = max(lo, key0) - key0;
+      const int vhi = row_valid ? min(qpos, k_end - 1) - key0 : -1;
 #pragma unroll
-    for (int e = 0; e < 64; ++e) {
-      const int kj = key0 + e;
-      float v = x[e] * p.scale_log2;
-      bool vis = row_valid && kj < k_end;
-      if (p.mask) {
+      for (int e = 0; e < 64; ++e) {
+        x[e] = (e >= vlo && e <= vhi) ? x[e] * p.scale_log2 : -INFINITY;
+        mb = fmaxf(mb, x[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 64; ++e) {
+        const int kj = key0 + e;
+        float v = x[e] * p.scale_log2;
+        bool vis = row_valid && kj < k_end;
         if (vis) {
           const long long mi = (long long)s * p.mask_ld + kj;
           const float mv = p.mask_dtype == ANEMLL_F32 ? reinterpret_cast<const float*>(p.mask)[mi]
@@ -582,17 +624,15 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
           v += mv * 1.4426950408889634f;
           vis = v != -INFINITY;
         }
-      } else {
-        vis = vis && kj <= qpos && kj >= lo;
+        x[e] = vis ? v : -INFINITY;
+        mb = fmaxf(mb, x[e]);
       }
-      x[e] = vis ? v : -INFINITY;
-      mb = fmaxf(mb, x[e]);
     }
     float alpha = 1.f;
     bool rescale = false;
     if (mb > m_run + 8.f) {  // also true when m_run is still -inf
       if (m_run != -INFINITY) {
-        alpha = exp2f(m_run - mb);
+        alpha = fast_exp2(m_run - mb);
         rescale = true;
       }
       m_run = mb;
@@ -604,7 +644,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       float p8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        p8[e] = exp2f(x[cb * 8 + e] - base);
+        p8[e] = fast_exp2(x[cb * 8 + e] - base);
         ls += p8[e];
       }
       uint4 u;
@@ -648,64 +688,70 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   if (!ok) atomicExch(&g_kv_tc_error, 1);
   if (pending >= 0 && !ok) tc::mbar_wait(kvb0 + 8u * (pending & 1), (uint32_t)((pending >> 1) & 1));
 
-  // ---- epilogue: this thread's row ----
-  if (ok && row_valid) {
-    const int hq = kvh * G + g;
-    if (p.n_splits == 1) {
-      const float inv = nblk > 0 ? 1.f / l_run : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD;
-      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + s) * p.Hq * HD +
-                                   (long long)hq * HD
-                             : nullptr;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float o[32];
-        if (nblk > 0) {
-          tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
-          tc::tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0.f;
-        }
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          uint4 u;
-          T* h = reinterpret_cast<T*>(&u);
-          uint4 gu;
-          if (grow) gu = *reinterpret_cast<const uint4*>(grow + c * 32 + c8 * 8);
-          const T* gh = reinterpret_cast<const T*>(&gu);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float v = o[c8 * 8 + e] * inv;
-            if (grow) v *= 1.f / (1.f + __expf(-to_f32(gh[e])));
-            h[e] = from_f32<T>(v);
-          }
-          *reinterpret_cast<uint4*>(orow + c * 32 + c8 * 8) = u;
-        }
-      }
-    } else {
-      const int R = p.S * G;
+  // ---- epilogue: O rows leave through shared memory (the P tile) in 32-column slices, so
+  //      that global stores are whole 128-byte row segments ----
+  if (ok) {
+    const int R = p.S * G;
+    float* stage = reinterpret_cast<float*>(sm + OFF_P);  // [128 rows][32 floats], float4 index swizzled
+    const float scale_row = p.n_splits == 1 ? (nblk > 0 && l_run > 0.f ? 1.f / l_run : 0.f) : 1.f;
+    if (p.n_splits > 1 && row_valid) {
       const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)s * G + g;
-      float* wo = p.ws_o + row_id * HD;
-#pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        float o[32];
-        if (nblk > 0) {
-          tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
-          tc::tmem_wait_ld();
-        } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = 0.f;
-        }
-#pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(wo + c * 32 + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
-      }
       p.ws_ml[row_id * 2 + 0] = m_run;
       p.ws_ml[row_id * 2 + 1] = l_run;
     }
-  } else if (ok && !row_valid) {
-    // padding rows hold no output
+#pragma unroll 1
+    for (int c = 0; c < HD / 32; ++c) {
+      float o[32];
+      if (nblk > 0) {  // uniform across the CTA: every lane takes part in the warp-wide TMEM load
+        tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+        tc::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[e] = 0.f;
+      }
+#pragma unroll
+      for (int c4 = 0; c4 < 8; ++c4)
+        *reinterpret_cast<float4*>(stage + tid * 32 + ((c4 ^ (tid & 7)) << 2)) =
+            make_float4(o[c4 * 4] * scale_row, o[c4 * 4 + 1] * scale_row, o[c4 * 4 + 2] * scale_row,
+                        o[c4 * 4 + 3] * scale_row);
+      __syncthreads();
+      if (p.n_splits > 1) {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int idx = tid + it * 128, r = idx >> 3, c4 = idx & 7;
+          const int rs = tile * 16 + (r & 15), rg = r >> 4;
+          if (rs < p.S) {
+            const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)rs * G + rg;
+            *reinterpret_cast<float4*>(p.ws_o + row_id * HD + c * 32 + c4 * 4) =
+                *reinterpret_cast<const float4*>(stage + r * 32 + ((c4 ^ (r & 7)) << 2));
+          }
+        }
+      } else {
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          const int idx = tid + it * 128, r = idx >> 2, c8 = idx & 3;
+          const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
+          if (rs < p.S) {
+            const long long off = ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD + c * 32 + c8 * 8;
+            const float4 a = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8) ^ (r & 7)) << 2));
+            const float4 bq = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8 + 1) ^ (r & 7)) << 2));
+            float v[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
+            if (p.gate) {
+              const uint4 gu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.gate) + off);
+              const T* gh = reinterpret_cast<const T*>(&gu);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[e] *= 1.f / (1.f + __expf(-to_f32(gh[e])));
+            }
+            uint4 u;
+            T* h = reinterpret_cast<T*>(&u);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(v[e]);
+            *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off) = u;
+          }
+        }
+      }
+      __syncthreads();
+    }
   }
   // the other warps' epilogue reads of TMEM must finish before the allocation is released
   __syncwarp();
@@ -751,7 +797,7 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
   const int L = p.key_hi - p.key_lo;
   const int nblocks = max(1, (L + TC_KB - 1) / TC_KB);
   const long base = (long)row_tiles * p.B * p.Hkv;
-  int want = (int)((148 + base - 1) / base);
+  int want = (int)(148 / base);  // one wave: every CTA holds a whole SM (shared memory)
   want = max(1, min(want, min(nblocks, pl0.n_splits)));
   const int bps = (nblocks + want - 1) / want;
   const int ks = bps * TC_KB;
