@@ -448,12 +448,16 @@ def bench_kv_attention(args, ws, rank, local):
 
 def traffic_from_profiles(name):
     """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
-    path = os.path.join(ROOT, "profiles", "traffic.json")
+    path = os.path.join(ROOT, "profiles", "traffic.txt")  # "<workload> <bytes per launch>" lines
     try:
         with open(path) as f:
-            return json.load(f).get(name)
+            for line in f:
+                parts = line.split()
+                if len(parts) == 2 and parts[0] == name:
+                    return int(parts[1])
     except (OSError, ValueError):
-        return None
+        pass
+    return None
 
 
 def reference_arm(args, ws, rank):
