@@ -18,13 +18,19 @@ import torch.nn as nn
 
 from . import _lib
 
-__all__ = ["kv_attention", "kv_attention_workspace_size", "unified_cache_layer", "QwenAttentionB200"]
+__all__ = ["kv_attention", "kv_attention_workspace_size", "kv_device_error", "unified_cache_layer",
+           "QwenAttentionB200"]
 
 _ws_cache: dict = {}
 
 
 def kv_attention_workspace_size(B, S, H_q, H_kv, head_dim, ctx) -> int:
     return int(_lib.load().anemll_kv_attention_workspace_size(B, S, H_q, H_kv, head_dim, ctx))
+
+
+def kv_device_error(reset=True) -> int:
+    """Non-zero if a TMA-fed KV launch stopped on a bounded wait (synchronous)."""
+    return int(_lib.load().anemll_kv_attention_error(int(bool(reset))))
 
 
 def _workspace(device, nbytes):

@@ -71,7 +71,7 @@ kv_attn_kernel(KvParams p) {
   constexpr int ROWS = 16 * MW;
   constexpr int NT = MW * 32;
   constexpr int NTILE_O = HD / 8;
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
   T* Qs = reinterpret_cast<T*>(smem_raw);
   T* Ks = Qs + ROWS * HD;       // [2][NB][HD]
   T* Vs = Ks + 2 * NB * HD;     // [2][NB][HD]
@@ -654,6 +654,16 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       *reinterpret_cast<uint4*>(sm + OFF_P + swz128(tid, cb)) = u;
     }
     l_run = l_run * alpha + ls;
+    if (key0 + TC_KB > k_end) {
+      // V rows past the split end (unwritten cache rows, possibly not finite) are zeroed, so that
+      // their zero weights give exact zeros in P V
+      const int nz = key0 + TC_KB - k_end;
+      for (int i = tid; i < nz * NKB * 8; i += 128) {
+        const int r = TC_KB - nz + i / (NKB * 8), c = (i / 8) % NKB, u = i % 8;
+        *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + c) * KV_BLK + r * 128 + u * 16) =
+            make_uint4(0, 0, 0, 0);
+      }
+    }
     if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM access; alpha = 1 on other lanes
 #pragma unroll 1
       for (int c = 0; c < HD / 32; ++c) {
@@ -760,6 +770,332 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   if (warp == 0) tc::tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------
+// Decode-shaped calls (S * G <= 16 query rows, e.g. one token of 8 GQA heads).
+// A CTA owns one (sequence, kv head) and one key split.  K/V chunks of 64 keys
+// arrive by TMA (128-byte swizzle, up to MAX_STAGES chunks in flight), and the
+// four warps split every chunk: warp w takes keys [16w, 16w + 16) with its own
+// online softmax on mma.sync m16n8k16, so a chunk is four independent
+// dependency chains instead of one.  At the end the warps' (max, sum, O) are
+// merged through shared memory and the CTA writes either the final gated rows
+// (one split) or one partial per row for kv_combine_kernel.  The new cache rows
+// are copied from k_new / v_new into the landed tiles and into the cache by the
+// warp that owns them.  V rows past the split end are zeroed in shared memory.
+constexpr int DC_KC = 64;  // keys per chunk: 16 per warp
+
+template <int HD>
+struct DcLayout {
+  static constexpr int NKB = HD / 64;
+  static constexpr int KV_BLK = DC_KC * 128;                    // [64 keys][128 B] per 64-column block
+  static constexpr int STAGE = 2 * NKB * KV_BLK;                 // K blocks, then V blocks
+  static constexpr int OFF_Q = 0;                                // [NKB][16 rows][128 B]
+  static constexpr int OFF_ST = NKB * 16 * 128;                  // stages (and the merge slab after the loop)
+  static constexpr int SLAB_LD = HD + 8;                         // floats per merge-slab row (bank spread)
+  static constexpr int SLAB = 4 * 16 * SLAB_LD * 4;
+  static constexpr int MAX_STAGES = HD == 256 ? 2 : HD == 128 ? 3 : 4;
+  static size_t smem_bytes(int stages) {
+    const size_t st = (size_t)stages * STAGE;
+    return (size_t)OFF_ST + (st > (size_t)SLAB ? st : (size_t)SLAB) + 1024;
+  }
+};
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(128, 1)
+kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages) {
+  using L = DcLayout<HD>;
+  constexpr int NKB = L::NKB;
+  constexpr int NTILE_O = HD / 8;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[L::MAX_STAGES];
+  __shared__ float s_m[4][16], s_l[4][16];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int G = p.Hq / p.Hkv;
+  const int R = p.S * G;
+  const int bh = blockIdx.y, b = bh / p.Hkv, kvh = bh % p.Hkv;
+  const int split = blockIdx.x;
+  const int k_begin = p.key_lo + split * p.ks;
+  const int k_end = min(p.key_hi, k_begin + p.ks);
+  const int nch = k_end > k_begin ? (k_end - k_begin + DC_KC - 1) / DC_KC : 0;
+  const int NS = n_stages;
+  const uint32_t sbase = tc::smem_u32(sm);
+  const uint32_t full0 = tc::smem_u32(&full[0]);
+
+  T* Kc = reinterpret_cast<T*>(p.kc) + (long long)b * p.bs + (long long)kvh * p.hs;
+  T* Vc = reinterpret_cast<T*>(p.vc) + (long long)b * p.bs + (long long)kvh * p.hs;
+  const T* kn = p.has_new ? reinterpret_cast<const T*>(p.k_new) + (long long)bh * p.S * HD : nullptr;
+  const T* vn = p.has_new ? reinterpret_cast<const T*>(p.v_new) + (long long)bh * p.S * HD : nullptr;
+
+  auto issue = [&](int c) {  // chunk c into stage c % NS
+    const int st = c % NS;
+    const uint32_t fb = full0 + 8u * st;
+    tc::mbar_arrive_expect_tx(fb, (uint32_t)L::STAGE);
+    const int key0 = k_begin + c * DC_KC;
+#pragma unroll
+    for (int cb = 0; cb < NKB; ++cb) {
+      const uint32_t dk = sbase + L::OFF_ST + st * L::STAGE + cb * L::KV_BLK;
+      const uint32_t dv = dk + NKB * L::KV_BLK;
+      if (p.B > 1) {
+        tc::tma_load_4d(dk, &maps.k, cb * 64, key0, kvh, b, fb);
+        tc::tma_load_4d(dv, &maps.v, cb * 64, key0, kvh, b, fb);
+      } else {
+        tc::tma_load_3d(dk, &maps.k, cb * 64, key0, kvh, fb);
+        tc::tma_load_3d(dv, &maps.v, cb * 64, key0, kvh, fb);
+      }
+    }
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) tc::mbar_init(&full[s], 1);
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int c = 0; c < NS && c < nch; ++c) issue(c);
+
+  // Q tile: 16 rows (rows >= R are zero), swizzled like the TMA tiles
+  for (int i = tid; i < 16 * (HD / 8); i += 128) {
+    const int r = i / (HD / 8), c = i % (HD / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < R) {
+      const int s = r / G, h = kvh * G + r % G;
+      v = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) + ((long long)(b * p.Hq + h) * p.S + s) * HD +
+                                          c * 8);
+    }
+    *reinterpret_cast<uint4*>(sm + L::OFF_Q + (c >> 3) * 2048 + swz128(r, c & 7)) = v;
+  }
+
+  // visibility of this thread's rows g and g + 8
+  int rows_s[2], rows_lo[2], rows_hi[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g + h * 8;
+    const int s = r < R ? r / G : 0;
+    rows_s[h] = s;
+    const int pq = p.pos + s;
+    int lo = 0;
+    if (p.window > 0) lo = p.aligned ? max(0, min(p.pos + p.S, p.ctx) - p.window) : pq - p.window + 1;
+    rows_lo[h] = lo;
+    rows_hi[h] = r < R ? pq : -1;
+  }
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float o_acc[NTILE_O][4];
+#pragma unroll
+  for (int i = 0; i < NTILE_O; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+
+  bool ok = true;
+  int c = 0;
+#pragma unroll 1
+  for (; c < nch; ++c) {
+    const int st = c % NS;
+    // the barrier also means every warp is done with chunk c - 1, whose stage is then refilled
+    // (NS >= 2 whenever a refill happens, so that stage is not the one waited for here)
+    ok = __syncthreads_and(tc::mbar_wait(full0 + 8u * st, (uint32_t)((c / NS) & 1)));
+    if (!ok) break;
+    if (tid == 0 && c >= 1 && c - 1 + NS < nch) issue(c - 1 + NS);
+    uint8_t* Kt = sm + L::OFF_ST + st * L::STAGE;
+    uint8_t* Vt = Kt + NKB * L::KV_BLK;
+    const int key0 = k_begin + c * DC_KC;
+    const int kw0 = key0 + warp * 16;  // this warp's first key
+
+    // new rows into the landed tiles (and the cache); V rows past the split end zeroed
+    bool touched = false;
+    if (p.has_new) {
+      const int j0 = max(kw0, p.pos), j1 = min(min(kw0 + 16, k_end), p.pos + p.S);
+      if (j1 > j0) {
+        touched = true;
+        for (int i = lane; i < (j1 - j0) * (HD / 8); i += 32) {
+          const int j = j0 + i / (HD / 8), ch = i % (HD / 8), r = j - key0;
+          const uint4 kv = *reinterpret_cast<const uint4*>(kn + (long long)(j - p.pos) * HD + ch * 8);
+          const uint4 vv = *reinterpret_cast<const uint4*>(vn + (long long)(j - p.pos) * HD + ch * 8);
+          *reinterpret_cast<uint4*>(Kt + (ch >> 3) * L::KV_BLK + swz128(r, ch & 7)) = kv;
+          *reinterpret_cast<uint4*>(Vt + (ch >> 3) * L::KV_BLK + swz128(r, ch & 7)) = vv;
+          *reinterpret_cast<uint4*>(Kc + (long long)j * HD + ch * 8) = kv;
+          *reinterpret_cast<uint4*>(Vc + (long long)j * HD + ch * 8) = vv;
+        }
+      }
+    }
+    if (kw0 + 16 > k_end) {
+      const int z0 = max(kw0, k_end);
+      touched = true;
+      for (int i = lane; i < (kw0 + 16 - z0) * NKB * 8; i += 32) {
+        const int r = z0 - key0 + i / (NKB * 8), cb = (i / 8) % NKB, u = i % 8;
+        *reinterpret_cast<uint4*>(Vt + cb * L::KV_BLK + r * 128 + u * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (touched) tc::fence_async_smem();  // these generic writes precede the stage's next TMA refill
+    __syncwarp();
+
+    // S = Q K^T: 16 rows x 16 keys, two accumulator sets to halve the dependency chain
+    float sc[2][2][4];
+#pragma unroll
+    for (int a2 = 0; a2 < 2; ++a2)
+#pragma unroll
+      for (int n = 0; n < 2; ++n) sc[a2][n][0] = sc[a2][n][1] = sc[a2][n][2] = sc[a2][n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+      uint32_t a[4], bfr[4];
+      {
+        const int r = lane & 15, ch = kk * 2 + (lane >> 4);
+        ldmatrix_x4(a, sm + L::OFF_Q + (ch >> 3) * 2048 + swz128(r, ch & 7));
+      }
+      {
+        const int r = warp * 16 + (lane & 7) + ((lane >> 4) << 3), ch = kk * 2 + ((lane >> 3) & 1);
+        ldmatrix_x4(bfr, Kt + (ch >> 3) * L::KV_BLK + swz128(r, ch & 7));
+      }
+      mma_16816<T>(sc[kk & 1][0], a, bfr[0], bfr[1]);
+      mma_16816<T>(sc[kk & 1][1], a, bfr[2], bfr[3]);
+    }
+    // scale, mask, online softmax (base 2)
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const int j = kw0 + n * 8 + t4 * 2 + (e & 1);
+        float v = (sc[0][n][e] + sc[1][n][e]) * p.scale_log2;
+        bool vis = j < k_end;
+        if (p.mask) {
+          if (vis && rows_hi[h] >= 0) {
+            const long long mi = (long long)rows_s[h] * p.mask_ld + j;
+            const float mv = p.mask_dtype == ANEMLL_F32 ? reinterpret_cast<const float*>(p.mask)[mi]
+                           : p.mask_dtype == ANEMLL_F16 ? __half2float(reinterpret_cast<const __half*>(p.mask)[mi])
+                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.mask)[mi]);
+            v += mv * 1.4426950408889634f;
+          } else {
+            vis = false;
+          }
+          if (v == -INFINITY) vis = false;
+        } else {
+          vis = vis && j <= rows_hi[h] && j >= rows_lo[h];
+        }
+        v = vis ? v : -INFINITY;
+        sc[0][n][e] = v;
+        mx[h] = fmaxf(mx[h], v);
+      }
+    }
+    float alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float mnew = fmaxf(m_run[h], mx[h]);
+      const float base = mnew == -INFINITY ? 0.f : mnew;
+      alpha[h] = fast_exp2(m_run[h] - base);
+      m_run[h] = mnew;
+      mx[h] = base;
+    }
+    float rs[2] = {0.f, 0.f};
+    uint32_t pf[4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+      const float p0 = fast_exp2(sc[0][n][0] - mx[0]);
+      const float p1 = fast_exp2(sc[0][n][1] - mx[0]);
+      const float p2 = fast_exp2(sc[0][n][2] - mx[1]);
+      const float p3 = fast_exp2(sc[0][n][3] - mx[1]);
+      rs[0] += p0 + p1;
+      rs[1] += p2 + p3;
+      pf[n * 2 + 0] = pack2<T>(p0, p1);
+      pf[n * 2 + 1] = pack2<T>(p2, p3);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+      rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+      l_run[h] = l_run[h] * alpha[h] + rs[h];
+    }
+    // O = alpha O + P V
+#pragma unroll
+    for (int n2 = 0; n2 < HD / 16; ++n2) {
+      uint32_t bfr[4];
+      const int r = warp * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), ch = n2 * 2 + (lane >> 4);
+      ldmatrix_x4_trans(bfr, Vt + (ch >> 3) * L::KV_BLK + swz128(r, ch & 7));
+#pragma unroll
+      for (int q2 = 0; q2 < 2; ++q2) {
+        float* o = o_acc[2 * n2 + q2];
+        o[0] *= alpha[0];
+        o[1] *= alpha[0];
+        o[2] *= alpha[1];
+        o[3] *= alpha[1];
+        mma_16816<T>(o, pf, bfr[2 * q2], bfr[2 * q2 + 1]);
+      }
+    }
+  }
+  if (!ok) {
+    atomicExch(&g_kv_tc_error, 1);
+    // chunks issued and not consumed, [c, issued_end), may still be landing: wait for them
+    // (bounded) before the CTA exits.  Chunks [0, NS) are issued up front and iteration
+    // c' >= 1 issues chunk c' - 1 + NS, so issued_end = min(nch, max(NS, c - 1 + NS)).
+    const int issued_end = min(nch, c == 0 ? NS : c - 1 + NS);
+    for (int x = c; x < issued_end; ++x) tc::mbar_wait(full0 + 8u * (x % NS), (uint32_t)((x / NS) & 1));
+    return;  // block-uniform: ok came from __syncthreads_and
+  }
+
+  // ---- merge the four warps' partial softmax states through shared memory ----
+  if (t4 == 0) {
+    s_m[warp][g] = m_run[0];
+    s_m[warp][g + 8] = m_run[1];
+  }
+  __syncthreads();  // also: every warp is done with the stage memory the slab reuses
+  float* slab = reinterpret_cast<float*>(sm + L::OFF_ST);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g + h * 8;
+    float M = s_m[0][r];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) M = fmaxf(M, s_m[w][r]);
+    const float f = m_run[h] == -INFINITY ? 0.f : fast_exp2(m_run[h] - M);
+    if (t4 == 0) s_l[warp][r] = l_run[h] * f;
+    float* row = slab + (warp * 16 + r) * L::SLAB_LD + t4 * 2;
+#pragma unroll
+    for (int i = 0; i < NTILE_O; ++i)
+      *reinterpret_cast<float2*>(row + i * 8) = make_float2(o_acc[i][2 * h] * f, o_acc[i][2 * h + 1] * f);
+  }
+  __syncthreads();
+  for (int idx = tid; idx < R * (HD / 4); idx += 128) {
+    const int r = idx / (HD / 4), d = (idx % (HD / 4)) * 4;
+    float4 o = *reinterpret_cast<const float4*>(slab + r * L::SLAB_LD + d);
+    float Ls = s_l[0][r], M = s_m[0][r];
+#pragma unroll
+    for (int w = 1; w < 4; ++w) {
+      const float4 x = *reinterpret_cast<const float4*>(slab + (w * 16 + r) * L::SLAB_LD + d);
+      o.x += x.x;
+      o.y += x.y;
+      o.z += x.z;
+      o.w += x.w;
+      Ls += s_l[w][r];
+      M = fmaxf(M, s_m[w][r]);
+    }
+    if (p.n_splits == 1) {
+      const int s = r / G, hq = kvh * G + r % G;
+      const long long off = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
+      const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+      float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
+      if (p.gate) {
+        const uint2 gu = *reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p.gate) + off);
+        const T* gh = reinterpret_cast<const T*>(&gu);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] *= 1.f / (1.f + __expf(-to_f32(gh[e])));
+      }
+      uint2 u;
+      T* hh = reinterpret_cast<T*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hh[e] = from_f32<T>(v[e]);
+      *reinterpret_cast<uint2*>(reinterpret_cast<T*>(p.out) + off) = u;
+    } else {
+      const long long row_id = ((long long)bh * p.n_splits + split) * R + r;
+      *reinterpret_cast<float4*>(p.ws_o + row_id * HD + d) = o;
+      if (d == 0) {
+        p.ws_ml[row_id * 2 + 0] = M;
+        p.ws_ml[row_id * 2 + 1] = Ls;
+      }
+    }
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 kv_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -783,6 +1119,70 @@ int kv_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   ANEMLL_REQUIRE(r == CUDA_SUCCESS, ANEMLL_EINVAL, "kv_attention: tensor map encoding failed (%d)", (int)r);
   return ANEMLL_OK;
+}
+
+// K and V cache maps: [hd, ctx, H_kv(, B)] with 64-element x 64-key boxes, 128-byte swizzle.
+int kv_cache_maps(KvTcMaps& maps, const KvParams& p, int HD) {
+  static_assert(TC_KB == DC_KC, "prefill and decode kernels share the 64-key cache box");
+  const cuuint32_t bk[4] = {64, (cuuint32_t)TC_KB, 1, 1};
+  int rc;
+  if (p.B > 1) {
+    const cuuint64_t dk[4] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv, (cuuint64_t)p.B};
+    const cuuint64_t sk[3] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2, (cuuint64_t)p.bs * 2};
+    rc = kv_encode(&maps.k, p.kc, 4, dk, sk, bk);
+    if (!rc) rc = kv_encode(&maps.v, p.vc, 4, dk, sk, bk);
+  } else {
+    const cuuint64_t dk[3] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv};
+    const cuuint64_t sk[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2};
+    rc = kv_encode(&maps.k, p.kc, 3, dk, sk, bk);
+    if (!rc) rc = kv_encode(&maps.v, p.vc, 3, dk, sk, bk);
+  }
+  return rc;
+}
+
+// Decode kernel: at most 16 query rows, cache strides whole 16-byte units, 8-byte aligned out / gate.
+bool dec_eligible(int S, int Hq, int Hkv, long long bs, long long hs, const void* out, const void* gate) {
+  return (long long)S * (Hq / Hkv) <= 16 && (hs * 2) % 16 == 0 && (bs * 2) % 16 == 0 && aligned(out, 8) &&
+         (!gate || aligned(gate, 8));
+}
+
+template <typename T, int HD>
+int launch_kv_dec(KvParams& p, const Plan& pl0, cudaStream_t st) {
+  using L = DcLayout<HD>;
+  // about two CTAs per SM, never more splits than the generic plan (workspace bound)
+  const int Lk = p.key_hi - p.key_lo;
+  const int nchunks = max(1, (Lk + DC_KC - 1) / DC_KC);
+  const long base = (long)p.B * p.Hkv;
+  int want = (int)((2L * 148 + base - 1) / base);
+  want = max(1, min(want, min(nchunks, pl0.n_splits)));
+  const int cps = (nchunks + want - 1) / want;  // chunks per split
+  const int ks = cps * DC_KC;
+  const int n_splits = max(1, (Lk + ks - 1) / ks);
+  const int stages = min(cps, L::MAX_STAGES);
+  KvParams q = p;
+  q.n_splits = n_splits;
+  q.ks = ks;
+  if (n_splits > 1) {
+    const size_t R = (size_t)p.S * (p.Hq / p.Hkv);
+    q.ws_ml = q.ws_o + (size_t)p.B * p.Hkv * n_splits * R * HD;
+  }
+  KvTcMaps maps;
+  int rc = kv_cache_maps(maps, p, HD);
+  if (rc) return rc;
+  const size_t smem = L::smem_bytes(stages);
+  auto kern = kv_decode_kernel<T, HD>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  dim3 grid(n_splits, p.B * p.Hkv);
+  kern<<<grid, 128, smem, st>>>(maps, q, stages);
+  rc = launch_status("kv_attention_decode");
+  if (rc) return rc;
+  if (n_splits > 1) {
+    const int R = p.S * (p.Hq / p.Hkv);
+    dim3 g2(R, p.B * p.Hkv);
+    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(q);
+    rc = launch_status("kv_combine");
+  }
+  return rc;
 }
 
 bool tc_eligible(int S, int Hq, int Hkv, int hd, long long bs, long long hs, const void* out, const void* gate) {
@@ -815,19 +1215,7 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
     const cuuint64_t sq[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.S * HD * 2};
     const cuuint32_t bq[3] = {64, 16, 8};
     int rc = kv_encode(&maps.q, p.q, 3, dq, sq, bq);
-    if (rc) return rc;
-    const cuuint32_t bk[4] = {64, (cuuint32_t)TC_KB, 1, 1};
-    if (p.B > 1) {
-      const cuuint64_t dk[4] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv, (cuuint64_t)p.B};
-      const cuuint64_t sk[3] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2, (cuuint64_t)p.bs * 2};
-      rc = kv_encode(&maps.k, p.kc, 4, dk, sk, bk);
-      if (!rc) rc = kv_encode(&maps.v, p.vc, 4, dk, sk, bk);
-    } else {
-      const cuuint64_t dk[3] = {(cuuint64_t)HD, (cuuint64_t)p.ctx, (cuuint64_t)p.Hkv};
-      const cuuint64_t sk[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.hs * 2};
-      rc = kv_encode(&maps.k, p.kc, 3, dk, sk, bk);
-      if (!rc) rc = kv_encode(&maps.v, p.vc, 3, dk, sk, bk);
-    }
+    if (!rc) rc = kv_cache_maps(maps, p, HD);
     if (rc) return rc;
   }
   if (p.has_new) {
@@ -858,6 +1246,16 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
 }  // namespace anemll
 
 using namespace anemll;
+
+extern "C" int anemll_kv_attention_error(int reset) {
+  int h = 0;
+  if (cudaMemcpyFromSymbol(&h, g_kv_tc_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset && h) {
+    const int z = 0;
+    if (cudaMemcpyToSymbol(g_kv_tc_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  }
+  return h;
+}
 
 extern "C" size_t anemll_kv_attention_workspace_size(int B, int S, int H_q, int H_kv, int head_dim, int ctx) {
   if (B <= 0 || S <= 0 || H_q <= 0 || H_kv <= 0 || H_q % H_kv || ctx <= 0) return 0;
@@ -910,11 +1308,18 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
   cudaStream_t st = (cudaStream_t)stream;
   const bool use_tc = tc_eligible(S, H_q, H_kv, head_dim, cache_batch_stride, cache_head_stride, out, gate);
+  const bool use_dec = !use_tc && dec_eligible(S, H_q, H_kv, cache_batch_stride, cache_head_stride, out, gate);
   return ANEMLL_DISPATCH_HALF(dtype, T, [&] {
     switch (head_dim) {
-      case 64: return launch_kv<T, 64>(p, pl, st);
-      case 128: return use_tc ? launch_kv_tc<T, 128>(p, pl, st) : launch_kv<T, 128>(p, pl, st);
-      default: return use_tc ? launch_kv_tc<T, 256>(p, pl, st) : launch_kv<T, 256>(p, pl, st);
+      case 64: return use_dec ? launch_kv_dec<T, 64>(p, pl, st) : launch_kv<T, 64>(p, pl, st);
+      case 128:
+        return use_tc ? launch_kv_tc<T, 128>(p, pl, st)
+               : use_dec ? launch_kv_dec<T, 128>(p, pl, st)
+                         : launch_kv<T, 128>(p, pl, st);
+      default:
+        return use_tc ? launch_kv_tc<T, 256>(p, pl, st)
+               : use_dec ? launch_kv_dec<T, 256>(p, pl, st)
+                         : launch_kv<T, 256>(p, pl, st);
     }
   });
 }

@@ -149,6 +149,15 @@ int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, con
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Device-side status of the TMA-fed KV kernels (prefill chunks on the tensor
+ * cores, decode steps): non-zero if a bounded wait for a K/V tile ran out (the
+ * kernel then stopped early and that call's outputs are invalid).
+ * Synchronous; reset != 0 clears the flag.  Returns -1 on a CUDA error.  No
+ * counterpart in the reference (diagnostics of this library).
+ */
+int anemll_kv_attention_error(int reset);
+
+/*
  * Allocation-free form of anemll_kv_attention (no counterpart in the
  * reference).  For callers that cannot allocate device memory when they call
  * in — an engine that reserves all GPU memory at start-up and forbids later

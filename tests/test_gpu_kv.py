@@ -79,6 +79,7 @@ def test_cfg2_chunked_prefill_and_decode(window):
         else:
             ok.write_cache(cache_ref, k, v, 0, 1, p)
     assert torch.equal(cache_dev.cpu(), cache_ref.half())
+    assert attention.kv_device_error() == 0
 
 
 def test_batched_cache_and_workspace_errors():
@@ -115,3 +116,68 @@ def test_bf16_cache():
     ref = ok.attend(q, kc.unsqueeze(0), vc.unsqueeze(0), ok.additive_mask(S, ctx, pos), gate)
     # bf16 probabilities feed the PV product: its 8-bit mantissa sets this bound
     assert_close(out.float(), ref, "bf16", rel_l2=5e-3, max_abs=1e-2)
+
+
+def _aligned4_out(B, S, width, dt):
+    """An output view whose address is 4- but not 8-byte aligned: the library then takes its
+    generic split-KV kernel instead of the TMA decode kernel."""
+    buf = torch.empty(B * S * width + 2, dtype=dt, device=DEV)
+    out = buf[2:].view(B, S, width)
+    assert out.data_ptr() % 8 == 4
+    return out
+
+
+@pytest.mark.parametrize("hd", [64, 128, 256])
+@pytest.mark.parametrize("dt", [torch.half, torch.bfloat16])
+def test_decode_kernels_match_oracle(hd, dt):
+    """Decode-shaped calls (S x G <= 16 query rows), batched caches: the TMA decode kernel and
+    the generic split-KV kernel both match the oracle under causal, sliding-window and
+    explicit masks, with 1, 8 and 16 query heads per kv head; written cache rows bit-exact."""
+    torch.manual_seed(11 + hd)
+    B, ctx = 2, 1536
+    cases = [  # (H_q, H_kv, S, pos, window, explicit mask)
+        (16, 2, 1, 1000, 0, False), (16, 2, 1, 1400, 300, False), (16, 2, 2, 777, 0, True),
+        (16, 2, 1, 63, 0, False), (32, 2, 1, 1535, 0, False), (4, 4, 3, 500, 128, False),
+    ]
+    # bf16 probabilities and outputs carry an 8-bit mantissa: 5e-3 / 1e-2 for bf16
+    rel_l2, max_abs = (1e-3, 2e-3) if dt == torch.half else (5e-3, 1e-2)
+    for Hq, Hkv, S, pos, window, use_mask in cases:
+        kc = torch.randn(B, Hkv, ctx, hd).to(dt)
+        vc = torch.randn(B, Hkv, ctx, hd).to(dt)
+        q = torch.randn(B, Hq, S, hd).to(dt)
+        kn = torch.randn(B, Hkv, S, hd).to(dt)
+        vn = torch.randn(B, Hkv, S, hd).to(dt)
+        gate = torch.randn(B, S, Hq * hd).to(dt)
+        kr, vr = kc.float().clone(), vc.float().clone()
+        kr[:, :, pos:pos + S] = kn.float()
+        vr[:, :, pos:pos + S] = vn.float()
+        amask = ok.additive_mask(S, ctx, pos, window)
+        ref = ok.attend(q, kr, vr, amask, gate)
+        for generic in (False, True):
+            kd, vd = kc.to(DEV), vc.to(DEV)
+            out = _aligned4_out(B, S, Hq * hd, dt) if generic else None
+            res = attention.kv_attention(q.to(DEV), kd, vd, pos, k_new=kn.to(DEV), v_new=vn.to(DEV),
+                                         gate=gate.to(DEV), causal_mask=amask.to(dt).to(DEV) if use_mask else None,
+                                         window=0 if use_mask else window, out=out)
+            name = f"hd {hd} {dt} Hq {Hq} Hkv {Hkv} S {S} pos {pos} w {window} mask {use_mask} generic {generic}"
+            assert_close(res.float().cpu(), ref, name, rel_l2=rel_l2, max_abs=max_abs)
+            assert torch.equal(kd.cpu().float(), kr) and torch.equal(vd.cpu().float(), vr), name
+    assert attention.kv_device_error() == 0
+
+
+def test_unwritten_cache_rows_are_never_read():
+    """Cache rows past the visible range may hold anything, NaN included: prefill chunks (tcgen05
+    path), decode steps (TMA decode kernel) and the generic kernel read none of them."""
+    torch.manual_seed(12)
+    for Hq, Hkv, hd, S, pos in [(16, 2, 256, 64, 300), (16, 2, 256, 48, 100), (16, 2, 128, 1, 333),
+                                (8, 2, 64, 20, 70), (16, 2, 256, 1, 0)]:
+        ctx = 1024
+        kc = torch.randn(Hkv, ctx, hd).half()
+        vc = torch.randn(Hkv, ctx, hd).half()
+        q = torch.randn(1, Hq, S, hd).half()
+        gate = torch.randn(1, S, Hq * hd).half()
+        ref = ok.attend(q, kc.unsqueeze(0), vc.unsqueeze(0), ok.additive_mask(S, ctx, pos), gate)
+        kc[:, pos + S:] = float("nan")
+        vc[:, pos + S:] = float("nan")
+        out = attention.kv_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos, gate=gate.to(DEV))
+        assert_close(out.float().cpu(), ref, f"hd {hd} S {S} pos {pos}")
