@@ -66,6 +66,16 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Programmatic dependent launch (PTX griddepcontrol): a kernel launched with programmatic stream
+// serialisation may start while the previous kernel of the stream is still running; it must call
+// griddep_wait() before it reads or writes global memory (the wait returns once the previous grid has
+// completed and its writes are visible; without that launch attribute it returns at once).
+// griddep_launch_dependents() lets the next such kernel start launching early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 __device__ __forceinline__ float softplus(float x) {
   // log(1 + e^x), evaluated without overflow (same threshold behaviour as torch's softplus, beta=1, threshold=20)
   return x > 20.0f ? x : log1pf(__expf(x));

@@ -68,6 +68,7 @@ __device__ __forceinline__ void load_rows_async(T* smem, int nrows, const T* con
 template <typename T, int HD, int MW>
 __global__ void __launch_bounds__(MW * 32)
 kv_attn_kernel(KvParams p) {
+  griddep_wait();
   constexpr int ROWS = 16 * MW;
   constexpr int NT = MW * 32;
   constexpr int NTILE_O = HD / 8;
@@ -287,6 +288,7 @@ kv_attn_kernel(KvParams p) {
     }
     __syncthreads();
   }
+  griddep_launch_dependents();
 
   // epilogue
 #pragma unroll
@@ -327,61 +329,130 @@ kv_attn_kernel(KvParams p) {
 }
 
 // Merge the split partials of each row: out = sum_i w_i O_i / sum_i w_i l_i, w_i = 2^(m_i - max m).
-template <typename T, int HD>
-__global__ void __launch_bounds__(HD)
+// One CTA per row with CB_WARPS warps: warp w reads splits w, w + CB_WARPS, ... (each lane HD/32
+// consecutive columns, so a warp reads whole partial rows), and every one of its partial loads is
+// issued before the weights are known, so the kernel waits on a single memory round trip.  The
+// warp sums meet in shared memory.
+// PER = splits per warp (1, 2, 4, 8 or 16), the smallest that covers n_splits, keeps the registers
+// (and so the CTAs per SM) in step with the split count.
+constexpr int CB_WARPS = 8;
+constexpr int CB_MAX_SPLITS = 128;
+
+template <typename T, int HD, int PER>
+__global__ void __launch_bounds__(CB_WARPS * 32)
 kv_combine_kernel(KvParams p) {
+  static_assert(PER <= CB_MAX_SPLITS / CB_WARPS, "split count above the combine's limit");
+  griddep_wait();
+  griddep_launch_dependents();
+  constexpr int VPT = HD / 32;  // columns per lane
   const int G = p.Hq / p.Hkv;
   const int R = p.S * G;
   const int r = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / p.Hkv, kvh = bh % p.Hkv;
-  const int d = threadIdx.x;
-  constexpr int NW = HD / 32;
-  __shared__ float s_w[128];  // n_splits <= 128
-  __shared__ float s_red[NW];
-  // (max, sum) of the splits in parallel: thread d holds splits d, d + HD, ...
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float s_w[CB_MAX_SPLITS];
+  __shared__ float s_red[CB_WARPS];
+  __shared__ __align__(16) float s_acc[CB_WARPS][HD];
   const int ns = p.n_splits;
   const long long row0 = (long long)bh * ns * R + r;  // row id of split 0; split i adds i * R
-  float mloc = -INFINITY;
-  for (int i = d; i < ns; i += HD) mloc = fmaxf(mloc, p.ws_ml[(row0 + (long long)i * R) * 2]);
-  float M = warp_max(mloc);
-  if ((d & 31) == 0) s_red[d >> 5] = M;
-  __syncthreads();
-  M = -INFINITY;
+  const long long step = (long long)R * HD;
+  const float* po = p.ws_o + row0 * HD + lane * VPT;
+  float v[PER][VPT];
 #pragma unroll
-  for (int w = 0; w < NW; ++w) M = fmaxf(M, s_red[w]);
-  const float base = M == -INFINITY ? 0.f : M;
-  float lloc = 0.f;
-  for (int i = d; i < ns; i += HD) {
-    const float wi = fast_exp2(p.ws_ml[(row0 + (long long)i * R) * 2] - base);
-    s_w[i] = wi;
-    lloc += wi * p.ws_ml[(row0 + (long long)i * R) * 2 + 1];
+  for (int k = 0; k < PER; ++k) {
+    const int i = warp + CB_WARPS * k;
+#pragma unroll
+    for (int e = 0; e < VPT; e += 2) {
+      float2 x = make_float2(0.f, 0.f);
+      if (i < ns) x = *reinterpret_cast<const float2*>(po + i * step + e);
+      v[k][e] = x.x;
+      v[k][e + 1] = x.y;
+    }
   }
-  __syncthreads();  // every s_w written, every s_red read
-  float Lp = warp_sum(lloc);
-  if ((d & 31) == 0) s_red[d >> 5] = Lp;
+  // (max, sum) of the splits: thread t holds split t
+  float mt = -INFINITY, lt = 0.f;
+  if (tid < ns) {
+    mt = p.ws_ml[(row0 + (long long)tid * R) * 2];
+    lt = p.ws_ml[(row0 + (long long)tid * R) * 2 + 1];
+  }
+  float M = warp_max(mt);
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+#pragma unroll
+  for (int w = 1; w < CB_WARPS; ++w) M = fmaxf(M, s_red[w]);
+  const float base = M == -INFINITY ? 0.f : M;
+  const float wt = tid < ns ? fast_exp2(mt - base) : 0.f;
+  if (tid < ns) s_w[tid] = wt;
+  const float Lp = warp_sum(wt * lt);
+  __syncthreads();  // every s_w written, every read of M from s_red done
+  if (lane == 0) s_red[warp] = Lp;
+  float acc[VPT];
+#pragma unroll
+  for (int e = 0; e < VPT; ++e) acc[e] = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = warp + CB_WARPS * k;
+    if (i < ns) {
+      const float wi = s_w[i];
+#pragma unroll
+      for (int e = 0; e < VPT; ++e) acc[e] += wi * v[k][e];
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < VPT; e += 2) *reinterpret_cast<float2*>(&s_acc[warp][lane * VPT + e]) = make_float2(acc[e], acc[e + 1]);
   __syncthreads();
   float L = 0.f;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) L += s_red[w];
-  // weighted sum of the partial rows, eight independent loads in flight
-  const float* po = p.ws_o + row0 * HD + d;
-  const long long step = (long long)R * HD;
-  float acc = 0.f;
-  int i = 0;
-  for (; i + 8 <= ns; i += 8) {
-    float v8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v8[u] = po[(long long)(i + u) * step];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) acc += s_w[i + u] * v8[u];
-  }
-  for (; i < ns; ++i) acc += s_w[i] * po[(long long)i * step];
+  for (int w = 0; w < CB_WARPS; ++w) L += s_red[w];
   const int s = r / G, hq = kvh * G + r % G;
-  const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
-  float v = acc / L;
-  if (p.gate) v *= 1.f / (1.f + __expf(-to_f32(reinterpret_cast<const T*>(p.gate)[o])));
-  reinterpret_cast<T*>(p.out)[o] = from_f32<T>(v);
+  for (int d = tid; d < HD; d += CB_WARPS * 32) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < CB_WARPS; ++w) a += s_acc[w][d];
+    const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
+    float val = a / L;
+    if (p.gate) val *= 1.f / (1.f + __expf(-to_f32(reinterpret_cast<const T*>(p.gate)[o])));
+    reinterpret_cast<T*>(p.out)[o] = from_f32<T>(val);
+  }
+}
+
+// Launch with programmatic stream serialisation, so that the kernel's launch overlaps the tail of the
+// previous kernel in the stream.  Every kernel launched this way calls griddep_wait() before its first
+// global-memory access.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: launch failed, CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+    return (int)e;
+  }
+  return launch_status(what);
+}
+
+template <typename T, int HD>
+int launch_combine(const KvParams& q, cudaStream_t st) {
+  const int R = q.S * (q.Hq / q.Hkv);
+  const dim3 grid(R, q.B * q.Hkv), block(CB_WARPS * 32);
+  const int per = (q.n_splits + CB_WARPS - 1) / CB_WARPS;
+  if (per <= 1) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 1>, grid, block, 0, st, q);
+  if (per <= 2) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 2>, grid, block, 0, st, q);
+  if (per <= 4) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 4>, grid, block, 0, st, q);
+  if (per <= 8) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 8>, grid, block, 0, st, q);
+  return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 16>, grid, block, 0, st, q);
 }
 
 struct Plan {
@@ -420,24 +491,21 @@ Plan make_plan(int B, int S, int Hq, int Hkv, int ctx, int pos, int window, int 
 template <typename T, int HD>
 int launch_kv(KvParams& p, const Plan& pl, cudaStream_t st) {
   dim3 grid(pl.row_tiles, pl.n_splits, p.B * p.Hkv);
+  int rc;
   if (pl.mw == 1) {
     const size_t smem = (size_t)(16 * HD + 4 * NB * HD) * sizeof(T);
     auto kern = kv_attn_kernel<T, HD, 1>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 32, smem, st>>>(p);
+    rc = launch_pdl("kv_attention", kern, grid, dim3(32), smem, st, p);
   } else {
     const size_t smem = (size_t)(64 * HD + 4 * NB * HD) * sizeof(T);
     auto kern = kv_attn_kernel<T, HD, 4>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<grid, 128, smem, st>>>(p);
+    rc = launch_pdl("kv_attention", kern, grid, dim3(128), smem, st, p);
   }
-  int rc = launch_status("kv_attention");
   if (rc) return rc;
   if (pl.n_splits > 1) {
-    const int R = p.S * (p.Hq / p.Hkv);
-    dim3 g2(R, p.B * p.Hkv);
-    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(p);
-    rc = launch_status("kv_combine");
+    rc = launch_combine<T, HD>(p, st);
   }
   return rc;
 }
@@ -458,8 +526,9 @@ size_t workspace_bytes_for(int n_splits, int B, int S, int Hq, int Hkv, int hd) 
 // on CUDA cores (thread = row) writes fp16 P to shared memory, O += P V on the
 // tensor core into TMEM (M=128 N=hd K=64).  The running max is kept stale until
 // it grows by more than 2^8, so O in TMEM is rescaled only then.  The new cache
-// rows are stored by a small copy kernel launched just before.  Partials use the
-// same workspace format and combine kernel as the mma.sync path.
+// rows are copied from k_new / v_new into the landed K/V tiles of every CTA whose
+// blocks hold them, and row-tile-0 CTAs store them into the cache.  Partials use
+// the same workspace format and combine kernel as the mma.sync path.
 constexpr int TC_KB = 64;  // keys per block
 
 struct KvTcMaps {
@@ -468,31 +537,12 @@ struct KvTcMaps {
 
 __device__ int g_kv_tc_error = 0;
 
-template <typename T>
-__global__ void kv_write_kernel(KvParams p, int HD) {
-  // one 16-byte chunk per thread: [b][kvh][s][hd/8] for K and V
-  const int per = HD / 8;
-  const long long n = (long long)p.B * p.Hkv * p.S * per;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < 2 * n; i += (long long)gridDim.x * blockDim.x) {
-    const int which = i >= n;
-    const long long e = which ? i - n : i;
-    const int c = (int)(e % per);
-    const long long rs = e / per;
-    const int s = (int)(rs % p.S);
-    const int bh = (int)(rs / p.S);
-    const int b = bh / p.Hkv, kvh = bh % p.Hkv;
-    const T* src = reinterpret_cast<const T*>(which ? p.v_new : p.k_new) + ((long long)bh * p.S + s) * HD + c * 8;
-    T* dst = reinterpret_cast<T*>(which ? p.vc : p.kc) + (long long)b * p.bs + (long long)kvh * p.hs +
-             (long long)(p.pos + s) * HD + c * 8;
-    *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
-  }
-}
-
 __device__ __forceinline__ uint32_t swz128(int r, int ch) { return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)); }
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(128, 1)
 kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
+  griddep_wait();
   constexpr int NKB = HD / 64;                 // 64-element column blocks of a row
   constexpr int Q_BLK = 128 * 128;             // [128 rows][128 B]
   constexpr int KV_BLK = TC_KB * 128;          // [64 keys][128 B]
@@ -577,6 +627,30 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     ok = __syncthreads_and(tc::mbar_wait(kvb0 + 8u * buf, (uint32_t)((j >> 1) & 1)));  // block-uniform
     if (!ok) break;
     pending = j + 1 < nblk ? j + 1 : -1;
+    const int key0 = k_begin + j * TC_KB;
+    if (p.has_new && key0 < p.pos + p.S && key0 + TC_KB > p.pos) {  // block-uniform
+      // the new rows of this block: from k_new / v_new into the landed tiles, and by row tile 0
+      // into the cache (other tiles of the split may have read those cache rows before or while
+      // they are written; their tiles are overwritten here as well)
+      const int j0 = max(key0, p.pos), j1 = min(min(key0 + TC_KB, k_end), p.pos + p.S);
+      const T* kn = reinterpret_cast<const T*>(p.k_new) + (long long)bh * p.S * HD;
+      const T* vn = reinterpret_cast<const T*>(p.v_new) + (long long)bh * p.S * HD;
+      T* Kc = reinterpret_cast<T*>(p.kc) + (long long)b * p.bs + (long long)kvh * p.hs;
+      T* Vc = reinterpret_cast<T*>(p.vc) + (long long)b * p.bs + (long long)kvh * p.hs;
+      for (int i = tid; i < (j1 - j0) * (HD / 8); i += 128) {
+        const int jj = j0 + i / (HD / 8), ch = i % (HD / 8), r = jj - key0;
+        const uint4 kv = *reinterpret_cast<const uint4*>(kn + (long long)(jj - p.pos) * HD + ch * 8);
+        const uint4 vv = *reinterpret_cast<const uint4*>(vn + (long long)(jj - p.pos) * HD + ch * 8);
+        *reinterpret_cast<uint4*>(sm + OFF_K + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = kv;
+        *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = vv;
+        if (tile == 0) {
+          *reinterpret_cast<uint4*>(Kc + (long long)jj * HD + ch * 8) = kv;
+          *reinterpret_cast<uint4*>(Vc + (long long)jj * HD + ch * 8) = vv;
+        }
+      }
+      tc::fence_async_smem();  // generic writes before the tensor core reads the tiles
+      __syncthreads();
+    }
     tc::fence_after();
     // S = Q K^T
     if (tid == 0) {
@@ -599,7 +673,6 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     tc::tmem_ld32(lane_addr + COL_SB + buf * 64, x);
     tc::tmem_ld32(lane_addr + COL_SB + buf * 64 + 32, x + 32);
     tc::tmem_wait_ld();
-    const int key0 = k_begin + j * TC_KB;
     float mb = -INFINITY;
     if (!p.mask) {
       // keys visible to this row form one interval of the block: [vlo, vhi]
@@ -697,6 +770,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   }
   if (!ok) atomicExch(&g_kv_tc_error, 1);
   if (pending >= 0 && !ok) tc::mbar_wait(kvb0 + 8u * (pending & 1), (uint32_t)((pending >> 1) & 1));
+  griddep_launch_dependents();
 
   // ---- epilogue: O rows leave through shared memory (the P tile) in 32-column slices, so
   //      that global stores are whole 128-byte row segments ----
@@ -802,6 +876,7 @@ struct DcLayout {
 template <typename T, int HD>
 __global__ void __launch_bounds__(128, 1)
 kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages) {
+  griddep_wait();
   using L = DcLayout<HD>;
   constexpr int NKB = L::NKB;
   constexpr int NTILE_O = HD / 8;
@@ -1034,6 +1109,7 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
     return;  // block-uniform: ok came from __syncthreads_and
   }
 
+  griddep_launch_dependents();
   // ---- merge the four warps' partial softmax states through shared memory ----
   if (t4 == 0) {
     s_m[warp][g] = m_run[0];
@@ -1173,14 +1249,10 @@ int launch_kv_dec(KvParams& p, const Plan& pl0, cudaStream_t st) {
   auto kern = kv_decode_kernel<T, HD>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(n_splits, p.B * p.Hkv);
-  kern<<<grid, 128, smem, st>>>(maps, q, stages);
-  rc = launch_status("kv_attention_decode");
+  rc = launch_pdl("kv_attention_decode", kern, grid, dim3(128), smem, st, maps, q, stages);
   if (rc) return rc;
   if (n_splits > 1) {
-    const int R = p.S * (p.Hq / p.Hkv);
-    dim3 g2(R, p.B * p.Hkv);
-    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(q);
-    rc = launch_status("kv_combine");
+    rc = launch_combine<T, HD>(q, st);
   }
   return rc;
 }
@@ -1218,26 +1290,15 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
     if (!rc) rc = kv_cache_maps(maps, p, HD);
     if (rc) return rc;
   }
-  if (p.has_new) {
-    const long long n = 2LL * p.B * p.Hkv * p.S * (HD / 8);
-    const int blocks = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
-    kv_write_kernel<T><<<blocks, 256, 0, st>>>(q, HD);
-    const int rc = launch_status("kv_cache_write");
-    if (rc) return rc;
-  }
   constexpr int NKB = HD / 64;
   const size_t smem = (size_t)NKB * 128 * 128 + 4 * (size_t)NKB * TC_KB * 128 + 128 * 128 + 1024;
   auto kern = kv_attn_tc_kernel<T, HD>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(row_tiles, n_splits, p.B * p.Hkv);
-  kern<<<grid, 128, smem, st>>>(maps, q);
-  int rc = launch_status("kv_attention_tc");
+  int rc = launch_pdl("kv_attention_tc", kern, grid, dim3(128), smem, st, maps, q);
   if (rc) return rc;
   if (n_splits > 1) {
-    const int R = p.S * (p.Hq / p.Hkv);
-    dim3 g2(R, p.B * p.Hkv);
-    kv_combine_kernel<T, HD><<<g2, HD, 0, st>>>(q);
-    rc = launch_status("kv_combine");
+    rc = launch_combine<T, HD>(q, st);
   }
   return rc;
 }
