@@ -4,32 +4,36 @@
 // tokens in order; the fp32 state S [d_k=128, d_v=128] lives in tensor memory
 // (TMEM) as S^T (lane = d_v index, column = d_k index) for the whole sequence
 // and leaves the SM only after the last chunk.  With G the in-chunk cumulative
-// log-decay and Gam[i,j] = exp(G_i - G_j), per chunk:
+// log-decay, Gam[i,j] = exp(G_i - G_j), and rq, rk the reciprocal l2 norms of
+// the q and k rows (1 when the caller normalised them already), per chunk:
 //
-//   D1   = [Q;K] K^T                         (tcgen05, M=128 N=64 K=128)
-//   P    = lower_incl(Q K^T * Gam)           (CUDA cores, fp16 to smem)
-//   A    = strict_lower(diag(beta) K K^T * Gam), T = (I + A)^-1   (CUDA cores, fp32, blockwise)
-//   U^T  = V^T (T diag(beta))^T              (tcgen05, M=128 N=64 K=64)
-//   W^T  = K^T (T diag(beta e^G))^T          (tcgen05, M=128 N=64 K=64)
-//   Vn^T = U^T - S^T W^T                     (tcgen05, A negated, accumulates on U)
-//   O1^T = S^T Q^T,  O2^T = Vn^T P^T         (tcgen05; O = diag(e^G) O1 + O2 at readout)
-//   S^T  = e^{G_c} S^T + (diag(e^{G_c - G}) Vn)^T K   (e^{G_c} applied in TMEM, then tcgen05)
+//   D1   = [Q;K] [Q;K]^T                          (tcgen05, M=128 N=128 K=128; its
+//                                                  diagonal gives the row norms)
+//   P    = lower_incl(rq rk^T (Q K^T) * Gam)      (CUDA cores, fp16 to smem)
+//   A    = strict_lower(diag(beta rk) K K^T diag(rk) * Gam)
+//   T    = (I + A)^-1: 16x16 diagonal blocks by forward substitution (fp32),
+//          16 -> 32 -> 64 merges T21 = -T22 (A21 T11) on mma.sync (fp16 operands)
+//   U^T  = V^T (T diag(beta))^T                   (tcgen05, M=128 N=64 K=64)
+//   W^T  = K^T (T diag(beta e^G rk))^T            (tcgen05)
+//   Vn^T = U^T - S^T W^T                          (tcgen05, A negated, accumulates on U)
+//   O1^T = S^T Q^T,  O2^T = Vn^T P^T              (tcgen05; O = diag(e^G rq) O1 + O2 at readout)
+//   S^T  = e^{G_c} S^T + (diag(e^{G_c - G} rk) Vn)^T K   (e^{G_c} applied in TMEM)
 //
-// Every product is arranged so that M = 128 (d_v or d_k on TMEM lanes).  All
-// operands are fp16 in 128-byte-swizzled shared memory; accumulators are fp32
-// in TMEM.  fp16 (10-bit mantissa) operands keep the result within 1e-3
-// relative L2 of an fp32 evaluation; bf16 inputs are converted to fp16 in
-// place.  The attention scale multiplies O in fp32 at the end (O is linear in q).
+// Operand precision.  q, k and v are used as they arrive (fp16 or bf16) — no
+// conversion pass.  The derived operands that multiply them, T diag(beta),
+// T diag(beta e^G rk) and the decayed Vn, are split into a hi and a lo part of
+// the input type (x = hi + lo, about 16 significant bits) and enter their
+// products as two accumulating MMAs; S^T and W^T are single-precision-of-the-
+// input-type operands; the Vn P^T product runs in fp16.  A CPU emulation of
+// every rounding point gives output rel-L2 ~3e-4 and state rel-L2 ~3e-6
+// against an fp64 recurrence (bf16 inputs, cfg0 distributions).
 //
-// Occupancy: two CTAs per SM (128 threads, 256 TMEM columns and ~109 KB of
-// shared memory each), so two heads' latency-bound phases interleave on the
-// SM.  Shared memory is reused phase by phase (see the map below).  q/k/v
-// tiles arrive by TMA (3-D tensor maps over [d, head, token], 64-token x
-// 64-element boxes, 128-byte swizzle done by the copy engine); the next chunk's
-// copies are issued as soon as the state update has released the tiles.
-// T = (I + A)^-1 is built blockwise: four 16x16 diagonal blocks by forward
-// substitution, then 16 -> 32 -> 64 merges T21 = -T22 (A21 T11) as small fp32
-// matrix products over all threads.
+// Occupancy: two CTAs per SM (128 threads, 256 TMEM columns and ~111 KB of
+// shared memory each).  Shared memory is reused phase by phase (map below).
+// q/k tiles and v tiles arrive by TMA on separate barriers (3-D tensor maps
+// over [d, head, token], 64-token x 64-element boxes, 128-byte swizzle): the
+// next chunk's v is requested once U has been formed, its q/k once the state
+// update has read k.
 //
 // Semantics: torch_chunk_gated_delta_rule of transformers 5.5.0
 // (modeling_qwen3_5.py:234-311); chunk (WY/UT) form of Yang et al. (2024).
@@ -50,31 +54,39 @@ constexpr int C = 64;
 constexpr int D = 128;
 constexpr int NT = 128;
 constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t COL_S = 0, COL_U = 128, COL_R = 192;  // U: U -> Vn -> O2;  R: D1 -> W -> O1
+// S^T: cols 0-127.  D1: cols 128-255.  Then U -> Vn -> O2 at 128-191, W -> O1 at 192-255.
+constexpr uint32_t COL_S = 0, COL_D1 = 128, COL_U = 128, COL_W = 192;
 
-// shared memory map (bytes from a 1024-byte aligned base) and lifetimes within a chunk:
-//   QK (TMA): rows 0-63 Q, 64-127 K                     [load .. S update]
-//   V  (TMA) V -> W [tok][d_k] -> Vn^T [d_v][tok]      (W after U/W, Vn after V'/O1)
-//   VD (dec Vn)^T                                       [Vn readout .. S update]
-//   P                                                   [P/A .. O2]
-//   X: A fp32 | T fp32 -> T1,T2 (over A) -> S^T fp16 (after U/W) -> O staging (after V'/O1)
+// Shared memory (bytes from a 1024-byte aligned base) and lifetimes within a chunk:
+//   QK (TMA)  rows 0-63 Q, 64-127 K, two 64-column blocks          [load .. state update]
+//   V  (TMA)  two 64-column blocks                                   [load .. U]
+//   P  fp16 [i][j]                                                   [P/A .. O2]
+//   R1 32 KB: T1 hi|lo, T2 hi|lo [i][j]  ->  S^T copy [d_v][d_k]  ->  decayed Vn hi|lo [d_v][tok]
+//   R2 16 KB: A fp16 | T fp16 [i][j]  ->  W^T [d_k][tok]  ->  Vn fp16 [d_v][tok]  ->  O staging [tok][d_v]
+//   AD fp32 diagonal 16x16 blocks of A
 constexpr int QK_BLK = 128 * 128;  // one 64-column block of a 128-row tile
 constexpr int T64_BLK = 64 * 128;  // one 64-column block of a 64-row tile
-constexpr int LDF = 68;            // fp32 row pitch (floats) of A and T
 constexpr int OFF_QK = 0;
 constexpr int OFF_V = OFF_QK + 2 * QK_BLK;
-constexpr int OFF_VD = OFF_V + 2 * T64_BLK;
-constexpr int OFF_P = OFF_VD + 2 * T64_BLK;
-constexpr int OFF_X = OFF_P + T64_BLK;
-constexpr int OFF_A = OFF_X, OFF_T = OFF_X + 64 * LDF * 4;
-constexpr int OFF_T1 = OFF_X, OFF_T2 = OFF_X + T64_BLK;
-constexpr int OFF_ST = OFF_X, OFF_OST = OFF_X;
-constexpr int OFF_GB = OFF_X + 2 * 64 * LDF * 4;  // raw g[64], beta[64]
-constexpr int OFF_MISC = OFF_GB + 128 * 4;        // G, beta, e^G, dec [64] each, gamma
-constexpr int SMEM_BYTES = OFF_MISC + 4 * 64 * 4 + 16 + 1024;
-constexpr uint32_t TILE_TX_BYTES = 2 * QK_BLK + 2 * T64_BLK;  // six 8 KB boxes per chunk
-static_assert(OFF_X % 1024 == 0 && OFF_V % 1024 == 0, "tile alignment");
-static_assert(2 * QK_BLK <= 2 * 64 * LDF * 4, "S^T must fit in the A|T region");
+constexpr int OFF_P = OFF_V + 2 * T64_BLK;
+constexpr int OFF_R1 = OFF_P + T64_BLK;
+constexpr int OFF_T1H = OFF_R1, OFF_T1L = OFF_R1 + T64_BLK, OFF_T2H = OFF_R1 + 2 * T64_BLK,
+              OFF_T2L = OFF_R1 + 3 * T64_BLK;
+constexpr int OFF_ST = OFF_R1;                          // [d_v 128][d_k] as two 64-column blocks
+constexpr int OFF_DH = OFF_R1, OFF_DL = OFF_R1 + QK_BLK;  // [d_v 128][tok 64]
+constexpr int OFF_R2 = OFF_R1 + 4 * T64_BLK;
+constexpr int OFF_A16 = OFF_R2, OFF_T16 = OFF_R2 + T64_BLK;
+constexpr int OFF_W = OFF_R2;    // W^T [d_k 128][tok 64], MN-major operand
+constexpr int OFF_VN = OFF_R2;   // Vn^T [d_v 128][tok 64]
+constexpr int OFF_OST = OFF_R2;  // [tok 64][d_v 128] 2-byte staging
+constexpr int OFF_AD = OFF_R2 + QK_BLK;
+constexpr int OFF_MISC = OFF_AD + 4 * 16 * 16 * 4;
+// MISC (floats): raw g[64] beta[64] | Gl, beta, e^G, dec, rq, rk, T2 column scale [64] each | gamma
+constexpr int M_GB = 0, M_GL = 128, M_BETA = 192, M_EG = 256, M_DEC = 320, M_RQ = 384, M_RK = 448, M_T2S = 512,
+              M_GAMMA = 576;
+constexpr int SMEM_BYTES = OFF_MISC + 580 * 4 + 1024;
+constexpr uint32_t QK_TX_BYTES = 2 * QK_BLK, V_TX_BYTES = 2 * T64_BLK;
+static_assert(OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && OFF_R1 % 1024 == 0 && OFF_R2 % 1024 == 0, "tile alignment");
 static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
 
 struct TileMaps {
@@ -86,21 +98,43 @@ __device__ int g_chunked_error = 0;
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` inside a 128-byte-row swizzled block
 // (the TMA 128-byte swizzle: chunk index XOR row index mod 8, 1024-byte aligned blocks)
 __device__ __forceinline__ uint32_t sw(int r, int ch) { return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)); }
+// byte offset of 2-byte element (r, c), c in 0..63
 __device__ __forceinline__ uint32_t sw_elem(int r, int c) { return sw(r, c >> 3) + (uint32_t)((c & 7) << 1); }
 
 template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& u, float* f) {
-  const T* h = reinterpret_cast<const T*>(&u);
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&u);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = to_f32(h[i]);
+  for (int i = 0; i < 4; ++i) w[i] = pack2<T>(f[2 * i], f[2 * i + 1]);
+  return u;
 }
 
-__device__ __forceinline__ uint4 pack8_f16(const float* f) {
-  uint4 u;
-  __half2* h = reinterpret_cast<__half2*>(&u);
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+// x = hi + lo with hi, lo of type T (lo = the rounding remainder of hi)
+template <typename T>
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  hi = pack2<T>(a, b);
+  const float2 h = unpack2<T>(hi);
+  lo = pack2<T>(a - h.x, b - h.y);
+}
+
+template <typename T>
+__device__ __forceinline__ void pack8_hilo(const float* f, uint4& hi, uint4& lo) {
+  uint32_t* h = reinterpret_cast<uint32_t*>(&hi);
+  uint32_t* l = reinterpret_cast<uint32_t*>(&lo);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-  return u;
+  for (int i = 0; i < 4; ++i) split2<T>(f[2 * i], f[2 * i + 1], h[i], l[i]);
 }
 
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
@@ -110,44 +144,12 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
-// Rewrite the chunk's tiles in place as fp16: convert from TIn, l2-normalise q
-// and k rows if asked, zero the rows at and past `nvalid`.
-template <typename TIn>
-__device__ __forceinline__ void convert_tiles(uint8_t* qk, uint8_t* vt, int nvalid, int l2norm, int tid) {
-  const int ch = tid & 15;
-  const int blk = ch >> 3, cb = ch & 7;
-#pragma unroll 1
-  for (int it = 0; it < 8; ++it) {
-    const int r = (tid >> 4) + it * 8;
-    uint4* pq = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(r, cb));
-    uint4* pk = reinterpret_cast<uint4*>(qk + blk * QK_BLK + sw(64 + r, cb));
-    uint4* pv = reinterpret_cast<uint4*>(vt + blk * T64_BLK + sw(r, cb));
-    float fq[8], fk[8], fv[8];
-    if (r < nvalid) {
-      unpack8<TIn>(*pq, fq);
-      unpack8<TIn>(*pk, fk);
-      unpack8<TIn>(*pv, fv);
-    } else {
+// lane-indexed element of a 32-register row (the diagonal of a 32x32 TMEM block)
+__device__ __forceinline__ float pick_lane(const float* r, int lane) {
+  float d = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) fq[i] = fk[i] = fv[i] = 0.f;
-    }
-    if (l2norm) {
-      float sq = 0.f, sk = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { sq += fq[i] * fq[i]; sk += fk[i] * fk[i]; }
-#pragma unroll
-      for (int o = 1; o < 16; o <<= 1) {
-        sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        sk += __shfl_xor_sync(0xffffffffu, sk, o);
-      }
-      const float rq = rsqrtf(sq + 1e-6f), rk = rsqrtf(sk + 1e-6f);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { fq[i] *= rq; fk[i] *= rk; }
-    }
-    *pq = pack8_f16(fq);
-    *pk = pack8_f16(fk);
-    *pv = pack8_f16(fv);
-  }
+  for (int e = 0; e < 32; ++e) d = e == lane ? r[e] : d;
+  return d;
 }
 
 template <typename TIn, typename TOut>
@@ -155,18 +157,21 @@ __global__ void __launch_bounds__(NT, 2)
 gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restrict__ g, const float* __restrict__ beta,
                    float* __restrict__ state, TOut* __restrict__ out, int T, int Hqk, int Hv, float scale,
                    int l2norm) {
+  constexpr bool kBF = std::is_same<TIn, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* sG = reinterpret_cast<float*>(sm + OFF_MISC);
-  float* sBeta = sG + 64;
-  float* sEG = sG + 128;
-  float* sDec = sG + 192;
-  float* sGamma = sG + 256;
-  float* sA = reinterpret_cast<float*>(sm + OFF_A);
-  float* sT = reinterpret_cast<float*>(sm + OFF_T);
-  const float* sGB = reinterpret_cast<const float*>(sm + OFF_GB);
-  __shared__ uint64_t mbar;  // tensor-core completions
-  __shared__ uint64_t tbar;  // TMA arrivals
+  float* misc = reinterpret_cast<float*>(sm + OFF_MISC);
+  float* sGB = misc + M_GB;
+  float* sGl = misc + M_GL;
+  float* sBeta = misc + M_BETA;
+  float* sEG = misc + M_EG;
+  float* sDec = misc + M_DEC;
+  float* sRq = misc + M_RQ;
+  float* sRk = misc + M_RK;
+  float* sT2s = misc + M_T2S;
+  float* sAd = reinterpret_cast<float*>(sm + OFF_AD);
+  __shared__ uint64_t mbar;           // tensor-core completions
+  __shared__ uint64_t qkbar, vbar;    // TMA arrivals of the q/k and v tiles
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -176,34 +181,39 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   const int hk = hv / (Hv / Hqk);
   const uint32_t sbase = tc::smem_u32(sm);
   const uint32_t bar = tc::smem_u32(&mbar);
-  const uint32_t tb = tc::smem_u32(&tbar);
+  const uint32_t qkb = tc::smem_u32(&qkbar), vb = tc::smem_u32(&vbar);
   const int nchunks = (T + C - 1) / C;
-  // fp16 inputs without l2-norm need no rewrite except for a ragged last chunk
-  const bool always_convert = !std::is_same<TIn, __half>::value || l2norm;
 
-  auto issue_loads = [&](int cc) {
+  auto issue_qk = [&](int cc) {
     const int tok0 = b * T + cc * C;
     if (tid == 0) {
-      tc::mbar_arrive_expect_tx(tb, TILE_TX_BYTES);
-      const uint32_t qk = sbase + OFF_QK, vt = sbase + OFF_V;
-      tc::tma_load_3d(qk, &maps.q, 0, hk, tok0, tb);
-      tc::tma_load_3d(qk + QK_BLK, &maps.q, 64, hk, tok0, tb);
-      tc::tma_load_3d(qk + 64 * 128, &maps.k, 0, hk, tok0, tb);
-      tc::tma_load_3d(qk + QK_BLK + 64 * 128, &maps.k, 64, hk, tok0, tb);
-      tc::tma_load_3d(vt, &maps.v, 0, hv, tok0, tb);
-      tc::tma_load_3d(vt + T64_BLK, &maps.v, 64, hv, tok0, tb);
+      tc::mbar_arrive_expect_tx(qkb, QK_TX_BYTES);
+      const uint32_t qk = sbase + OFF_QK;
+      tc::tma_load_3d(qk, &maps.q, 0, hk, tok0, qkb);
+      tc::tma_load_3d(qk + QK_BLK, &maps.q, 64, hk, tok0, qkb);
+      tc::tma_load_3d(qk + 64 * 128, &maps.k, 0, hk, tok0, qkb);
+      tc::tma_load_3d(qk + QK_BLK + 64 * 128, &maps.k, 64, hk, tok0, qkb);
     }
     const int r = tid & 63;
     if (cc * C + r < T) {
       const size_t idx = ((size_t)b * T + cc * C + r) * Hv + hv;
-      cp_async4(sm + OFF_GB + (tid >> 6) * 256 + r * 4, (tid >> 6) ? beta + idx : g + idx);
+      cp_async4(sGB + (tid >> 6) * 64 + r, (tid >> 6) ? beta + idx : g + idx);
     }
     cp_async_commit();
+  };
+  auto issue_v = [&](int cc) {
+    if (tid == 0) {
+      const int tok0 = b * T + cc * C;
+      tc::mbar_arrive_expect_tx(vb, V_TX_BYTES);
+      tc::tma_load_3d(sbase + OFF_V, &maps.v, 0, hv, tok0, vb);
+      tc::tma_load_3d(sbase + OFF_V + T64_BLK, &maps.v, 64, hv, tok0, vb);
+    }
   };
 
   if (tid == 0) {
     tc::mbar_init(&mbar, 1);
-    tc::mbar_init(&tbar, 1);
+    tc::mbar_init(&qkbar, 1);
+    tc::mbar_init(&vbar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
   }
@@ -214,11 +224,12 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
-  issue_loads(0);
+  issue_qk(0);
+  issue_v(0);
   const uint32_t tmem = tmem_slot;
   const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lane quarter
   uint32_t phase = 0;
-  int pending_chunk = 0;  // chunk whose tiles were requested and not yet waited for (-1: none)
+  int pending_qk = 0, pending_v = 0;  // chunk whose tiles were requested and not yet waited for (-1: none)
 
   // ---- initial state: thread d holds column d of S (row d of S^T) ----
   float* Sg = state + (size_t)bh * D * D;
@@ -251,20 +262,35 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     __syncthreads();
     tc::fence_after();
   };
+  constexpr uint32_t ID_D1 = tc::idesc_f16(128, 128, false, false, false, kBF);
+  constexpr uint32_t ID_UW = tc::idesc_f16(128, 64, true, false, false, kBF);
+  constexpr uint32_t ID_VN = tc::idesc_f16(128, 64, false, true, true, kBF);
+  constexpr uint32_t ID_O1 = tc::idesc_f16(128, 64, false, false, false, kBF);
+  constexpr uint32_t ID_O2 = tc::idesc_f16(128, 64, false, false, false, false);
+  constexpr uint32_t ID_SU = tc::idesc_f16(128, 128, false, true, false, kBF);
 
 #pragma unroll 1
   for (int c = 0; c < nchunks && !abort_flag; ++c) {
     const int t0 = c * C;
     const int nvalid = min(C, T - t0);
     // ---------------- tiles and gates of this chunk ----------------
-    if (!__syncthreads_and(tc::mbar_wait(tb, (uint32_t)(c & 1)))) {
+    if (!__syncthreads_and(tc::mbar_wait(qkb, (uint32_t)(c & 1)))) {
       fail();
       break;
     }
-    pending_chunk = -1;
+    pending_qk = -1;
     cp_async_wait<0>();
-    __syncthreads();
-    if (always_convert || nvalid < C) convert_tiles<TIn>(sm + OFF_QK, sm + OFF_V, nvalid, l2norm, tid);
+    // ---------------- D1 = [Q;K] [Q;K]^T (issued before the gates are formed) ----------------
+    if (tid == 0) {
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t koff = (uint32_t)((s >> 2) * QK_BLK + (s & 3) * 32);
+        const uint64_t d = tc::sdesc_sw128(sbase + OFF_QK + koff, 16, 1024);
+        tc::mma_f16(tmem + COL_D1, d, d, ID_D1, s > 0);
+      }
+      tc::commit(bar);
+    }
+    __syncthreads();  // raw g / beta of every thread visible
     if (warp == 0) {
       const int i0 = 2 * lane, i1 = 2 * lane + 1;
       const float g0 = i0 < nvalid ? sGB[i0] : 0.f, g1 = i1 < nvalid ? sGB[i1] : 0.f;
@@ -275,204 +301,287 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         const float n = __shfl_up_sync(0xffffffffu, s, o);
         if (lane >= o) s += n;
       }
-      const float G1 = s, G0 = s - g1;
-      const float Glast = __shfl_sync(0xffffffffu, G1, 31);
-      sG[i0] = G0;
-      sG[i1] = G1;
+      constexpr float L2E = 1.4426950408889634f;
+      const float Gl1 = s * L2E, Gl0 = (s - g1) * L2E;
+      const float Gll = __shfl_sync(0xffffffffu, Gl1, 31);
+      sGl[i0] = Gl0;
+      sGl[i1] = Gl1;
       sBeta[i0] = b0;
       sBeta[i1] = b1;
-      sEG[i0] = __expf(G0);
-      sEG[i1] = __expf(G1);
-      sDec[i0] = __expf(Glast - G0);
-      sDec[i1] = __expf(Glast - G1);
-      if (lane == 0) *sGamma = __expf(Glast);
-    }
-    sync_smem_for_mma();
-
-    // ---------------- D1 = [Q;K] K^T ----------------
-    if (tid == 0) {
-      constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t koff = (uint32_t)((s >> 2) * QK_BLK + (s & 3) * 32);
-        const uint64_t ad = tc::sdesc_sw128(sbase + OFF_QK + koff, 16, 1024);
-        const uint64_t bd = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + koff, 16, 1024);
-        tc::mma_f16(tmem + COL_R, ad, bd, id, s > 0);
+      sEG[i0] = fast_exp2(Gl0);
+      sEG[i1] = fast_exp2(Gl1);
+      sDec[i0] = fast_exp2(Gll - Gl0);
+      sDec[i1] = fast_exp2(Gll - Gl1);
+      if (lane == 0) misc[M_GAMMA] = fast_exp2(Gll);
+      if (!l2norm) {
+        sRq[i0] = sRq[i1] = 1.f;
+        sRk[i0] = sRk[i1] = 1.f;
+        sT2s[i0] = b0 * fast_exp2(Gl0);
+        sT2s[i1] = b1 * fast_exp2(Gl1);
       }
-      tc::commit(bar);
     }
-    if (!sync_mma()) break;
+    if (!sync_mma()) break;  // D1 done; gates visible
 
     // ---------------- P (rows 0-63), A (rows 64-127) ----------------
     {
+      const bool qrow = tid < 64;
       const int i = tid & 63;
-      const float Gi = sG[i];
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_R, r0);
-      tc::tmem_ld32(lane_addr + COL_R + 32, r1);
-      tc::tmem_wait_ld();
-      if (tid < 64) {
+      float r0[32], r1[32];  // columns 64-127 of D1: row . k_j
+      tc::tmem_ld32(lane_addr + COL_D1 + 64, r0);
+      tc::tmem_ld32(lane_addr + COL_D1 + 96, r1);
+      if (l2norm) {
+        float rn;
+        if (qrow) {  // |q_i|^2 sits in column i of the QQ^T block
+          float rd[32];
+          tc::tmem_ld32(lane_addr + COL_D1 + (warp & 1) * 32, rd);
+          tc::tmem_wait_ld();
+          rn = rsqrtf(pick_lane(rd, lane) + 1e-6f);
+          sRq[i] = rn;
+        } else {  // |k_i|^2 sits in column 64 + i
+          tc::tmem_wait_ld();
+          rn = rsqrtf(pick_lane((warp & 1) ? r1 : r0, lane) + 1e-6f);
+          sRk[i] = rn;
+        }
+        __syncthreads();
+        if (!qrow) sT2s[i] = sBeta[i] * sEG[i] * rn;
+      } else {
+        tc::tmem_wait_ld();
+      }
+      const float Gi = sGl[i];
+      // column groups of 8 that lie wholly above this warp's rows are zero
+      const int cb_end = (warp & 1) ? 8 : 4;
+      if (qrow) {
+        const float rqi = sRq[i];
 #pragma unroll
         for (int cb = 0; cb < 8; ++cb) {
-          const float4 ga = ld4(sG + cb * 8), gb = ld4(sG + cb * 8 + 4);
-          const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
           float p8[8];
+          if (cb < cb_end) {
+            const float4 ga = ld4(sGl + cb * 8), gb = ld4(sGl + cb * 8 + 4);
+            const float4 ka = ld4(sRk + cb * 8), kb = ld4(sRk + cb * 8 + 4);
+            const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+            const float rkj[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int j = cb * 8 + e;
-            const float x = j < 32 ? r0[j] : r1[j - 32];
-            p8[e] = j <= i ? x * __expf(Gi - gj[e]) : 0.f;
+            for (int e = 0; e < 8; ++e) {
+              const int j = cb * 8 + e;
+              const float x = j < 32 ? r0[j] : r1[j - 32];
+              p8[e] = j <= i ? x * rqi * rkj[e] * fast_exp2(Gi - gj[e]) : 0.f;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) p8[e] = 0.f;
           }
-          *reinterpret_cast<uint4*>(sm + OFF_P + sw(i, cb)) = pack8_f16(p8);
+          *reinterpret_cast<uint4*>(sm + OFF_P + sw(i, cb)) = pack8<__half>(p8);
         }
       } else {
-        const float bi = sBeta[i];
-        float* arow = sA + i * LDF;
+        const float bi = sBeta[i] * sRk[i];
+        const int blk = i >> 4;
 #pragma unroll
-        for (int j4 = 0; j4 < 16; ++j4) {
-          const float4 g4 = ld4(sG + j4 * 4);
-          const float gj[4] = {g4.x, g4.y, g4.z, g4.w};
-          float a4[4];
+        for (int cb = 0; cb < 8; ++cb) {
+          float a8[8];
+          if (cb < cb_end) {
+            const float4 ga = ld4(sGl + cb * 8), gb = ld4(sGl + cb * 8 + 4);
+            const float4 ka = ld4(sRk + cb * 8), kb = ld4(sRk + cb * 8 + 4);
+            const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+            const float rkj[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int j = j4 * 4 + e;
-            const float x = j < 32 ? r0[j] : r1[j - 32];
-            a4[e] = j < i ? bi * x * __expf(Gi - gj[e]) : 0.f;
+            for (int e = 0; e < 8; ++e) {
+              const int j = cb * 8 + e;
+              const float x = j < 32 ? r0[j] : r1[j - 32];
+              a8[e] = j < i ? bi * x * rkj[e] * fast_exp2(Gi - gj[e]) : 0.f;
+            }
+            if ((cb >> 1) == blk) {  // the diagonal 16x16 block, fp32, for the substitution
+              float* ad = sAd + blk * 256 + (i & 15) * 16 + (cb & 1) * 8;
+              *reinterpret_cast<float4*>(ad) = make_float4(a8[0], a8[1], a8[2], a8[3]);
+              *reinterpret_cast<float4*>(ad + 4) = make_float4(a8[4], a8[5], a8[6], a8[7]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a8[e] = 0.f;
           }
-          *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(a4[0], a4[1], a4[2], a4[3]);
+          *reinterpret_cast<uint4*>(sm + OFF_A16 + sw(i, cb)) = pack8<__half>(a8);
         }
       }
     }
-    tc::fence_before();
     __syncthreads();
 
-    // ---------------- T = (I + A)^-1, blockwise ----------------
-    // (1) diagonal 16x16 blocks: thread (blk, j) solves column j by right-looking substitution;
-    //     the upper blocks T[0:16,16:32] and T[32:48,48:64] that the merges read are zeroed
-    {
-      const int z = tid * 4, sel = z >> 8, w = z & 255;
-      const int zr = (sel ? 32 : 0) + (w >> 4), zc = (sel ? 48 : 16) + (w & 15);
-      *reinterpret_cast<float4*>(sT + zr * LDF + zc) = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
+    // ---------------- T = (I + A)^-1 -> T1 = T diag(beta), T2 = T diag(beta e^G rk), hi|lo ----------------
+    // (1) threads 0-63: diagonal 16x16 blocks, thread (blk, j) solves column j by right-looking
+    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-127 zero the
+    //     strictly upper blocks of T1, T2 and the two upper blocks of T that the merges read
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
+      const float* ab = sAd + (tid >> 4) * 256;
       float xs[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) xs[i] = i == j ? 1.f : 0.f;
+      for (int r = 0; r < 16; ++r) xs[r] = r == j ? 1.f : 0.f;
 #pragma unroll
       for (int kk = 0; kk < 15; ++kk) {
         const float xk = xs[kk];
 #pragma unroll
-        for (int i = kk + 1; i < 16; ++i) xs[i] -= sA[(o + i) * LDF + o + kk] * xk;
+        for (int r = kk + 1; r < 16; ++r) xs[r] -= ab[r * 16 + kk] * xk;
       }
+      const int col = o + j;
+      const float s1 = sBeta[col], s2 = sT2s[col];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) sT[(o + i) * LDF + o + j] = xs[i];
-    }
-    __syncthreads();
-    // (2) 16 -> 32: X = A_{r,c} T_{c,c} (kept in A's unused upper block), T_{r,c} = -T_{r,r} X
-    {
-      const int m = tid >> 6, idx = tid & 63, r = idx >> 2, c0 = (idx & 3) * 4;
-      const int ro = m ? 48 : 16, co = m ? 32 : 0;  // block rows ro.., block cols co..
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kk = 0; kk < 16; ++kk) {
-        const float a = sA[(ro + r) * LDF + co + kk];
-        const float4 t4 = ld4(sT + (co + kk) * LDF + co + c0);
-        acc[0] += a * t4.x; acc[1] += a * t4.y; acc[2] += a * t4.z; acc[3] += a * t4.w;
+      for (int r = 0; r < 16; ++r) {
+        const uint32_t off = sw_elem(o + r, col);
+        *reinterpret_cast<__half*>(sm + OFF_T16 + off) = __float2half_rn(xs[r]);
+        const float v1 = xs[r] * s1, v2 = xs[r] * s2;
+        const TIn h1 = from_f32<TIn>(v1), h2 = from_f32<TIn>(v2);
+        *reinterpret_cast<TIn*>(sm + OFF_T1H + off) = h1;
+        *reinterpret_cast<TIn*>(sm + OFF_T1L + off) = from_f32<TIn>(v1 - to_f32(h1));
+        *reinterpret_cast<TIn*>(sm + OFF_T2H + off) = h2;
+        *reinterpret_cast<TIn*>(sm + OFF_T2L + off) = from_f32<TIn>(v2 - to_f32(h2));
       }
-      *reinterpret_cast<float4*>(sA + (ro - 16 + r) * LDF + co + 16 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      __syncthreads();
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 16; ++kk) {
-        const float t = sT[(ro + r) * LDF + ro + kk];
-        const float4 x4 = ld4(sA + (ro - 16 + kk) * LDF + co + 16 + c0);
-        acc[0] += t * x4.x; acc[1] += t * x4.y; acc[2] += t * x4.z; acc[3] += t * x4.w;
-      }
-      *reinterpret_cast<float4*>(sT + (ro + r) * LDF + co + c0) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
-    }
-    __syncthreads();
-    // (3) 32 -> 64: Y = A[32:64, 0:32] T[0:32, 0:32] (kept in A[0:32, 32:64]); T[32:64, 0:32] = -T[32:64, 32:64] Y
-    {
-      const int r = tid >> 2, c0 = (tid & 3) * 8;
-      float acc[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll 8
-      for (int kk = 0; kk < 32; ++kk) {
-        const float a = sA[(32 + r) * LDF + kk];
-        const float4 t0 = ld4(sT + kk * LDF + c0), t1 = ld4(sT + kk * LDF + c0 + 4);
-        acc[0] += a * t0.x; acc[1] += a * t0.y; acc[2] += a * t0.z; acc[3] += a * t0.w;
-        acc[4] += a * t1.x; acc[5] += a * t1.y; acc[6] += a * t1.z; acc[7] += a * t1.w;
-      }
-      *reinterpret_cast<float4*>(sA + r * LDF + 32 + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      *reinterpret_cast<float4*>(sA + r * LDF + 36 + c0) = make_float4(acc[4], acc[5], acc[6], acc[7]);
-      __syncthreads();
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll 8
-      for (int kk = 0; kk < 32; ++kk) {
-        const float t = sT[(32 + r) * LDF + 32 + kk];
-        const float4 y0 = ld4(sA + kk * LDF + 32 + c0), y1 = ld4(sA + kk * LDF + 36 + c0);
-        acc[0] += t * y0.x; acc[1] += t * y0.y; acc[2] += t * y0.z; acc[3] += t * y0.w;
-        acc[4] += t * y1.x; acc[5] += t * y1.y; acc[6] += t * y1.z; acc[7] += t * y1.w;
-      }
-      *reinterpret_cast<float4*>(sT + (32 + r) * LDF + c0) = make_float4(-acc[0], -acc[1], -acc[2], -acc[3]);
-      *reinterpret_cast<float4*>(sT + (32 + r) * LDF + c0 + 4) = make_float4(-acc[4], -acc[5], -acc[6], -acc[7]);
-    }
-    __syncthreads();
-    // T1 = T diag(beta), T2 = T diag(beta e^G): fp16, swizzled, over A's (now dead) storage
-    {
-      const int r = tid >> 1, cq = (tid & 1) * 4;  // four 8-column chunks per thread
-#pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        const int c8 = (cq + cb) * 8;
-        const float4 ta = ld4(sT + r * LDF + c8), tb4 = ld4(sT + r * LDF + c8 + 4);
-        const float4 ba = ld4(sBeta + c8), bb = ld4(sBeta + c8 + 4);
-        const float4 ea = ld4(sEG + c8), eb = ld4(sEG + c8 + 4);
-        const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb4.x, tb4.y, tb4.z, tb4.w};
-        const float bv[8] = {ba.x, ba.y, ba.z, ba.w, bb.x, bb.y, bb.z, bb.w};
-        const float ev[8] = {ea.x, ea.y, ea.z, ea.w, eb.x, eb.y, eb.z, eb.w};
-        float t1[8], t2[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float t = c8 + e <= r ? tv[e] : 0.f;
-          t1[e] = t * bv[e];
-          t2[e] = t1[e] * ev[e];
+    } else {
+      // upper blocks of T1, T2 (hi, lo): rows 0-15 cols 16-63, rows 16-31 cols 32-63, rows 32-47 cols 48-63,
+      // i.e. 16-byte chunks (r, ch) with ch >= 2 * (r / 16 + 1); plus T blocks (0,1) and (2,3)
+      const int u = tid - 64;
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll 1
+      for (int idx = u; idx < 48 * 8; idx += 64) {
+        const int r = idx >> 3, ch = idx & 7;
+        if (ch >= 2 * ((r >> 4) + 1)) {
+          const uint32_t off = sw(r, ch);
+          *reinterpret_cast<uint4*>(sm + OFF_T1H + off) = z;
+          *reinterpret_cast<uint4*>(sm + OFF_T1L + off) = z;
+          *reinterpret_cast<uint4*>(sm + OFF_T2H + off) = z;
+          *reinterpret_cast<uint4*>(sm + OFF_T2L + off) = z;
         }
-        *reinterpret_cast<uint4*>(sm + OFF_T1 + sw(r, cq + cb)) = pack8_f16(t1);
-        *reinterpret_cast<uint4*>(sm + OFF_T2 + sw(r, cq + cb)) = pack8_f16(t2);
+      }
+      {
+        const int r = (u >> 1) & 15, ch = ((u >> 5) ? 6 : 2) + (u & 1), ro = (u >> 5) ? 32 : 0;
+        *reinterpret_cast<uint4*>(sm + OFF_T16 + sw(ro + r, ch)) = z;
       }
     }
+    __syncthreads();
+    const int g8 = lane >> 2, t4 = lane & 3;  // mma.sync fragment coordinates
+    // (2) 16 -> 32 (warps 0, 1: blocks (1,0) and (3,2)):  X^T = T_cc^T A_rc^T,  T_rc = -T_rr X
+    if (warp < 2) {
+      const int rr0 = warp ? 48 : 16, cc0 = warp ? 32 : 0;
+      uint32_t at[4], bA[4], aR[4];
+      ldmatrix_x4_trans(at, sm + OFF_T16 + sw(cc0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
+      ldmatrix_x4(bA, sm + OFF_A16 + sw(rr0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
+      ldmatrix_x4(aR, sm + OFF_T16 + sw(rr0 + (lane & 15), (rr0 >> 3) + (lane >> 4)));
+      float xt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      mma_16816<__half>(xt[0], at, bA[0], bA[1]);
+      mma_16816<__half>(xt[1], at, bA[2], bA[3]);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t b0 = pack2<__half>(xt[0][2 * nt], xt[0][2 * nt + 1]);
+        const uint32_t b1 = pack2<__half>(xt[1][2 * nt], xt[1][2 * nt + 1]);
+        mma_16816<__half>(o4, aR, b0, b1);
+        const int col = cc0 + 8 * nt + 2 * t4;
+        const float s1a = sBeta[col], s1b = sBeta[col + 1], s2a = sT2s[col], s2b = sT2s[col + 1];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float va = -o4[2 * hh], vb = -o4[2 * hh + 1];
+          const uint32_t off = sw_elem(rr0 + g8 + 8 * hh, col);
+          *reinterpret_cast<uint32_t*>(sm + OFF_T16 + off) = pack2<__half>(va, vb);
+          uint32_t hi, lo;
+          split2<TIn>(va * s1a, vb * s1b, hi, lo);
+          *reinterpret_cast<uint32_t*>(sm + OFF_T1H + off) = hi;
+          *reinterpret_cast<uint32_t*>(sm + OFF_T1L + off) = lo;
+          split2<TIn>(va * s2a, vb * s2b, hi, lo);
+          *reinterpret_cast<uint32_t*>(sm + OFF_T2H + off) = hi;
+          *reinterpret_cast<uint32_t*>(sm + OFF_T2L + off) = lo;
+        }
+      }
+    }
+    __syncthreads();
+    // (3) 32 -> 64 (all warps; warp = (row half mt, column half nh) of T[32:64, 0:32]):
+    //     Y^T = T00^T A10^T (rows nh*16.. of Y^T), T[32+16mt.., 16nh..] = -T11 Y
+    {
+      const int nh = warp & 1, mt = warp >> 1;
+      float yt[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) yt[n][0] = yt[n][1] = yt[n][2] = yt[n][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t at[4];
+        ldmatrix_x4_trans(at, sm + OFF_T16 + sw(16 * ks + (lane & 7) + ((lane >> 4) << 3), 2 * nh + ((lane >> 3) & 1)));
+#pragma unroll
+        for (int ap = 0; ap < 2; ++ap) {
+          uint32_t bA[4];
+          ldmatrix_x4(bA, sm + OFF_A16 + sw(32 + 16 * ap + (lane & 7) + ((lane >> 4) << 3), 2 * ks + ((lane >> 3) & 1)));
+          mma_16816<__half>(yt[2 * ap], at, bA[0], bA[1]);
+          mma_16816<__half>(yt[2 * ap + 1], at, bA[2], bA[3]);
+        }
+      }
+      float o4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        uint32_t aR[4];
+        ldmatrix_x4(aR, sm + OFF_T16 + sw(32 + 16 * mt + (lane & 15), 4 + 2 * ks + (lane >> 4)));
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const uint32_t b0 = pack2<__half>(yt[2 * ks][2 * nt], yt[2 * ks][2 * nt + 1]);
+          const uint32_t b1 = pack2<__half>(yt[2 * ks + 1][2 * nt], yt[2 * ks + 1][2 * nt + 1]);
+          mma_16816<__half>(o4[nt], aR, b0, b1);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int col = 16 * nh + 8 * nt + 2 * t4;
+        const float s1a = sBeta[col], s1b = sBeta[col + 1], s2a = sT2s[col], s2b = sT2s[col + 1];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float va = -o4[nt][2 * hh], vb = -o4[nt][2 * hh + 1];
+          const uint32_t off = sw_elem(32 + 16 * mt + g8 + 8 * hh, col);
+          uint32_t hi, lo;
+          split2<TIn>(va * s1a, vb * s1b, hi, lo);
+          *reinterpret_cast<uint32_t*>(sm + OFF_T1H + off) = hi;
+          *reinterpret_cast<uint32_t*>(sm + OFF_T1L + off) = lo;
+          split2<TIn>(va * s2a, vb * s2b, hi, lo);
+          *reinterpret_cast<uint32_t*>(sm + OFF_T2H + off) = hi;
+          *reinterpret_cast<uint32_t*>(sm + OFF_T2L + off) = lo;
+        }
+      }
+    }
+    // v of this chunk must have landed before U
+    if (!__syncthreads_and(tc::mbar_wait(vb, (uint32_t)(c & 1)))) {
+      fail();
+      break;
+    }
+    pending_v = -1;
     sync_smem_for_mma();
 
-    // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T ----------------
+    // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T (hi and lo parts) ----------------
     if (tid == 0) {
-      constexpr uint32_t id = tc::idesc_f16(128, 64, true, false);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 2048, T64_BLK, 1024);
-        const uint64_t b1 = tc::sdesc_sw128(sbase + OFF_T1 + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_U, av, b1, id, s > 0);
-        const uint64_t ak = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
-        const uint64_t b2 = tc::sdesc_sw128(sbase + OFF_T2 + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_R, ak, b2, id, s > 0);
+      for (int part = 0; part < 2; ++part) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 2048, T64_BLK, 1024);
+          const uint64_t b1 = tc::sdesc_sw128(sbase + (part ? OFF_T1L : OFF_T1H) + s * 32, 16, 1024);
+          tc::mma_f16(tmem + COL_U, av, b1, ID_UW, part > 0 || s > 0);
+          const uint64_t ak = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
+          const uint64_t b2 = tc::sdesc_sw128(sbase + (part ? OFF_T2L : OFF_T2H) + s * 32, 16, 1024);
+          tc::mma_f16(tmem + COL_W, ak, b2, ID_UW, part > 0 || s > 0);
+        }
       }
       tc::commit(bar);
     }
     if (!sync_mma()) break;
+    // v is free: request the next chunk's v tile
+    if (c + 1 < nchunks) {
+      issue_v(c + 1);
+      pending_v = c + 1;
+    }
 
-    // ---------------- W readout (into the V region) and state readout (into X) ----------------
+    // ---------------- W^T readout (MN-major operand) and S^T readout (copy, then S^T *= gamma) ----------------
     {
       float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_R, r0);
-      tc::tmem_ld32(lane_addr + COL_R + 32, r1);
+      tc::tmem_ld32(lane_addr + COL_W, r0);
+      tc::tmem_ld32(lane_addr + COL_W + 32, r1);
       tc::tmem_wait_ld();
-      uint8_t* wb = sm + OFF_V + (tid >> 6) * T64_BLK;  // W [token][d_k], two 64-column blocks
 #pragma unroll
-      for (int t = 0; t < 64; ++t)
-        *reinterpret_cast<__half*>(wb + sw_elem(t, tid & 63)) = __float2half_rn(t < 32 ? r0[t] : r1[t - 32]);
-      const float gamma = *sGamma;
+      for (int cb = 0; cb < 4; ++cb) {
+        *reinterpret_cast<uint4*>(sm + OFF_W + sw(tid, cb)) = pack8<TIn>(r0 + cb * 8);
+        *reinterpret_cast<uint4*>(sm + OFF_W + sw(tid, cb + 4)) = pack8<TIn>(r1 + cb * 8);
+      }
+      const float gamma = misc[M_GAMMA];
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
         float s32[32];
@@ -481,7 +590,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
           const int kc = j * 4 + cb;  // 16-byte chunk index 0..15 along d_k
-          *reinterpret_cast<uint4*>(sm + OFF_ST + (kc >> 3) * QK_BLK + sw(tid, kc & 7)) = pack8_f16(s32 + cb * 8);
+          *reinterpret_cast<uint4*>(sm + OFF_ST + (kc >> 3) * QK_BLK + sw(tid, kc & 7)) = pack8<TIn>(s32 + cb * 8);
         }
 #pragma unroll
         for (int e = 0; e < 32; ++e) s32[e] *= gamma;
@@ -493,21 +602,19 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- Vn^T = U^T - S^T W^T ; O1^T = S^T Q^T ----------------
     if (tid == 0) {
-      constexpr uint32_t idn = tc::idesc_f16(128, 64, false, false, true);
-      constexpr uint32_t id = tc::idesc_f16(128, 64, false, false);
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint64_t as = tc::sdesc_sw128(sbase + OFF_ST + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
-        const uint64_t bw = tc::sdesc_sw128(sbase + OFF_V + (s >> 2) * T64_BLK + (s & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_U, as, bw, idn, 1);
+        const uint64_t bw = tc::sdesc_sw128(sbase + OFF_W + s * 2048, 8192, 1024);
+        tc::mma_f16(tmem + COL_U, as, bw, ID_VN, 1);
         const uint64_t bq = tc::sdesc_sw128(sbase + OFF_QK + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_R, as, bq, id, s > 0);
+        tc::mma_f16(tmem + COL_W, as, bq, ID_O1, s > 0);
       }
       tc::commit(bar);
     }
     if (!sync_mma()) break;
 
-    // ---------------- Vn readout: lane = d_v index, columns = tokens ----------------
+    // ---------------- Vn readout: Vn (fp16) and the decayed Vn diag(dec rk) (hi|lo) ----------------
     {
       float r0[32], r1[32];
       tc::tmem_ld32(lane_addr + COL_U, r0);
@@ -517,62 +624,72 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       for (int cb = 0; cb < 8; ++cb) {
         float x[8], y[8];
         const float4 d0 = ld4(sDec + cb * 8), d1 = ld4(sDec + cb * 8 + 4);
-        const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+        const float4 k0 = ld4(sRk + cb * 8), k1 = ld4(sRk + cb * 8 + 4);
+        const float dd[8] = {d0.x * k0.x, d0.y * k0.y, d0.z * k0.z, d0.w * k0.w,
+                             d1.x * k1.x, d1.y * k1.y, d1.z * k1.z, d1.w * k1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int t = cb * 8 + e;
           x[e] = t < 32 ? r0[t] : r1[t - 32];
           y[e] = x[e] * dd[e];
         }
-        *reinterpret_cast<uint4*>(sm + OFF_V + sw(tid, cb)) = pack8_f16(x);
-        *reinterpret_cast<uint4*>(sm + OFF_VD + sw(tid, cb)) = pack8_f16(y);
+        *reinterpret_cast<uint4*>(sm + OFF_VN + sw(tid, cb)) = pack8<__half>(x);
+        uint4 hi, lo;
+        pack8_hilo<TIn>(y, hi, lo);
+        *reinterpret_cast<uint4*>(sm + OFF_DH + sw(tid, cb)) = hi;
+        *reinterpret_cast<uint4*>(sm + OFF_DL + sw(tid, cb)) = lo;
       }
     }
     sync_smem_for_mma();
 
-    // ---------------- O2^T = Vn^T P^T (into U's columns) ; S^T += (dec Vn)^T K ----------------
+    // ---------------- O2^T = Vn^T P^T (into U's columns) ; S^T += (dec Vn)^T K (hi and lo) ----------------
     if (tid == 0) {
-      constexpr uint32_t id64 = tc::idesc_f16(128, 64, false, false);
-      constexpr uint32_t id128 = tc::idesc_f16(128, 128, false, true);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 32, 16, 1024);
+        const uint64_t av = tc::sdesc_sw128(sbase + OFF_VN + s * 32, 16, 1024);
         const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_U, av, bp, id64, s > 0);
-        const uint64_t ad = tc::sdesc_sw128(sbase + OFF_VD + s * 32, 16, 1024);
-        const uint64_t bk = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
-        tc::mma_f16(tmem + COL_S, ad, bk, id128, 1);
+        tc::mma_f16(tmem + COL_U, av, bp, ID_O2, s > 0);
+      }
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint64_t ad = tc::sdesc_sw128(sbase + (part ? OFF_DL : OFF_DH) + s * 32, 16, 1024);
+          const uint64_t bk = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
+          tc::mma_f16(tmem + COL_S, ad, bk, ID_SU, 1);
+        }
       }
       tc::commit(bar);
     }
     if (!sync_mma()) break;
-    // the tiles are free: start the next chunk's copies while O drains
+    // q/k are free: start the next chunk's copies while O drains
     if (c + 1 < nchunks) {
-      issue_loads(c + 1);
-      pending_chunk = c + 1;
+      issue_qk(c + 1);
+      pending_qk = c + 1;
     }
 
-    // ---------------- O = (e^G O1 + O2) * scale -> global ----------------
+    // ---------------- O = (e^G rq O1 + O2) * scale -> global ----------------
     {
       float o1[32], o2[32];
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
-        tc::tmem_ld32(lane_addr + COL_R + hh * 32, o1);
+        tc::tmem_ld32(lane_addr + COL_W + hh * 32, o1);
         tc::tmem_ld32(lane_addr + COL_U + hh * 32, o2);
         tc::tmem_wait_ld();
         if constexpr (sizeof(TOut) == 2) {
-          TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging over X
+          TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int tt = hh * 32 + t;
-            ost[tt * D + tid] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
+            ost[tt * D + tid] = from_f32<TOut>((sEG[tt] * sRq[tt] * o1[t] + o2[t]) * scale);
           }
         } else {
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int tt = hh * 32 + t;
             if (tt < nvalid)
-              out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + tid] = from_f32<TOut>((sEG[tt] * o1[t] + o2[t]) * scale);
+              out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + tid] =
+                  from_f32<TOut>((sEG[tt] * sRq[tt] * o1[t] + o2[t]) * scale);
           }
         }
       }
@@ -594,7 +711,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
   cp_async_wait<0>();
   // a stopped CTA still lets the tiles it requested land before it leaves (bounded)
-  if (pending_chunk >= 0) tc::mbar_wait(tb, (uint32_t)(pending_chunk & 1));
+  if (pending_qk >= 0) tc::mbar_wait(qkb, (uint32_t)(pending_qk & 1));
+  if (pending_v >= 0) tc::mbar_wait(vb, (uint32_t)(pending_v & 1));
   // ---- final state ----
   if (!abort_flag) {
     float buf[32];

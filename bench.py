@@ -323,7 +323,7 @@ def bench_gdn_prefill(args, ws, rank, local):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f16 tensor-core operands, f32 accumulate/state, bf16 in/out",
+        "dtype": "bf16 (inputs as tensor-core operands; derived operands split hi+lo), f32 accumulate/state, bf16 in/out",
         "data": "synthetic (seeded on device; q/k l2-normalised N(0,1), v ~N(0,1))",
         "config": {"workload": "gdn_chunked_prefill", "batch": nseq, "seq_len": seqlen, "chunk": CHUNK,
                    "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV,
