@@ -16,7 +16,8 @@
 //   U^T  = V^T (T diag(beta))^T                   (tcgen05, M=128 N=64 K=64)
 //   W^T  = K^T (T diag(beta e^G rk))^T            (tcgen05)
 //   Vn^T = U^T - S^T W^T                          (tcgen05, A negated, accumulates on U)
-//   O1^T = S^T Q^T,  O2^T = Vn^T P^T              (tcgen05; O = diag(e^G rq) O1 + O2 at readout)
+//   O1^T = S^T Q^T,  O2^T = Vn^T P^T              (tcgen05; O = diag(e^G rq) O1 + O2 at readout,
+//                                                  the attention scale folded into P and the O1 factor)
 //   S^T  = e^{G_c} S^T + (diag(e^{G_c - G} rk) Vn)^T K   (e^{G_c} applied in TMEM)
 //
 // Operand precision.  q, k and v are used as they arrive (fp16 or bf16) — no
@@ -80,14 +81,20 @@ constexpr int OFF_W = OFF_R2;    // W^T [d_k 128][tok 64], MN-major operand
 constexpr int OFF_VN = OFF_R2;   // Vn^T [d_v 128][tok 64]
 constexpr int OFF_OST = OFF_R2;  // [tok 64][d_v 128] 2-byte staging
 constexpr int OFF_AD = OFF_R2 + QK_BLK;
-constexpr int OFF_MISC = OFF_AD + 4 * 16 * 16 * 4;
-// MISC (floats): raw g[64] beta[64] | Gl, beta, e^G, dec, rq, rk, T2 column scale [64] each | gamma
-constexpr int M_GB = 0, M_GL = 128, M_BETA = 192, M_EG = 256, M_DEC = 320, M_RQ = 384, M_RK = 448, M_T2S = 512,
-              M_GAMMA = 576;
-constexpr int SMEM_BYTES = OFF_MISC + 580 * 4 + 1024;
+constexpr int AD_BLK = 16 * 16 + 16;  // floats per diagonal block of A, column-major, padded (bank spread)
+constexpr int OFF_MISC = OFF_AD + 4 * AD_BLK * 4;
+// MISC (floats), per token of the chunk unless noted:
+//   raw g[64] beta[64] | G log2e | beta | dec rk (dec = e^{G_c - G}) | O1 factor e^G rq scale |
+//   T2 column scale beta e^G rk | log2 column factor Gk = G log2e - log2 rk |
+//   log2 row factors of P (G log2e + log2(rq scale)) and of A (G log2e + log2(beta rk)) | gamma, G_c log2e
+constexpr int M_GB = 0, M_GL = 128, M_BETA = 192, M_DK = 256, M_OF = 320, M_T2S = 384, M_GK = 448, M_GQ = 512,
+              M_GA = 576, M_GAMMA = 640, M_GLL = 641;
+constexpr int SMEM_BYTES = OFF_MISC + 644 * 4 + 1024;  // + slack for the 1024-byte alignment of the base
 constexpr uint32_t QK_TX_BYTES = 2 * QK_BLK, V_TX_BYTES = 2 * T64_BLK;
 static_assert(OFF_V % 1024 == 0 && OFF_P % 1024 == 0 && OFF_R1 % 1024 == 0 && OFF_R2 % 1024 == 0, "tile alignment");
-static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
+// two CTAs per SM: each also holds 1 KB of static shared memory (the aligned dynamic base pads the
+// static section to 1 KB) and the 1 KB the hardware reserves per CTA, out of 228 KB per SM
+static_assert(2 * (SMEM_BYTES + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
 
 struct TileMaps {
   CUtensorMap q, k, v;
@@ -164,11 +171,12 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   float* sGB = misc + M_GB;
   float* sGl = misc + M_GL;
   float* sBeta = misc + M_BETA;
-  float* sEG = misc + M_EG;
-  float* sDec = misc + M_DEC;
-  float* sRq = misc + M_RQ;
-  float* sRk = misc + M_RK;
+  float* sDk = misc + M_DK;
+  float* sOf = misc + M_OF;
   float* sT2s = misc + M_T2S;
+  float* sGk = misc + M_GK;
+  float* sGq = misc + M_GQ;
+  float* sGa = misc + M_GA;
   float* sAd = reinterpret_cast<float*>(sm + OFF_AD);
   __shared__ uint64_t mbar;           // tensor-core completions
   __shared__ uint64_t qkbar, vbar;    // TMA arrivals of the q/k and v tiles
@@ -308,21 +316,32 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       sGl[i1] = Gl1;
       sBeta[i0] = b0;
       sBeta[i1] = b1;
-      sEG[i0] = fast_exp2(Gl0);
-      sEG[i1] = fast_exp2(Gl1);
-      sDec[i0] = fast_exp2(Gll - Gl0);
-      sDec[i1] = fast_exp2(Gll - Gl1);
-      if (lane == 0) misc[M_GAMMA] = fast_exp2(Gll);
-      if (!l2norm) {
-        sRq[i0] = sRq[i1] = 1.f;
-        sRk[i0] = sRk[i1] = 1.f;
-        sT2s[i0] = b0 * fast_exp2(Gl0);
-        sT2s[i1] = b1 * fast_exp2(Gl1);
+      if (lane == 0) {
+        misc[M_GAMMA] = fast_exp2(Gll);
+        misc[M_GLL] = Gll;
+      }
+      if (!l2norm) {  // rq = rk = 1
+        const float e0 = fast_exp2(Gl0), e1 = fast_exp2(Gl1), d0 = fast_exp2(Gll - Gl0), d1 = fast_exp2(Gll - Gl1);
+        const float ls = log2f(scale);
+        sDk[i0] = d0;
+        sDk[i1] = d1;
+        sOf[i0] = e0 * scale;
+        sOf[i1] = e1 * scale;
+        sT2s[i0] = b0 * e0;
+        sT2s[i1] = b1 * e1;
+        sGk[i0] = Gl0;
+        sGk[i1] = Gl1;
+        sGq[i0] = Gl0 + ls;
+        sGq[i1] = Gl1 + ls;
+        sGa[i0] = Gl0 + log2f(b0);
+        sGa[i1] = Gl1 + log2f(b1);
       }
     }
     if (!sync_mma()) break;  // D1 done; gates visible
 
     // ---------------- P (rows 0-63), A (rows 64-127) ----------------
+    // P_ij = x_ij 2^(Gq_i - Gk_j) (j <= i), A_ij = x_ij 2^(Ga_i - Gk_j) (j < i): the norms, beta and the
+    // attention scale ride in the log2 row / column factors
     {
       const bool qrow = tid < 64;
       const int i = tid & 63;
@@ -330,76 +349,56 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       tc::tmem_ld32(lane_addr + COL_D1 + 64, r0);
       tc::tmem_ld32(lane_addr + COL_D1 + 96, r1);
       if (l2norm) {
-        float rn;
+        const float Gli = sGl[i];
         if (qrow) {  // |q_i|^2 sits in column i of the QQ^T block
           float rd[32];
           tc::tmem_ld32(lane_addr + COL_D1 + (warp & 1) * 32, rd);
           tc::tmem_wait_ld();
-          rn = rsqrtf(pick_lane(rd, lane) + 1e-6f);
-          sRq[i] = rn;
+          const float rq = rsqrtf(pick_lane(rd, lane) + 1e-6f);
+          sOf[i] = fast_exp2(Gli) * rq * scale;
+          sGq[i] = Gli + log2f(rq * scale);
         } else {  // |k_i|^2 sits in column 64 + i
           tc::tmem_wait_ld();
-          rn = rsqrtf(pick_lane((warp & 1) ? r1 : r0, lane) + 1e-6f);
-          sRk[i] = rn;
+          const float rk = rsqrtf(pick_lane((warp & 1) ? r1 : r0, lane) + 1e-6f);
+          const float bi = sBeta[i];
+          sDk[i] = fast_exp2(misc[M_GLL] - Gli) * rk;
+          sT2s[i] = bi * fast_exp2(Gli) * rk;
+          sGk[i] = Gli - log2f(rk);
+          sGa[i] = Gli + log2f(bi * rk);
         }
         __syncthreads();
-        if (!qrow) sT2s[i] = sBeta[i] * sEG[i] * rn;
       } else {
         tc::tmem_wait_ld();
       }
-      const float Gi = sGl[i];
+      const float Gr = qrow ? sGq[i] : sGa[i];
+      const int lim = qrow ? i : i - 1;  // last visible column
       // column groups of 8 that lie wholly above this warp's rows are zero
       const int cb_end = (warp & 1) ? 8 : 4;
-      if (qrow) {
-        const float rqi = sRq[i];
+      const int blk = i >> 4;
+      uint8_t* dst = sm + (qrow ? OFF_P : OFF_A16);
 #pragma unroll
-        for (int cb = 0; cb < 8; ++cb) {
-          float p8[8];
-          if (cb < cb_end) {
-            const float4 ga = ld4(sGl + cb * 8), gb = ld4(sGl + cb * 8 + 4);
-            const float4 ka = ld4(sRk + cb * 8), kb = ld4(sRk + cb * 8 + 4);
-            const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-            const float rkj[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+      for (int cb = 0; cb < 8; ++cb) {
+        float v8[8];
+        if (cb < cb_end) {
+          const float4 ga = ld4(sGk + cb * 8), gb = ld4(sGk + cb * 8 + 4);
+          const float gk[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int j = cb * 8 + e;
-              const float x = j < 32 ? r0[j] : r1[j - 32];
-              p8[e] = j <= i ? x * rqi * rkj[e] * fast_exp2(Gi - gj[e]) : 0.f;
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) p8[e] = 0.f;
+          for (int e = 0; e < 8; ++e) {
+            const int j = cb * 8 + e;
+            const float x = j < 32 ? r0[j] : r1[j - 32];
+            const float v = x * fast_exp2(Gr - gk[e]);
+            v8[e] = j <= lim ? v : 0.f;
           }
-          *reinterpret_cast<uint4*>(sm + OFF_P + sw(i, cb)) = pack8<__half>(p8);
-        }
-      } else {
-        const float bi = sBeta[i] * sRk[i];
-        const int blk = i >> 4;
+          if (!qrow && (cb >> 1) == blk) {  // the diagonal 16x16 block, fp32, column-major
+            float* ad = sAd + blk * AD_BLK + (cb & 1) * 8 * 16 + (i & 15);
 #pragma unroll
-        for (int cb = 0; cb < 8; ++cb) {
-          float a8[8];
-          if (cb < cb_end) {
-            const float4 ga = ld4(sGl + cb * 8), gb = ld4(sGl + cb * 8 + 4);
-            const float4 ka = ld4(sRk + cb * 8), kb = ld4(sRk + cb * 8 + 4);
-            const float gj[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-            const float rkj[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const int j = cb * 8 + e;
-              const float x = j < 32 ? r0[j] : r1[j - 32];
-              a8[e] = j < i ? bi * x * rkj[e] * fast_exp2(Gi - gj[e]) : 0.f;
-            }
-            if ((cb >> 1) == blk) {  // the diagonal 16x16 block, fp32, for the substitution
-              float* ad = sAd + blk * 256 + (i & 15) * 16 + (cb & 1) * 8;
-              *reinterpret_cast<float4*>(ad) = make_float4(a8[0], a8[1], a8[2], a8[3]);
-              *reinterpret_cast<float4*>(ad + 4) = make_float4(a8[4], a8[5], a8[6], a8[7]);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) a8[e] = 0.f;
+            for (int e = 0; e < 8; ++e) ad[e * 16] = v8[e];
           }
-          *reinterpret_cast<uint4*>(sm + OFF_A16 + sw(i, cb)) = pack8<__half>(a8);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v8[e] = 0.f;
         }
+        *reinterpret_cast<uint4*>(dst + sw(i, cb)) = pack8<__half>(v8);
       }
     }
     __syncthreads();
@@ -410,15 +409,24 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     //     strictly upper blocks of T1, T2 and the two upper blocks of T that the merges read
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
-      const float* ab = sAd + (tid >> 4) * 256;
+      const float* ab = sAd + (tid >> 4) * AD_BLK;  // column kk at ab + 16 kk
       float xs[16];
 #pragma unroll
       for (int r = 0; r < 16; ++r) xs[r] = r == j ? 1.f : 0.f;
 #pragma unroll
       for (int kk = 0; kk < 15; ++kk) {
         const float xk = xs[kk];
+        float col[16];
 #pragma unroll
-        for (int r = kk + 1; r < 16; ++r) xs[r] -= ab[r * 16 + kk] * xk;
+        for (int q4 = (kk + 1) >> 2; q4 < 4; ++q4) {
+          const float4 a4 = ld4(ab + kk * 16 + q4 * 4);
+          col[q4 * 4] = a4.x;
+          col[q4 * 4 + 1] = a4.y;
+          col[q4 * 4 + 2] = a4.z;
+          col[q4 * 4 + 3] = a4.w;
+        }
+#pragma unroll
+        for (int r = kk + 1; r < 16; ++r) xs[r] -= col[r] * xk;
       }
       const int col = o + j;
       const float s1 = sBeta[col], s2 = sT2s[col];
@@ -623,10 +631,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 #pragma unroll
       for (int cb = 0; cb < 8; ++cb) {
         float x[8], y[8];
-        const float4 d0 = ld4(sDec + cb * 8), d1 = ld4(sDec + cb * 8 + 4);
-        const float4 k0 = ld4(sRk + cb * 8), k1 = ld4(sRk + cb * 8 + 4);
-        const float dd[8] = {d0.x * k0.x, d0.y * k0.y, d0.z * k0.z, d0.w * k0.w,
-                             d1.x * k1.x, d1.y * k1.y, d1.z * k1.z, d1.w * k1.w};
+        const float4 d0 = ld4(sDk + cb * 8), d1 = ld4(sDk + cb * 8 + 4);
+        const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int t = cb * 8 + e;
@@ -676,20 +682,24 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         tc::tmem_ld32(lane_addr + COL_W + hh * 32, o1);
         tc::tmem_ld32(lane_addr + COL_U + hh * 32, o2);
         tc::tmem_wait_ld();
+        float of[32];  // per-token O1 factor e^G rq scale (O2 arrives scaled through P)
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+          const float4 f = ld4(sOf + hh * 32 + t4 * 4);
+          of[t4 * 4] = f.x;
+          of[t4 * 4 + 1] = f.y;
+          of[t4 * 4 + 2] = f.z;
+          of[t4 * 4 + 3] = f.w;
+        }
         if constexpr (sizeof(TOut) == 2) {
           TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging
 #pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const int tt = hh * 32 + t;
-            ost[tt * D + tid] = from_f32<TOut>((sEG[tt] * sRq[tt] * o1[t] + o2[t]) * scale);
-          }
+          for (int t = 0; t < 32; ++t) ost[(hh * 32 + t) * D + tid] = from_f32<TOut>(fmaf(of[t], o1[t], o2[t]));
         } else {
 #pragma unroll
           for (int t = 0; t < 32; ++t) {
             const int tt = hh * 32 + t;
-            if (tt < nvalid)
-              out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + tid] =
-                  from_f32<TOut>((sEG[tt] * sRq[tt] * o1[t] + o2[t]) * scale);
+            if (tt < nvalid) out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + tid] = fmaf(of[t], o1[t], o2[t]);
           }
         }
       }
