@@ -29,8 +29,12 @@
 // every rounding point gives output rel-L2 ~3e-4 and state rel-L2 ~3e-6
 // against an fp64 recurrence (bf16 inputs, cfg0 distributions).
 //
-// Occupancy: two CTAs per SM (128 threads, 256 TMEM columns and ~111 KB of
-// shared memory each).  Shared memory is reused phase by phase (map below).
+// Occupancy: two CTAs per SM (256 threads, 256 TMEM columns and ~112 KB of
+// shared memory each).  Warps w and w + 4 share TMEM lane quarter w and split
+// every row readout by columns, so four warps per scheduler hide the latency
+// of the tensor-memory loads, the exponentials and the barriers.  Shared memory
+// is reused phase by phase (map below); the first half of the state readout
+// runs while the tensor core forms U and W.
 // q/k tiles and v tiles arrive by TMA on separate barriers (3-D tensor maps
 // over [d, head, token], 64-token x 64-element boxes, 128-byte swizzle): the
 // next chunk's v is requested once U has been formed, its q/k once the state
@@ -53,7 +57,7 @@ namespace {
 
 constexpr int C = 64;
 constexpr int D = 128;
-constexpr int NT = 128;
+constexpr int NT = 256;
 constexpr uint32_t TMEM_COLS = 256;
 // S^T: cols 0-127.  D1: cols 128-255.  Then U -> Vn -> O2 at 128-191, W -> O1 at 192-255.
 constexpr uint32_t COL_S = 0, COL_D1 = 128, COL_U = 128, COL_W = 192;
@@ -62,8 +66,8 @@ constexpr uint32_t COL_S = 0, COL_D1 = 128, COL_U = 128, COL_W = 192;
 //   QK (TMA)  rows 0-63 Q, 64-127 K, two 64-column blocks          [load .. state update]
 //   V  (TMA)  two 64-column blocks                                   [load .. U]
 //   P  fp16 [i][j]                                                   [P/A .. O2]
-//   R1 32 KB: T1 hi|lo, T2 hi|lo [i][j]  ->  S^T copy [d_v][d_k]  ->  decayed Vn hi|lo [d_v][tok]
-//   R2 16 KB: A fp16 | T fp16 [i][j]  ->  W^T [d_k][tok]  ->  Vn fp16 [d_v][tok]  ->  O staging [tok][d_v]
+//   R1 32 KB: T1 hi|lo, T2 hi|lo [i][j]  ->  W^T [d_k][tok] | S^T copy, d_k 64-127  ->  decayed Vn hi|lo [d_v][tok]
+//   R2 16 KB: A fp16 | T fp16 [i][j]  ->  S^T copy, d_k 0-63 [d_v][64]  ->  Vn fp16 [d_v][tok]  ->  O staging
 //   AD fp32 diagonal 16x16 blocks of A
 constexpr int QK_BLK = 128 * 128;  // one 64-column block of a 128-row tile
 constexpr int T64_BLK = 64 * 128;  // one 64-column block of a 64-row tile
@@ -73,11 +77,12 @@ constexpr int OFF_P = OFF_V + 2 * T64_BLK;
 constexpr int OFF_R1 = OFF_P + T64_BLK;
 constexpr int OFF_T1H = OFF_R1, OFF_T1L = OFF_R1 + T64_BLK, OFF_T2H = OFF_R1 + 2 * T64_BLK,
               OFF_T2L = OFF_R1 + 3 * T64_BLK;
-constexpr int OFF_ST = OFF_R1;                          // [d_v 128][d_k] as two 64-column blocks
+constexpr int OFF_W = OFF_R1;                           // W^T [d_k 128][tok 64], MN-major operand
+constexpr int OFF_SB1 = OFF_R1 + QK_BLK;                // S^T copy, d_k 64-127: [d_v 128][64]
 constexpr int OFF_DH = OFF_R1, OFF_DL = OFF_R1 + QK_BLK;  // [d_v 128][tok 64]
 constexpr int OFF_R2 = OFF_R1 + 4 * T64_BLK;
 constexpr int OFF_A16 = OFF_R2, OFF_T16 = OFF_R2 + T64_BLK;
-constexpr int OFF_W = OFF_R2;    // W^T [d_k 128][tok 64], MN-major operand
+constexpr int OFF_SB0 = OFF_R2;  // S^T copy, d_k 0-63
 constexpr int OFF_VN = OFF_R2;   // Vn^T [d_v 128][tok 64]
 constexpr int OFF_OST = OFF_R2;  // [tok 64][d_v 128] 2-byte staging
 constexpr int OFF_AD = OFF_R2 + QK_BLK;
@@ -183,7 +188,9 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;  // thread tid reads TMEM lane tid
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2;  // TMEM lane quarter, column half
+  const int row = tid & 127;                // the TMEM lane (tile row) this thread reads
   const int bh = blockIdx.x;
   const int b = bh / Hv, hv = bh % Hv;
   const int hk = hv / (Hv / Hqk);
@@ -203,7 +210,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       tc::tma_load_3d(qk + QK_BLK + 64 * 128, &maps.k, 64, hk, tok0, qkb);
     }
     const int r = tid & 63;
-    if (cc * C + r < T) {
+    if (tid < 128 && cc * C + r < T) {
       const size_t idx = ((size_t)b * T + cc * C + r) * Hv + hv;
       cp_async4(sGB + (tid >> 6) * 64 + r, (tid >> 6) ? beta + idx : g + idx);
     }
@@ -235,19 +242,20 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   issue_qk(0);
   issue_v(0);
   const uint32_t tmem = tmem_slot;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lane quarter
+  const uint32_t lane_addr = tmem + ((uint32_t)(qd * 32) << 16);  // this warp's TMEM lane quarter
   uint32_t phase = 0;
   int pending_qk = 0, pending_v = 0;  // chunk whose tiles were requested and not yet waited for (-1: none)
 
-  // ---- initial state: thread d holds column d of S (row d of S^T) ----
+  // ---- initial state: thread (row d, half hf) holds S[64 hf .. 64 hf + 63][d] (row d of S^T) ----
   float* Sg = state + (size_t)bh * D * D;
   {
     float buf[32];
 #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 2; ++j) {
+      const int k0 = 64 * hf + 32 * j;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) buf[i] = Sg[(size_t)(j * 32 + i) * D + tid];
-      tc::tmem_st32(lane_addr + COL_S + j * 32, buf);
+      for (int i = 0; i < 32; ++i) buf[i] = Sg[(size_t)(k0 + i) * D + row];
+      tc::tmem_st32(lane_addr + COL_S + k0, buf);
     }
     tc::tmem_wait_st();
   }
@@ -343,28 +351,33 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     // P_ij = x_ij 2^(Gq_i - Gk_j) (j <= i), A_ij = x_ij 2^(Ga_i - Gk_j) (j < i): the norms, beta and the
     // attention scale ride in the log2 row / column factors
     {
-      const bool qrow = tid < 64;
-      const int i = tid & 63;
-      float r0[32], r1[32];  // columns 64-127 of D1: row . k_j
-      tc::tmem_ld32(lane_addr + COL_D1 + 64, r0);
-      tc::tmem_ld32(lane_addr + COL_D1 + 96, r1);
+      const bool qrow = row < 64;
+      const int i = row & 63;
+      float r0[32];  // D1 columns 64 + 32 hf ..: row . k_j for j in [32 hf, 32 hf + 32)
+      tc::tmem_ld32(lane_addr + COL_D1 + 64 + 32 * hf, r0);
       if (l2norm) {
         const float Gli = sGl[i];
-        if (qrow) {  // |q_i|^2 sits in column i of the QQ^T block
-          float rd[32];
-          tc::tmem_ld32(lane_addr + COL_D1 + (warp & 1) * 32, rd);
+        if (qrow) {
+          if (hf == 0) {  // |q_i|^2 sits in column i of the QQ^T block
+            float rd[32];
+            tc::tmem_ld32(lane_addr + COL_D1 + (qd & 1) * 32, rd);
+            tc::tmem_wait_ld();
+            const float rq = rsqrtf(pick_lane(rd, lane) + 1e-6f);
+            sOf[i] = fast_exp2(Gli) * rq * scale;
+            sGq[i] = Gli + log2f(rq * scale);
+          } else {
+            tc::tmem_wait_ld();
+          }
+        } else {
           tc::tmem_wait_ld();
-          const float rq = rsqrtf(pick_lane(rd, lane) + 1e-6f);
-          sOf[i] = fast_exp2(Gli) * rq * scale;
-          sGq[i] = Gli + log2f(rq * scale);
-        } else {  // |k_i|^2 sits in column 64 + i
-          tc::tmem_wait_ld();
-          const float rk = rsqrtf(pick_lane((warp & 1) ? r1 : r0, lane) + 1e-6f);
-          const float bi = sBeta[i];
-          sDk[i] = fast_exp2(misc[M_GLL] - Gli) * rk;
-          sT2s[i] = bi * fast_exp2(Gli) * rk;
-          sGk[i] = Gli - log2f(rk);
-          sGa[i] = Gli + log2f(bi * rk);
+          if (hf == (qd & 1)) {  // |k_i|^2 sits in column 64 + i, held by this half
+            const float rk = rsqrtf(pick_lane(r0, lane) + 1e-6f);
+            const float bi = sBeta[i];
+            sDk[i] = fast_exp2(misc[M_GLL] - Gli) * rk;
+            sT2s[i] = bi * fast_exp2(Gli) * rk;
+            sGk[i] = Gli - log2f(rk);
+            sGa[i] = Gli + log2f(bi * rk);
+          }
         }
         __syncthreads();
       } else {
@@ -372,21 +385,20 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       }
       const float Gr = qrow ? sGq[i] : sGa[i];
       const int lim = qrow ? i : i - 1;  // last visible column
-      // column groups of 8 that lie wholly above this warp's rows are zero
-      const int cb_end = (warp & 1) ? 8 : 4;
+      const bool above = hf > (qd & 1);  // this warp's columns lie wholly above its rows
       const int blk = i >> 4;
       uint8_t* dst = sm + (qrow ? OFF_P : OFF_A16);
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
+      for (int cl = 0; cl < 4; ++cl) {
+        const int cb = 4 * hf + cl;
         float v8[8];
-        if (cb < cb_end) {
+        if (!above) {
           const float4 ga = ld4(sGk + cb * 8), gb = ld4(sGk + cb * 8 + 4);
           const float gk[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int j = cb * 8 + e;
-            const float x = j < 32 ? r0[j] : r1[j - 32];
-            const float v = x * fast_exp2(Gr - gk[e]);
+            const float v = r0[cl * 8 + e] * fast_exp2(Gr - gk[e]);
             v8[e] = j <= lim ? v : 0.f;
           }
           if (!qrow && (cb >> 1) == blk) {  // the diagonal 16x16 block, fp32, column-major
@@ -405,7 +417,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- T = (I + A)^-1 -> T1 = T diag(beta), T2 = T diag(beta e^G rk), hi|lo ----------------
     // (1) threads 0-63: diagonal 16x16 blocks, thread (blk, j) solves column j by right-looking
-    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-127 zero the
+    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-255 zero the
     //     strictly upper blocks of T1, T2 and the two upper blocks of T that the merges read
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
@@ -447,7 +459,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       const int u = tid - 64;
       const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll 1
-      for (int idx = u; idx < 48 * 8; idx += 64) {
+      for (int idx = u; idx < 48 * 8; idx += NT - 64) {
         const int r = idx >> 3, ch = idx & 7;
         if (ch >= 2 * ((r >> 4) + 1)) {
           const uint32_t off = sw(r, ch);
@@ -457,7 +469,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
           *reinterpret_cast<uint4*>(sm + OFF_T2L + off) = z;
         }
       }
-      {
+      if (u < 64) {
         const int r = (u >> 1) & 15, ch = ((u >> 5) ? 6 : 2) + (u & 1), ro = (u >> 5) ? 32 : 0;
         *reinterpret_cast<uint4*>(sm + OFF_T16 + sw(ro + r, ch)) = z;
       }
@@ -500,7 +512,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     __syncthreads();
     // (3) 32 -> 64 (all warps; warp = (row half mt, column half nh) of T[32:64, 0:32]):
     //     Y^T = T00^T A10^T (rows nh*16.. of Y^T), T[32+16mt.., 16nh..] = -T11 Y
-    {
+    if (warp < 4) {
       const int nh = warp & 1, mt = warp >> 1;
       float yt[4][4];
 #pragma unroll
@@ -571,6 +583,20 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       }
       tc::commit(bar);
     }
+    // meanwhile: S^T columns 0-63 -> the first block of the S^T copy; S^T *= gamma there
+    {
+      float s32[32];
+      tc::tmem_ld32(lane_addr + COL_S + 32 * hf, s32);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb)
+        *reinterpret_cast<uint4*>(sm + OFF_SB0 + sw(row, 4 * hf + cb)) = pack8<TIn>(s32 + cb * 8);
+      const float gamma = misc[M_GAMMA];
+#pragma unroll
+      for (int e = 0; e < 32; ++e) s32[e] *= gamma;
+      tc::tmem_st32(lane_addr + COL_S + 32 * hf, s32);
+      tc::tmem_wait_st();
+    }
     if (!sync_mma()) break;
     // v is free: request the next chunk's v tile
     if (c + 1 < nchunks) {
@@ -578,32 +604,24 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       pending_v = c + 1;
     }
 
-    // ---------------- W^T readout (MN-major operand) and S^T readout (copy, then S^T *= gamma) ----------------
+    // ---------------- W^T readout (MN-major operand) and S^T columns 64-127 (copy, then S^T *= gamma) ----------------
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_W, r0);
-      tc::tmem_ld32(lane_addr + COL_W + 32, r1);
+      float r0[32];
+      tc::tmem_ld32(lane_addr + COL_W + 32 * hf, r0);
       tc::tmem_wait_ld();
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        *reinterpret_cast<uint4*>(sm + OFF_W + sw(tid, cb)) = pack8<TIn>(r0 + cb * 8);
-        *reinterpret_cast<uint4*>(sm + OFF_W + sw(tid, cb + 4)) = pack8<TIn>(r1 + cb * 8);
-      }
+      for (int cb = 0; cb < 4; ++cb)
+        *reinterpret_cast<uint4*>(sm + OFF_W + sw(row, 4 * hf + cb)) = pack8<TIn>(r0 + cb * 8);
+      float s32[32];
+      tc::tmem_ld32(lane_addr + COL_S + 64 + 32 * hf, s32);
+      tc::tmem_wait_ld();
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb)
+        *reinterpret_cast<uint4*>(sm + OFF_SB1 + sw(row, 4 * hf + cb)) = pack8<TIn>(s32 + cb * 8);
       const float gamma = misc[M_GAMMA];
-#pragma unroll 1
-      for (int j = 0; j < 4; ++j) {
-        float s32[32];
-        tc::tmem_ld32(lane_addr + COL_S + j * 32, s32);
-        tc::tmem_wait_ld();
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          const int kc = j * 4 + cb;  // 16-byte chunk index 0..15 along d_k
-          *reinterpret_cast<uint4*>(sm + OFF_ST + (kc >> 3) * QK_BLK + sw(tid, kc & 7)) = pack8<TIn>(s32 + cb * 8);
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s32[e] *= gamma;
-        tc::tmem_st32(lane_addr + COL_S + j * 32, s32);
-      }
+      for (int e = 0; e < 32; ++e) s32[e] *= gamma;
+      tc::tmem_st32(lane_addr + COL_S + 64 + 32 * hf, s32);
       tc::tmem_wait_st();
     }
     sync_smem_for_mma();
@@ -612,7 +630,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     if (tid == 0) {
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
-        const uint64_t as = tc::sdesc_sw128(sbase + OFF_ST + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
+        const uint64_t as = tc::sdesc_sw128(sbase + ((s >> 2) ? OFF_SB1 : OFF_SB0) + (s & 3) * 32, 16, 1024);
         const uint64_t bw = tc::sdesc_sw128(sbase + OFF_W + s * 2048, 8192, 1024);
         tc::mma_f16(tmem + COL_U, as, bw, ID_VN, 1);
         const uint64_t bq = tc::sdesc_sw128(sbase + OFF_QK + (s >> 2) * QK_BLK + (s & 3) * 32, 16, 1024);
@@ -624,26 +642,22 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- Vn readout: Vn (fp16) and the decayed Vn diag(dec rk) (hi|lo) ----------------
     {
-      float r0[32], r1[32];
-      tc::tmem_ld32(lane_addr + COL_U, r0);
-      tc::tmem_ld32(lane_addr + COL_U + 32, r1);
+      float r0[32];
+      tc::tmem_ld32(lane_addr + COL_U + 32 * hf, r0);
       tc::tmem_wait_ld();
 #pragma unroll
-      for (int cb = 0; cb < 8; ++cb) {
-        float x[8], y[8];
+      for (int cl = 0; cl < 4; ++cl) {
+        const int cb = 4 * hf + cl;
+        float y[8];
         const float4 d0 = ld4(sDk + cb * 8), d1 = ld4(sDk + cb * 8 + 4);
         const float dd[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int t = cb * 8 + e;
-          x[e] = t < 32 ? r0[t] : r1[t - 32];
-          y[e] = x[e] * dd[e];
-        }
-        *reinterpret_cast<uint4*>(sm + OFF_VN + sw(tid, cb)) = pack8<__half>(x);
+        for (int e = 0; e < 8; ++e) y[e] = r0[cl * 8 + e] * dd[e];
+        *reinterpret_cast<uint4*>(sm + OFF_VN + sw(row, cb)) = pack8<__half>(r0 + cl * 8);
         uint4 hi, lo;
         pack8_hilo<TIn>(y, hi, lo);
-        *reinterpret_cast<uint4*>(sm + OFF_DH + sw(tid, cb)) = hi;
-        *reinterpret_cast<uint4*>(sm + OFF_DL + sw(tid, cb)) = lo;
+        *reinterpret_cast<uint4*>(sm + OFF_DH + sw(row, cb)) = hi;
+        *reinterpret_cast<uint4*>(sm + OFF_DL + sw(row, cb)) = lo;
       }
     }
     sync_smem_for_mma();
@@ -667,6 +681,9 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       }
       tc::commit(bar);
     }
+    float o1[32];  // O1 (untouched by these MMAs) is read while they run
+    tc::tmem_ld32(lane_addr + COL_W + 32 * hf, o1);
+    tc::tmem_wait_ld();
     if (!sync_mma()) break;
     // q/k are free: start the next chunk's copies while O drains
     if (c + 1 < nchunks) {
@@ -674,43 +691,37 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       pending_qk = c + 1;
     }
 
-    // ---------------- O = (e^G rq O1 + O2) * scale -> global ----------------
+    // ---------------- O = e^G rq scale O1 + O2 -> global (tokens 32 hf .. 32 hf + 31 of row d_v) ----------------
     {
-      float o1[32], o2[32];
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        tc::tmem_ld32(lane_addr + COL_W + hh * 32, o1);
-        tc::tmem_ld32(lane_addr + COL_U + hh * 32, o2);
-        tc::tmem_wait_ld();
-        float of[32];  // per-token O1 factor e^G rq scale (O2 arrives scaled through P)
+      float o2[32];
+      tc::tmem_ld32(lane_addr + COL_U + 32 * hf, o2);
+      tc::tmem_wait_ld();
+      float of[32];  // per-token O1 factor e^G rq scale (O2 arrives scaled through P)
 #pragma unroll
-        for (int t4 = 0; t4 < 8; ++t4) {
-          const float4 f = ld4(sOf + hh * 32 + t4 * 4);
-          of[t4 * 4] = f.x;
-          of[t4 * 4 + 1] = f.y;
-          of[t4 * 4 + 2] = f.z;
-          of[t4 * 4 + 3] = f.w;
-        }
-        if constexpr (sizeof(TOut) == 2) {
-          TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging
-#pragma unroll
-          for (int t = 0; t < 32; ++t) ost[(hh * 32 + t) * D + tid] = from_f32<TOut>(fmaf(of[t], o1[t], o2[t]));
-        } else {
-#pragma unroll
-          for (int t = 0; t < 32; ++t) {
-            const int tt = hh * 32 + t;
-            if (tt < nvalid) out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + tid] = fmaf(of[t], o1[t], o2[t]);
-          }
-        }
+      for (int q4 = 0; q4 < 8; ++q4) {
+        const float4 f = ld4(sOf + 32 * hf + q4 * 4);
+        of[q4 * 4] = f.x;
+        of[q4 * 4 + 1] = f.y;
+        of[q4 * 4 + 2] = f.z;
+        of[q4 * 4 + 3] = f.w;
       }
       if constexpr (sizeof(TOut) == 2) {
+        TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging
+#pragma unroll
+        for (int t = 0; t < 32; ++t) ost[(32 * hf + t) * D + row] = from_f32<TOut>(fmaf(of[t], o1[t], o2[t]));
         __syncthreads();
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int r = (tid >> 4) + it * 8, ch = tid & 15;
+        for (int it = 0; it < 4; ++it) {
+          const int idx = tid + it * NT, r = idx >> 4, ch = idx & 15;
           if (r < nvalid)
             *reinterpret_cast<uint4*>(out + (((size_t)b * T + t0 + r) * Hv + hv) * D + ch * 8) =
                 *reinterpret_cast<const uint4*>(sm + OFF_OST + r * 256 + ch * 16);
+        }
+      } else {
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int tt = 32 * hf + t;
+          if (tt < nvalid) out[(((size_t)b * T + t0 + tt) * Hv + hv) * D + row] = fmaf(of[t], o1[t], o2[t]);
         }
       }
     }
@@ -727,11 +738,12 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
   if (!abort_flag) {
     float buf[32];
 #pragma unroll 1
-    for (int j = 0; j < 4; ++j) {
-      tc::tmem_ld32(lane_addr + COL_S + j * 32, buf);
+    for (int j = 0; j < 2; ++j) {
+      const int k0 = 64 * hf + 32 * j;
+      tc::tmem_ld32(lane_addr + COL_S + k0, buf);
       tc::tmem_wait_ld();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) Sg[(size_t)(j * 32 + i) * D + tid] = buf[i];
+      for (int i = 0; i < 32; ++i) Sg[(size_t)(k0 + i) * D + row] = buf[i];
     }
   }
   tc::fence_before();
