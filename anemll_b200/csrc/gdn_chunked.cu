@@ -279,10 +279,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     tc::fence_after();
   };
   constexpr uint32_t ID_D1 = tc::idesc_f16(128, 128, false, false, false, kBF);
-  constexpr uint32_t ID_UW = tc::idesc_f16(128, 64, true, false, false, kBF);
   constexpr uint32_t ID_VN = tc::idesc_f16(128, 64, false, true, true, kBF);
   constexpr uint32_t ID_O1 = tc::idesc_f16(128, 64, false, false, false, kBF);
-  constexpr uint32_t ID_O2 = tc::idesc_f16(128, 64, false, false, false, false);
   constexpr uint32_t ID_SU = tc::idesc_f16(128, 128, false, true, false, kBF);
 
 #pragma unroll 1
@@ -388,11 +386,12 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
       const bool above = hf > (qd & 1);  // this warp's columns lie wholly above its rows
       const int blk = i >> 4;
       uint8_t* dst = sm + (qrow ? OFF_P : OFF_A16);
+      // (blocks above the diagonal are never read: the products that use P and A skip them)
 #pragma unroll
-      for (int cl = 0; cl < 4; ++cl) {
+      for (int cl = 0; cl < 4 && !above; ++cl) {
         const int cb = 4 * hf + cl;
         float v8[8];
-        if (!above) {
+        {
           const float4 ga = ld4(sGk + cb * 8), gb = ld4(sGk + cb * 8 + 4);
           const float gk[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
@@ -406,9 +405,6 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 #pragma unroll
             for (int e = 0; e < 8; ++e) ad[e * 16] = v8[e];
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v8[e] = 0.f;
         }
         *reinterpret_cast<uint4*>(dst + sw(i, cb)) = pack8<__half>(v8);
       }
@@ -417,8 +413,8 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- T = (I + A)^-1 -> T1 = T diag(beta), T2 = T diag(beta e^G rk), hi|lo ----------------
     // (1) threads 0-63: diagonal 16x16 blocks, thread (blk, j) solves column j by right-looking
-    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-255 zero the
-    //     strictly upper blocks of T1, T2 and the two upper blocks of T that the merges read
+    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-127 zero the
+    //     two upper blocks of T that the merges read
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
       const float* ab = sAd + (tid >> 4) * AD_BLK;  // column kk at ab + 16 kk
@@ -454,21 +450,10 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         *reinterpret_cast<TIn*>(sm + OFF_T2L + off) = from_f32<TIn>(v2 - to_f32(h2));
       }
     } else {
-      // upper blocks of T1, T2 (hi, lo): rows 0-15 cols 16-63, rows 16-31 cols 32-63, rows 32-47 cols 48-63,
-      // i.e. 16-byte chunks (r, ch) with ch >= 2 * (r / 16 + 1); plus T blocks (0,1) and (2,3)
+      // T blocks (0,1) and (2,3), which the 32 -> 64 merge reads as zeros (T1, T2 need no zeros:
+      // the products that use them skip the blocks above the diagonal)
       const int u = tid - 64;
       const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll 1
-      for (int idx = u; idx < 48 * 8; idx += NT - 64) {
-        const int r = idx >> 3, ch = idx & 7;
-        if (ch >= 2 * ((r >> 4) + 1)) {
-          const uint32_t off = sw(r, ch);
-          *reinterpret_cast<uint4*>(sm + OFF_T1H + off) = z;
-          *reinterpret_cast<uint4*>(sm + OFF_T1L + off) = z;
-          *reinterpret_cast<uint4*>(sm + OFF_T2H + off) = z;
-          *reinterpret_cast<uint4*>(sm + OFF_T2L + off) = z;
-        }
-      }
       if (u < 64) {
         const int r = (u >> 1) & 15, ch = ((u >> 5) ? 6 : 2) + (u & 1), ro = (u >> 5) ? 32 : 0;
         *reinterpret_cast<uint4*>(sm + OFF_T16 + sw(ro + r, ch)) = z;
@@ -568,17 +553,20 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     sync_smem_for_mma();
 
     // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T (hi and lo parts) ----------------
+    // T1, T2 are lower triangular: k-step s (tokens j in [16 s, 16 s + 16)) only reaches output
+    // tokens i >= 16 s, so it runs with N = 64 - 16 s on B rows and D columns from 16 s
     if (tid == 0) {
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
 #pragma unroll
         for (int s = 0; s < 4; ++s) {
+          const uint32_t id = tc::idesc_f16(128, 64 - 16 * s, true, false, false, kBF);
           const uint64_t av = tc::sdesc_sw128(sbase + OFF_V + s * 2048, T64_BLK, 1024);
-          const uint64_t b1 = tc::sdesc_sw128(sbase + (part ? OFF_T1L : OFF_T1H) + s * 32, 16, 1024);
-          tc::mma_f16(tmem + COL_U, av, b1, ID_UW, part > 0 || s > 0);
+          const uint64_t b1 = tc::sdesc_sw128(sbase + (part ? OFF_T1L : OFF_T1H) + s * 2048 + s * 32, 16, 1024);
+          tc::mma_f16(tmem + COL_U + 16 * s, av, b1, id, part > 0 || s > 0);
           const uint64_t ak = tc::sdesc_sw128(sbase + OFF_QK + 64 * 128 + s * 2048, QK_BLK, 1024);
-          const uint64_t b2 = tc::sdesc_sw128(sbase + (part ? OFF_T2L : OFF_T2H) + s * 32, 16, 1024);
-          tc::mma_f16(tmem + COL_W, ak, b2, ID_UW, part > 0 || s > 0);
+          const uint64_t b2 = tc::sdesc_sw128(sbase + (part ? OFF_T2L : OFF_T2H) + s * 2048 + s * 32, 16, 1024);
+          tc::mma_f16(tmem + COL_W + 16 * s, ak, b2, id, part > 0 || s > 0);
         }
       }
       tc::commit(bar);
@@ -665,10 +653,11 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
     // ---------------- O2^T = Vn^T P^T (into U's columns) ; S^T += (dec Vn)^T K (hi and lo) ----------------
     if (tid == 0) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
+      for (int s = 0; s < 4; ++s) {  // P is lower triangular: k-step s reaches tokens i >= 16 s only
+        const uint32_t id = tc::idesc_f16(128, 64 - 16 * s, false, false, false, false);
         const uint64_t av = tc::sdesc_sw128(sbase + OFF_VN + s * 32, 16, 1024);
-        const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 32, 16, 1024);
-        tc::mma_f16(tmem + COL_U, av, bp, ID_O2, s > 0);
+        const uint64_t bp = tc::sdesc_sw128(sbase + OFF_P + s * 2048 + s * 32, 16, 1024);
+        tc::mma_f16(tmem + COL_U + 16 * s, av, bp, id, s > 0);
       }
 #pragma unroll
       for (int part = 0; part < 2; ++part) {
