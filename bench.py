@@ -306,6 +306,30 @@ def bench_gdn_prefill(args, ws, rank, local):
     ms_max = max_over_ranks(ms, ws, dev)
     if gdn.chunked_device_error(reset=True):
         raise RuntimeError("chunked prefill reported a device-side wait timeout")
+
+    # end to end through the public op with host buffers: H2D of the shard's q/k/v/g/beta from pinned
+    # memory, the prefill, D2H of the output (a few steps: the copies dominate)
+    host = {n: w[n].cpu().pin_memory() for n in ("q", "k", "v", "g", "beta")}
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(x.numel() * x.element_size() for x in host.values())
+    d2h = hout.numel() * hout.element_size()
+    e2e_steps = min(args.steps, 3)
+
+    def e2e_step():
+        for n, x in host.items():
+            w[n].copy_(x, non_blocking=True)
+        gdn.chunk_gated_delta_rule_(w["q"], w["k"], w["v"], w["g"], w["beta"], state, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), ws, dev)
     tokens_local = b_loc * seqlen
     tokens_job = nseq * seqlen
     flop_launch = tokens_local * hv_loc * PREFILL_FLOP_PER_TOKEN_HEAD
@@ -332,6 +356,8 @@ def bench_gdn_prefill(args, ws, rank, local):
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / pk["bf16_tflops"], "peak_source": how,
                      "algorithmic_flop_per_launch": flop_launch, "traffic": None},
+        "e2e": {"value": tokens_job * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
@@ -411,6 +437,35 @@ def bench_kv_attention(args, ws, rank, local):
             dec_ms += e[2].elapsed_time(e[3])
     barrier(ws)
     tot_ms = max_over_ranks(pre_ms + dec_ms, ws, dev)
+
+    # end to end through the public op with host buffers (eager calls, no graph): per call the H2D of
+    # its q / k_new / v_new / gate from pinned memory, the call, and the D2H of its output
+    hcalls = [tuple(x.cpu().pin_memory() for x in c[1:]) for c in calls + dec]
+    houts = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    h2d = sum(x.numel() * x.element_size() for hc in hcalls for x in hc)
+    d2h = sum(o.numel() * o.element_size() for o in houts)
+
+    def e2e_pass():
+        for (p, qq, kk, vv, gg), o, hc, ho in zip(calls + dec, outs, hcalls, houts):
+            for dst, src in zip((qq, kk, vv, gg), hc):
+                dst.copy_(src, non_blocking=True)
+            attention.kv_attention(qq, K, V, p, k_new=kk, v_new=vv, gate=gg, window=window, out=o,
+                                   workspace=ws_buf)
+            ho.copy_(o, non_blocking=True)
+
+    e2e_pass()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    e2e_passes = min(args.steps, 3)
+    e2e_ms = 0.0
+    for _ in range(e2e_passes):
+        flush.zero_()
+        e[0].record(stream)
+        e2e_pass()
+        e[1].record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms += e[0].elapsed_time(e[1])
+    e2e_ms = max_over_ranks(e2e_ms, ws, dev)
     pre_ms_max = max_over_ranks(pre_ms, ws, dev)
     dec_ms_max = max_over_ranks(dec_ms, ws, dev)
     # algorithmic work: 4*hd*H_q FLOP per visible (query, key) pair in prefill; K+V bytes of visible keys in decode
@@ -446,6 +501,8 @@ def bench_kv_attention(args, ws, rank, local):
                      "algorithmic_flop_per_pass": flop_pre, "traffic": None,
                      "decode": {"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
                                 "algorithmic_bytes_per_pass": bytes_dec}},
+        "e2e": {"value": n_tok * e2e_passes / (e2e_ms / 1e3) * (1 if ws <= 2 else ws / 2), "unit": "tokens/s",
+                "passes": e2e_passes, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * (len(calls) + len(dec)) * 2,
         "clocks": clk.summary(),
     }
