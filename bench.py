@@ -355,7 +355,10 @@ def bench_gdn_prefill(args, ws, rank, local):
                    "parallelism": f"{ws} ranks, sequences x value heads, no collective"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / pk["bf16_tflops"], "peak_source": how,
-                     "algorithmic_flop_per_launch": flop_launch, "traffic": None},
+                     "algorithmic_flop_per_launch": flop_launch,
+                     # ncu DRAM bytes of one 8 x 4096 launch, scaled by the tokens to the 8 x 32768 launch
+                     "traffic": (traffic_from_profiles("gdn_chunked_prefill_8x32768")
+                                 if (ws, nseq, seqlen) == (1, 8, 32768) else None)},
         "e2e": {"value": tokens_job * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s", "steps": e2e_steps,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
@@ -500,7 +503,9 @@ def bench_kv_attention(args, ws, rank, local):
                      "frac": tflops / pk["bf16_tflops"], "peak_source": how,
                      "algorithmic_flop_per_pass": flop_pre, "traffic": None,
                      "decode": {"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
-                                "algorithmic_bytes_per_pass": bytes_dec}},
+                                "algorithmic_bytes_per_pass": bytes_dec,
+                                # ncu DRAM bytes of one causal decode-step launch (position 4032)
+                                "traffic_per_step": traffic_from_profiles("kv_decode_step") if not window else None}},
         "e2e": {"value": n_tok * e2e_passes / (e2e_ms / 1e3) * (1 if ws <= 2 else ws / 2), "unit": "tokens/s",
                 "passes": e2e_passes, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * (len(calls) + len(dec)) * 2,
