@@ -7,7 +7,7 @@ step of the whole batch = one kernel launch.  Weak scaling: every rank owns
 its own batch of 64 sequences; no collective on the data path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config gdn_decode|gdn_prefill|kv_attention]
+                  [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer]
 
 ``--impl reference`` times the CPU oracle of the same path on the host cores
 (the reference has no GPU implementation of this path), rank 0 only.
@@ -513,6 +513,216 @@ def bench_kv_attention(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------- GDN layer ----
+LAYER_PREFILL, LAYER_DECODE, HIDDEN = 512, 64, 2048
+LAYER_PROJ = 2 * H_QK * DK + 2 * H_V * DV + 2 * H_V  # in_proj_qkv | in_proj_z | in_proj_b | in_proj_a rows
+
+
+def layer_flop_per_token():
+    return 2 * HIDDEN * LAYER_PROJ + 2 * H_V * DV * HIDDEN + H_V * PREFILL_FLOP_PER_TOKEN_HEAD
+
+
+def layer_decode_bytes():
+    return 2 * (HIDDEN * LAYER_PROJ + H_V * DV * HIDDEN) + 2 * H_V * DK * DV * 4  # bf16 weights, state r+w
+
+
+def _load_layer(layer, w):
+    with torch.no_grad():
+        for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+            getattr(layer, n).weight.copy_(w[n])
+        layer.conv_weight.copy_(w["conv_w"])
+        layer.A_log.copy_(w["A_log"])
+        layer.dt_bias.copy_(w["dt_bias"])
+        layer.norm_weight.copy_(w["norm_w"])
+
+
+def bench_gdn_layer(args, ws, rank, local):
+    """One Qwen3.5 gated delta-rule layer through the drop-in module (cfg0 shape).
+
+    B=1 per rank, a 512-token prefill then 64 decode steps, hidden 2048, bf16,
+    random-init weights.  The input/output projections are torch GEMMs.  The
+    core runs the library's kernels: prologue, chunked prefill or recurrent
+    decode, gated RMSNorm.  One step = one pass (prefill + 64 decode steps),
+    replayed as two CUDA graphs.  Weak scaling: every rank runs its own
+    sequence."""
+    from anemll_b200 import gdn, inputs
+    dev = torch.device("cuda", local)
+    w, hidden = inputs.gdn_layer(seed=1000 * rank)
+    layer = gdn.GatedDeltaNet(dtype=torch.bfloat16, device=dev)
+    _load_layer(layer, w)
+    conv, rec = layer.new_states(1)
+    h = hidden.to(dev)
+    x_pre = h[:, :LAYER_PREFILL].contiguous()
+    x_dec = [h[:, LAYER_PREFILL + i:LAYER_PREFILL + i + 1].contiguous() for i in range(LAYER_DECODE)]
+
+    def run_pre():
+        return layer(x_pre, conv, rec, use_precomputed_states=False)
+
+    def run_dec():
+        return [layer(x, conv, rec, use_precomputed_states=True) for x in x_dec]
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            run_pre()
+            run_dec()
+        torch.cuda.synchronize(dev)
+        g_pre, g_dec = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_pre):
+            y_pre = run_pre()
+        with torch.cuda.graph(g_dec):
+            y_dec = run_dec()
+        g_pre.replay()
+        g_dec.replay()
+        torch.cuda.synchronize(dev)
+    barrier(ws)
+    stream = torch.cuda.current_stream(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # larger than the 126 MB L2
+    pre_ms = dec_ms = 0.0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()  # outside the timed regions
+            e[0].record(stream)
+            g_pre.replay()
+            e[1].record(stream)
+            flush.zero_()
+            e[2].record(stream)
+            g_dec.replay()
+            e[3].record(stream)
+            torch.cuda.synchronize(dev)
+            pre_ms += e[0].elapsed_time(e[1])
+            dec_ms += e[2].elapsed_time(e[3])
+    barrier(ws)
+    if gdn.chunked_device_error(reset=True):
+        raise RuntimeError("chunked prefill reported a device-side wait timeout")
+    tot_ms = max_over_ranks(pre_ms + dec_ms, ws, dev)
+
+    # end to end through the module with host buffers (eager): H2D of the pass's hidden states from
+    # pinned memory, prefill + 64 decode steps, D2H of every layer output
+    hx = hidden.pin_memory()
+    hy = torch.empty(1, LAYER_PREFILL + LAYER_DECODE, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    dx = torch.empty_like(h)
+
+    def e2e_pass():
+        dx.copy_(hx, non_blocking=True)
+        ya = layer(dx[:, :LAYER_PREFILL], conv, rec, use_precomputed_states=False)
+        hy[:, :LAYER_PREFILL].copy_(ya, non_blocking=True)
+        for i in range(LAYER_DECODE):
+            t = LAYER_PREFILL + i
+            yb = layer(dx[:, t:t + 1], conv, rec, use_precomputed_states=True)
+            hy[:, t:t + 1].copy_(yb, non_blocking=True)
+
+    with torch.no_grad():
+        e2e_pass()
+        torch.cuda.synchronize(dev)
+        e2e_passes = min(args.steps, 3)
+        e2e_ms = 0.0
+        for _ in range(e2e_passes):
+            flush.zero_()
+            e[0].record(stream)
+            e2e_pass()
+            e[1].record(stream)
+            torch.cuda.synchronize(dev)
+            e2e_ms += e[0].elapsed_time(e[1])
+    e2e_ms = max_over_ranks(e2e_ms, ws, dev)
+    n_tok = LAYER_PREFILL + LAYER_DECODE
+    pk, how = peaks()
+    tflops = LAYER_PREFILL * layer_flop_per_token() / (pre_ms / args.steps / 1e3) / 1e12
+    gbs = layer_decode_bytes() * LAYER_DECODE / (dec_ms / args.steps / 1e3) / 1e9
+    return {
+        "metric": "gdn_layer_tokens_per_s",
+        "value": ws * n_tok * args.steps / (tot_ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 activations and weights, f32 state",
+        "data": "synthetic (seeded; hidden ~N(0,1), weights ~N(0,0.02), conv ~N(0,0.1), A_log ~U(0, log 16))",
+        "config": {"workload": "gdn_layer", "batch_per_gpu": 1, "prefill": LAYER_PREFILL, "decode_steps": LAYER_DECODE,
+                   "hidden": HIDDEN, "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV, "chunk": CHUNK,
+                   "l2": "flushed (256 MB write) before the prefill and before the decode steps of every timed pass",
+                   "parallelism": f"weak, {ws} independent sequences"},
+        "prefill_ms": pre_ms / args.steps,
+        "decode_us_per_step": dec_ms / args.steps / LAYER_DECODE * 1e3,
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk["bf16_tflops"], "peak_source": how,
+                     "algorithmic_flop_per_prefill": LAYER_PREFILL * layer_flop_per_token(), "traffic": None,
+                     "decode": {"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                                "algorithmic_bytes_per_step": layer_decode_bytes()}},
+        "e2e": {"value": ws * n_tok * e2e_passes / (e2e_ms / 1e3), "unit": "tokens/s", "passes": e2e_passes,
+                "h2d_bytes_per_step": hx.numel() * hx.element_size(),
+                "d2h_bytes_per_step": hy.numel() * hy.element_size()},
+        "gpu_launches": args.steps * (1 + LAYER_DECODE) * 9,
+        "clocks": clk.summary(),
+    }
+
+
+# ------------------------------------------------------------ CPU samples ---
+def cpu_prefill_sample(threads, T=2048):
+    """Oracle chunked prefill of one sequence x T tokens x 32 heads on the host; returns tokens/s."""
+    from anemll_b200 import inputs
+    from oracle import gdn as og
+    torch.set_num_threads(threads)
+    w = inputs.gdn_prefill_device(B=1, T=T, device="cpu")
+    xs = [w[n].float() for n in ("q", "k", "v", "g", "beta")]
+    S0 = torch.zeros(1, H_V, DK, DV)
+    og.chunk_gated_delta_rule(*(x[:, :128] for x in xs), CHUNK, S0)
+    t0 = time.perf_counter()
+    og.chunk_gated_delta_rule(*xs, CHUNK, S0)
+    return T / (time.perf_counter() - t0), f"1 sequence x {T} tokens x {H_V} heads of the fp32 torch CPU oracle"
+
+
+def cpu_kv_sample(threads, window, n_chunks=4, n_dec=8):
+    """Oracle KV attention calls (cfg2 shape) on the host; returns tokens/s."""
+    from anemll_b200 import inputs
+    from oracle import kv_attention as ok
+    torch.set_num_threads(threads)
+    d = inputs.kv_attention()
+    cache = d["cache"].float().clone()
+    pos0 = d["prefill_from"]
+    calls = [(pos0 + 64 * i, 64) for i in range(n_chunks)] + [(d["prefill_to"] + i, 1) for i in range(n_dec)]
+    ntok = sum(n for _, n in calls)
+    t0 = time.perf_counter()
+    for p, n in calls:
+        j = p - pos0
+        ok.kv_attention_step(d["q"][:, :, j:j + n], d["k"][:, :, j:j + n], d["v"][:, :, j:j + n],
+                             d["gate"][:, j:j + n], cache, 0, 1, p, window)
+    return ntok / (time.perf_counter() - t0), (f"{n_chunks} prefill chunks of 64 and {n_dec} decode steps of the "
+                                                "fp32 torch CPU oracle (the reference's own algorithm in fp32)")
+
+
+def cpu_layer_sample(threads, n_dec=8):
+    """Oracle GDN layer (torch projections + oracle core) on the host: 512-token prefill and n_dec steps."""
+    from anemll_b200 import inputs
+    from oracle import gdn as og
+    import torch.nn.functional as F
+    torch.set_num_threads(threads)
+    w, hidden = inputs.gdn_layer()
+    W = {n: w[n].float() for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj")}
+    params = dict(conv_w=w["conv_w"], A_log=w["A_log"], dt_bias=w["dt_bias"], norm_w=w["norm_w"])
+    x = hidden.float()
+
+    def proj(xx):
+        return (F.linear(xx, W["in_proj_qkv"]), F.linear(xx, W["in_proj_z"]), F.linear(xx, W["in_proj_a"]),
+                F.linear(xx, W["in_proj_b"]))
+
+    t0 = time.perf_counter()
+    m, z, a, b = proj(x[:, :LAYER_PREFILL])
+    _, normed, conv, S = og.gdn_layer_prefill(m, z, a, b, params, H_QK, H_V, DK, DV)
+    F.linear(normed.reshape(1, LAYER_PREFILL, -1), W["out_proj"])
+    for i in range(n_dec):
+        m, z, a, b = proj(x[:, LAYER_PREFILL + i:LAYER_PREFILL + i + 1])
+        _, normed, conv, S = og.gdn_layer_decode(m, z, a, b, params, H_QK, H_V, DK, DV, conv, S)
+        F.linear(normed.reshape(1, 1, -1), W["out_proj"])
+    dt = time.perf_counter() - t0
+    return (LAYER_PREFILL + n_dec) / dt, (f"one layer: 512-token prefill and {n_dec} decode steps, torch fp32 "
+                                          "projections with the CPU oracle core")
+
+
 def traffic_from_profiles(name):
     """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")  # "<workload> <bytes per launch>" lines
@@ -528,43 +738,66 @@ def traffic_from_profiles(name):
 
 
 def reference_arm(args, ws, rank):
+    """The CPU path (the oracle port: the reference has no implementation of this path) on the host cores,
+    on the same config, metric and unit as our arm; rank 0 only."""
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    from anemll_b200 import inputs
-    from oracle import gdn as og
-    w = inputs.gdn_decode(B=DECODE_B, steps=DECODE_STEPS)
-    S = w["state"]
-    for i in range(args.warmup):
-        t = i % DECODE_STEPS
-        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        t = i % DECODE_STEPS
-        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
-    dt = time.perf_counter() - t0
-    v = args.steps / dt
+    if args.config == "gdn_decode":
+        from anemll_b200 import inputs
+        from oracle import gdn as og
+        w = inputs.gdn_decode(B=DECODE_B, steps=DECODE_STEPS)
+        S = w["state"]
+        for i in range(args.warmup):
+            t = i % DECODE_STEPS
+            _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            t = i % DECODE_STEPS
+            _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+        dt = time.perf_counter() - t0
+        v, unit, metric, ms = args.steps / dt, "steps/s", "gdn_decode_steps_per_s", dt * 1e3 / args.steps
+        sample = f"{args.steps} full-batch decode steps of the fp32 torch CPU oracle"
+        config = {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
+                  "d_k": DK, "d_v": DV}
+        scaling = "weak"
+    else:
+        vals = []
+        for _ in range(max(1, min(args.steps, 3))):
+            if args.config == "gdn_prefill":
+                v1, sample = cpu_prefill_sample(threads)
+            elif args.config == "kv_attention":
+                v1, sample = cpu_kv_sample(threads, args.window)
+            else:
+                v1, sample = cpu_layer_sample(threads)
+            vals.append(v1)
+        sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8}[args.config]
+        v, unit = max(vals), "tokens/s"
+        ms = sample_tokens / v * 1e3  # one step = one bounded sample
+        metric = {"gdn_prefill": "gdn_prefill_tokens_per_s", "kv_attention": "kv_attention_tokens_per_s",
+                  "gdn_layer": "gdn_layer_tokens_per_s"}[args.config]
+        config = {"workload": {"gdn_prefill": "gdn_chunked_prefill", "kv_attention": "kv_cache_attention",
+                               "gdn_layer": "gdn_layer"}[args.config], "sample": sample}
+        scaling = "strong" if args.config != "gdn_layer" else "weak"
+        sample = sample + f", best of {len(vals)}"
     return {
         "impl": "reference",
-        "metric": "gdn_decode_steps_per_s",
+        "metric": metric,
         "value": v,
-        "unit": "steps/s",
+        "unit": unit,
         "n_gpus": ws,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": dt * 1e3 / args.steps,
+        "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded)",
-        "config": {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
-                   "d_k": DK, "d_v": DV},
-        "cpu_baseline": {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} full-batch decode steps of the fp32 torch CPU oracle "
-                                   "(the reference has no implementation of this path)"},
-        "e2e": {"value": v, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": config,
+        "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
@@ -574,7 +807,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2560)
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="gdn_decode", choices=["gdn_decode", "gdn_prefill", "kv_attention"])
+    ap.add_argument("--config", default="gdn_decode",
+                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer"])
     ap.add_argument("--window", type=int, default=0, help="kv_attention: sliding window (0 = causal)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
@@ -590,19 +824,26 @@ def main():
                 res = bench_kv_attention(args, ws, rank, local)
             elif args.config == "gdn_prefill":
                 res = bench_gdn_prefill(args, ws, rank, local)
-                res["roofline"]["traffic"] = traffic_from_profiles("gdn_chunked_prefill")
+            elif args.config == "gdn_layer":
+                res = bench_gdn_layer(args, ws, rank, local)
             else:
                 res = bench_gdn_decode(args, ws, rank, local)
                 res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
-            if rank == 0 and args.config == "gdn_decode":
-                if ws == 1:
+            if rank == 0:
+                res["cpu_baseline"] = None
+                if ws == 1:  # the host sample runs at N=1 only
                     threads = os.cpu_count() or 1
-                    v = cpu_decode_sample(args.cpu_baseline_steps, threads)
-                    res["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
-                                           "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode steps of "
-                                                     "the fp32 torch CPU oracle"}
-                else:
-                    res["cpu_baseline"] = None
+                    if args.config == "gdn_decode":
+                        v = cpu_decode_sample(args.cpu_baseline_steps, threads)
+                        res["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
+                                               "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode "
+                                                         "steps of the fp32 torch CPU oracle"}
+                    else:
+                        v, sample = {"gdn_prefill": lambda: cpu_prefill_sample(threads),
+                                     "kv_attention": lambda: cpu_kv_sample(threads, args.window),
+                                     "gdn_layer": lambda: cpu_layer_sample(threads)}[args.config]()
+                        res["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                                               "sample": sample}
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:
