@@ -413,8 +413,7 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 
     // ---------------- T = (I + A)^-1 -> T1 = T diag(beta), T2 = T diag(beta e^G rk), hi|lo ----------------
     // (1) threads 0-63: diagonal 16x16 blocks, thread (blk, j) solves column j by right-looking
-    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo); threads 64-127 zero the
-    //     two upper blocks of T that the merges read
+    //     substitution and writes it to T (fp16) and T1, T2 (hi|lo)
     if (tid < 64) {
       const int o = (tid >> 4) * 16, j = tid & 15;
       const float* ab = sAd + (tid >> 4) * AD_BLK;  // column kk at ab + 16 kk
@@ -449,100 +448,112 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         *reinterpret_cast<TIn*>(sm + OFF_T2H + off) = h2;
         *reinterpret_cast<TIn*>(sm + OFF_T2L + off) = from_f32<TIn>(v2 - to_f32(h2));
       }
-    } else {
-      // T blocks (0,1) and (2,3), which the 32 -> 64 merge reads as zeros (T1, T2 need no zeros:
-      // the products that use them skip the blocks above the diagonal)
-      const int u = tid - 64;
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      if (u < 64) {
-        const int r = (u >> 1) & 15, ch = ((u >> 5) ? 6 : 2) + (u & 1), ro = (u >> 5) ? 32 : 0;
-        *reinterpret_cast<uint4*>(sm + OFF_T16 + sw(ro + r, ch)) = z;
-      }
     }
     __syncthreads();
     const int g8 = lane >> 2, t4 = lane & 3;  // mma.sync fragment coordinates
-    // (2) 16 -> 32 (warps 0, 1: blocks (1,0) and (3,2)):  X^T = T_cc^T A_rc^T,  T_rc = -T_rr X
-    if (warp < 2) {
-      const int rr0 = warp ? 48 : 16, cc0 = warp ? 32 : 0;
-      uint32_t at[4], bA[4], aR[4];
-      ldmatrix_x4_trans(at, sm + OFF_T16 + sw(cc0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
-      ldmatrix_x4(bA, sm + OFF_A16 + sw(rr0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
-      ldmatrix_x4(aR, sm + OFF_T16 + sw(rr0 + (lane & 15), (rr0 >> 3) + (lane >> 4)));
-      float xt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      mma_16816<__half>(xt[0], at, bA[0], bA[1]);
-      mma_16816<__half>(xt[1], at, bA[2], bA[3]);
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        float o4[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t b0 = pack2<__half>(xt[0][2 * nt], xt[0][2 * nt + 1]);
-        const uint32_t b1 = pack2<__half>(xt[1][2 * nt], xt[1][2 * nt + 1]);
-        mma_16816<__half>(o4, aR, b0, b1);
-        const int col = cc0 + 8 * nt + 2 * t4;
-        const float s1a = sBeta[col], s1b = sBeta[col + 1], s2a = sT2s[col], s2b = sT2s[col + 1];
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float va = -o4[2 * hh], vb = -o4[2 * hh + 1];
-          const uint32_t off = sw_elem(rr0 + g8 + 8 * hh, col);
-          *reinterpret_cast<uint32_t*>(sm + OFF_T16 + off) = pack2<__half>(va, vb);
-          uint32_t hi, lo;
-          split2<TIn>(va * s1a, vb * s1b, hi, lo);
-          *reinterpret_cast<uint32_t*>(sm + OFF_T1H + off) = hi;
-          *reinterpret_cast<uint32_t*>(sm + OFF_T1L + off) = lo;
-          split2<TIn>(va * s2a, vb * s2b, hi, lo);
-          *reinterpret_cast<uint32_t*>(sm + OFF_T2H + off) = hi;
-          *reinterpret_cast<uint32_t*>(sm + OFF_T2L + off) = lo;
-        }
-      }
-    }
-    __syncthreads();
-    // (3) 32 -> 64 (all warps; warp = (row half mt, column half nh) of T[32:64, 0:32]):
-    //     Y^T = T00^T A10^T (rows nh*16.. of Y^T), T[32+16mt.., 16nh..] = -T11 Y
+    // (2) 16 -> 32 -> 64 in one pass (warps 0-3; warp = (row half mt, column half nh) of
+    //     T[32:64, 0:32]):  Y^T = T[0:32,0:32]^T A[32:64,0:32]^T (rows 16 nh.. of Y^T) and
+    //     T[32+16mt.., 16nh..] = -T[32+16mt.., 32:64] Y.  The 16 -> 32 blocks are formed in registers by
+    //     the warps that need them: T10 = -T11' (A10 T00') by the warps with nh = 0 (as the transposed
+    //     A operand of Y^T, via movmatrix), T32 = -T33' (A32 T22') by the warps with mt = 1 (as the
+    //     A operand of the second product).  The zero blocks (0,1), (2,3) of T are skipped, not read.
     if (warp < 4) {
       const int nh = warp & 1, mt = warp >> 1;
+      // -T_rr (A_rc T_cc) for the 16x16 block (rr0, cc0), as C fragments
+      auto level1 = [&](int rr0, int cc0, float (&c)[2][4]) {
+        uint32_t at[4], bA[4], aR[4];
+        ldmatrix_x4_trans(at, sm + OFF_T16 + sw(cc0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
+        ldmatrix_x4(bA, sm + OFF_A16 + sw(rr0 + (lane & 7) + ((lane >> 4) << 3), (cc0 >> 3) + ((lane >> 3) & 1)));
+        ldmatrix_x4(aR, sm + OFF_T16 + sw(rr0 + (lane & 15), (rr0 >> 3) + (lane >> 4)));
+        float xt[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};  // X^T = T_cc^T A_rc^T
+        mma_16816<__half>(xt[0], at, bA[0], bA[1]);
+        mma_16816<__half>(xt[1], at, bA[2], bA[3]);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          c[nt][0] = c[nt][1] = c[nt][2] = c[nt][3] = 0.f;
+          mma_16816<__half>(c[nt], aR, pack2<__half>(xt[0][2 * nt], xt[0][2 * nt + 1]),
+                            pack2<__half>(xt[1][2 * nt], xt[1][2 * nt + 1]));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c[nt][e] = -c[nt][e];
+        }
+      };
+      // T1, T2 (hi|lo) of the 16x16 block at (r0, c0) from C fragments
+      auto store_t12 = [&](const float (&c)[2][4], int r0, int c0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const int col = c0 + 8 * nt + 2 * t4;
+          const float s1a = sBeta[col], s1b = sBeta[col + 1], s2a = sT2s[col], s2b = sT2s[col + 1];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float va = c[nt][2 * hh], vb = c[nt][2 * hh + 1];
+            const uint32_t off = sw_elem(r0 + g8 + 8 * hh, col);
+            uint32_t hi, lo;
+            split2<TIn>(va * s1a, vb * s1b, hi, lo);
+            *reinterpret_cast<uint32_t*>(sm + OFF_T1H + off) = hi;
+            *reinterpret_cast<uint32_t*>(sm + OFF_T1L + off) = lo;
+            split2<TIn>(va * s2a, vb * s2b, hi, lo);
+            *reinterpret_cast<uint32_t*>(sm + OFF_T2H + off) = hi;
+            *reinterpret_cast<uint32_t*>(sm + OFF_T2L + off) = lo;
+          }
+        }
+      };
+      // Y^T rows 16 nh..: k-steps over k = rows of T[0:32,0:32] (16 each) against A[32:64,0:32]^T
       float yt[4][4];
 #pragma unroll
       for (int n = 0; n < 4; ++n) yt[n][0] = yt[n][1] = yt[n][2] = yt[n][3] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        uint32_t at[4];
-        ldmatrix_x4_trans(at, sm + OFF_T16 + sw(16 * ks + (lane & 7) + ((lane >> 4) << 3), 2 * nh + ((lane >> 3) & 1)));
+      auto y_step = [&](const uint32_t (&aT)[4], int ks) {
 #pragma unroll
         for (int ap = 0; ap < 2; ++ap) {
           uint32_t bA[4];
           ldmatrix_x4(bA, sm + OFF_A16 + sw(32 + 16 * ap + (lane & 7) + ((lane >> 4) << 3), 2 * ks + ((lane >> 3) & 1)));
-          mma_16816<__half>(yt[2 * ap], at, bA[0], bA[1]);
-          mma_16816<__half>(yt[2 * ap + 1], at, bA[2], bA[3]);
+          mma_16816<__half>(yt[2 * ap], aT, bA[0], bA[1]);
+          mma_16816<__half>(yt[2 * ap + 1], aT, bA[2], bA[3]);
         }
+      };
+      if (nh == 0) {
+        float t10[2][4];
+        level1(16, 0, t10);
+        if (mt == 0) store_t12(t10, 16, 0);
+        uint32_t at[4];  // k = 0..15: diagonal block 0, transposed
+        ldmatrix_x4_trans(at, sm + OFF_T16 + sw((lane & 7) + ((lane >> 4) << 3), (lane >> 3) & 1));
+        y_step(at, 0);
+        const uint32_t a1[4] = {movmatrix_trans(pack2<__half>(t10[0][0], t10[0][1])),
+                                movmatrix_trans(pack2<__half>(t10[1][0], t10[1][1])),
+                                movmatrix_trans(pack2<__half>(t10[0][2], t10[0][3])),
+                                movmatrix_trans(pack2<__half>(t10[1][2], t10[1][3]))};  // k = 16..31: T10^T
+        y_step(a1, 1);
+      } else {
+        uint32_t at[4];  // k = 0..15: block (0,1) = 0;  k = 16..31: diagonal block 1, transposed
+        ldmatrix_x4_trans(at, sm + OFF_T16 + sw(16 + (lane & 7) + ((lane >> 4) << 3), 2 + ((lane >> 3) & 1)));
+        y_step(at, 1);
       }
       float o4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      auto t_step = [&](const uint32_t (&aR)[4], int ks) {  // k = Y rows 16 ks..16 ks + 15
 #pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        uint32_t aR[4];
-        ldmatrix_x4(aR, sm + OFF_T16 + sw(32 + 16 * mt + (lane & 15), 4 + 2 * ks + (lane >> 4)));
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const uint32_t b0 = pack2<__half>(yt[2 * ks][2 * nt], yt[2 * ks][2 * nt + 1]);
-          const uint32_t b1 = pack2<__half>(yt[2 * ks + 1][2 * nt], yt[2 * ks + 1][2 * nt + 1]);
-          mma_16816<__half>(o4[nt], aR, b0, b1);
-        }
+        for (int nt = 0; nt < 2; ++nt)
+          mma_16816<__half>(o4[nt], aR, pack2<__half>(yt[2 * ks][2 * nt], yt[2 * ks][2 * nt + 1]),
+                            pack2<__half>(yt[2 * ks + 1][2 * nt], yt[2 * ks + 1][2 * nt + 1]));
+      };
+      if (mt == 0) {
+        uint32_t aR[4];  // rows 32-47: diagonal block 2; block (2,3) = 0
+        ldmatrix_x4(aR, sm + OFF_T16 + sw(32 + (lane & 15), 4 + (lane >> 4)));
+        t_step(aR, 0);
+      } else {
+        float t32[2][4];
+        level1(48, 32, t32);
+        if (nh == 1) store_t12(t32, 48, 32);
+        const uint32_t a0[4] = {pack2<__half>(t32[0][0], t32[0][1]), pack2<__half>(t32[0][2], t32[0][3]),
+                                pack2<__half>(t32[1][0], t32[1][1]), pack2<__half>(t32[1][2], t32[1][3])};
+        t_step(a0, 0);
+        uint32_t aR[4];  // rows 48-63, k = 16..31: diagonal block 3
+        ldmatrix_x4(aR, sm + OFF_T16 + sw(48 + (lane & 15), 6 + (lane >> 4)));
+        t_step(aR, 1);
       }
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int col = 16 * nh + 8 * nt + 2 * t4;
-        const float s1a = sBeta[col], s1b = sBeta[col + 1], s2a = sT2s[col], s2b = sT2s[col + 1];
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float va = -o4[nt][2 * hh], vb = -o4[nt][2 * hh + 1];
-          const uint32_t off = sw_elem(32 + 16 * mt + g8 + 8 * hh, col);
-          uint32_t hi, lo;
-          split2<TIn>(va * s1a, vb * s1b, hi, lo);
-          *reinterpret_cast<uint32_t*>(sm + OFF_T1H + off) = hi;
-          *reinterpret_cast<uint32_t*>(sm + OFF_T1L + off) = lo;
-          split2<TIn>(va * s2a, vb * s2b, hi, lo);
-          *reinterpret_cast<uint32_t*>(sm + OFF_T2H + off) = hi;
-          *reinterpret_cast<uint32_t*>(sm + OFF_T2L + off) = lo;
-        }
-      }
+        for (int e = 0; e < 4; ++e) o4[nt][e] = -o4[nt][e];
+      store_t12(o4, 32 + 16 * mt, 16 * nh);
     }
     // v of this chunk must have landed before U
     if (!__syncthreads_and(tc::mbar_wait(vb, (uint32_t)(c & 1)))) {

@@ -61,4 +61,12 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Transpose of an 8x8 16-bit matrix held in the mma fragment layout (thread t: row t/4,
+// columns 2(t%4) and 2(t%4)+1), returned in the same layout (PTX movmatrix).
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(d) : "r"(a));
+  return d;
+}
+
 }  // namespace anemll
