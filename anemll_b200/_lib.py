@@ -35,6 +35,11 @@ _SIGS = {
                              _vp, _c_size, _vp], _c_int),
     "anemll_kv_attention_noalloc_max_scratch": ([], _c_size),
     "anemll_kv_attention_error": ([_c_int], _c_int),
+    "anemll_kv_update_mask": ([_vp, _vp, _c_int, _vp, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_i64, _c_i64,
+                               _vp], _c_int),
+    "anemll_kv_rotate_append": ([_vp, _vp, _c_int, _c_i64, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp], _c_int),
+    "anemll_kv_state_transition": ([_vp, _c_int, _vp, _c_int, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_float,
+                                    _vp], _c_int),
     "anemll_kv_attention_noalloc": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp, _c_int,
                                      _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp],
                                     _c_int),

@@ -7,7 +7,7 @@ step of the whole batch = one kernel launch.  Weak scaling: every rank owns
 its own batch of 64 sequences; no collective on the data path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer]
+                  [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer|cache_ops]
 
 ``--impl reference`` times the CPU oracle of the same path on the host cores
 (the reference has no GPU implementation of this path), rank 0 only.
@@ -661,6 +661,97 @@ def bench_gdn_layer(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------- cache ops ----
+def bench_cache_ops(args, ws, rank, local):
+    """Cache-management ops on a Gemma3-style split cache (HBM-bound copies).
+
+    One step = one decode-step's rotating update of all 18 local layers (window 512, 1 kv head,
+    hd 256, fp16; key and value slots, one call per layer), one 64-token update-mask write into
+    every local layer, and one resize of a 36-layer state [36, 1, 1024, 256] to 4096 rows
+    (current position 1000).  Calls replay as one CUDA graph; L2 flushed between steps.
+    Weak scaling (replicas)."""
+    from anemll_b200 import _lib as lib, cache_ops
+    dev = torch.device("cuda", local)
+    g = torch.Generator().manual_seed(6 + rank)
+    nl, H, sw, hd = 18, 1, 512, 256
+    kv = torch.randn(2 * nl, H, sw, hd, generator=g).half().to(dev)
+    key = torch.randn(1, H, 1, hd, generator=g).half().to(dev)
+    val = torch.randn(1, H, 1, hd, generator=g).half().to(dev)
+    new = torch.randn(2, H, 64, hd, generator=g).half().to(dev)
+    mask = torch.zeros(1, 1, sw, 64, dtype=torch.half)
+    for t in range(64):
+        mask[0, 0, 200 + t, t] = 1
+    mask = mask.to(dev)
+    st = torch.randn(36, 1, 1024, 256, generator=g).half().to(dev)
+    out = torch.empty(36, 1, 4096, 256, dtype=torch.half, device=dev)
+
+    def step():
+        for i in range(nl):
+            cache_ops.update_kv_local_(kv, i, nl, key, val, 1)
+        for i in range(nl):
+            cache_ops.apply_update_mask_(kv[i:i + 1], new[0:1], mask)
+            cache_ops.apply_update_mask_(kv[i + nl:i + nl + 1], new[1:2], mask)
+        rc = lib.load().anemll_kv_state_transition(lib.ptr(st), lib.F16, lib.ptr(out), lib.F16, 36, 1024, 4096, 256,
+                                                   1000, 0.0, lib.stream_ptr(dev))
+        lib.check(rc, "anemll_kv_state_transition")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ms = 0.0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms += e0.elapsed_time(e1)
+    barrier(ws)
+    ms_max = max_over_ranks(ms, ws, dev)
+    es = 2
+    b_rot = nl * 2 * H * 2 * sw * hd * es            # every slot read and written once
+    b_mask = nl * 2 * H * 3 * 64 * hd * es            # new rows read, touched rows read and written
+    b_tr = 36 * (1000 * 256 + 4096 * 256) * es        # valid rows read, the whole target written
+    bytes_step = b_rot + b_mask + b_tr
+    pk, how = peaks()
+    gbs = bytes_step / (ms / args.steps / 1e3) / 1e9
+    return {
+        "metric": "kv_cache_ops_bytes_per_s",
+        "value": ws * bytes_step * args.steps / (ms_max / 1e3) / 1e9,
+        "unit": "GB/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "kv_cache_ops", "local_layers": nl, "window": sw, "H_kv": H, "head_dim": hd,
+                   "mask_tokens": 64, "resize": "36x1x1024x256 -> 4096 rows, position 1000",
+                   "calls_per_step": 2 * nl + 2 * nl + 1,
+                   "l2": "flushed (256 MB write) before every timed step",
+                   "parallelism": f"weak, {ws} replicas"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / pk["hbm_gbs"], "peak_source": how, "algorithmic_bytes_per_step": bytes_step,
+                     "traffic": None,
+                     "bytes": {"rotate": b_rot, "update_mask": b_mask, "transition": b_tr}},
+        "gpu_launches": args.steps * (2 * nl + 2 * nl + 1),
+        "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------------------ CPU samples ---
 def cpu_prefill_sample(threads, T=2048):
     """Oracle chunked prefill of one sequence x T tokens x 32 heads on the host; returns tokens/s."""
@@ -693,6 +784,30 @@ def cpu_kv_sample(threads, window, n_chunks=4, n_dec=8):
                              d["gate"][:, j:j + n], cache, 0, 1, p, window)
     return ntok / (time.perf_counter() - t0), (f"{n_chunks} prefill chunks of 64 and {n_dec} decode steps of the "
                                                 "fp32 torch CPU oracle (the reference's own algorithm in fp32)")
+
+
+def cpu_cache_ops_sample(threads):
+    """The same cache-op step with the oracle's torch ops on the host cores; returns GB/s."""
+    from oracle import cache_ops as oc
+    torch.set_num_threads(threads)
+    nl, H, sw, hd = 18, 1, 512, 256
+    kv = torch.randn(2 * nl, H, sw, hd).half()
+    key = torch.randn(1, H, 1, hd).half()
+    new = torch.randn(1, H, 64, hd).half()
+    mask = torch.zeros(sw, 64)
+    for t in range(64):
+        mask[200 + t, t] = 1
+    st = torch.randn(36, 1, 1024, 256).half()
+    t0 = time.perf_counter()
+    for i in range(2 * nl):
+        kv[i:i + 1] = oc.rotate_append(kv[i:i + 1], key, 1)
+    for i in range(2 * nl):
+        kv[i:i + 1] = oc.update_mask_write(kv[i:i + 1], new, mask).half()
+    oc.transition_state(st, 4096, 1000)
+    dt = time.perf_counter() - t0
+    es = 2
+    byts = nl * 2 * H * 2 * sw * hd * es + nl * 2 * H * 3 * 64 * hd * es + 36 * (1000 * 256 + 4096 * 256) * es
+    return byts / dt / 1e9, "one step of the same cache ops with the oracle's torch CPU ops"
 
 
 def cpu_layer_sample(threads, n_dec=8):
@@ -769,17 +884,23 @@ def reference_arm(args, ws, rank):
                 v1, sample = cpu_prefill_sample(threads)
             elif args.config == "kv_attention":
                 v1, sample = cpu_kv_sample(threads, args.window)
+            elif args.config == "cache_ops":
+                v1, sample = cpu_cache_ops_sample(threads)
             else:
                 v1, sample = cpu_layer_sample(threads)
             vals.append(v1)
-        sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8}[args.config]
-        v, unit = max(vals), "tokens/s"
-        ms = sample_tokens / v * 1e3  # one step = one bounded sample
+        if args.config == "cache_ops":
+            v, unit = max(vals), "GB/s"
+            ms = None
+        else:
+            sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8}[args.config]
+            v, unit = max(vals), "tokens/s"
+            ms = sample_tokens / v * 1e3  # one step = one bounded sample
         metric = {"gdn_prefill": "gdn_prefill_tokens_per_s", "kv_attention": "kv_attention_tokens_per_s",
-                  "gdn_layer": "gdn_layer_tokens_per_s"}[args.config]
+                  "gdn_layer": "gdn_layer_tokens_per_s", "cache_ops": "kv_cache_ops_bytes_per_s"}[args.config]
         config = {"workload": {"gdn_prefill": "gdn_chunked_prefill", "kv_attention": "kv_cache_attention",
-                               "gdn_layer": "gdn_layer"}[args.config], "sample": sample}
-        scaling = "strong" if args.config != "gdn_layer" else "weak"
+                               "gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops"}[args.config], "sample": sample}
+        scaling = "strong" if args.config in ("gdn_prefill", "kv_attention") else "weak"
         sample = sample + f", best of {len(vals)}"
     return {
         "impl": "reference",
@@ -808,7 +929,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=32)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="gdn_decode",
-                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer"])
+                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer", "cache_ops"])
     ap.add_argument("--window", type=int, default=0, help="kv_attention: sliding window (0 = causal)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
@@ -826,6 +947,8 @@ def main():
                 res = bench_gdn_prefill(args, ws, rank, local)
             elif args.config == "gdn_layer":
                 res = bench_gdn_layer(args, ws, rank, local)
+            elif args.config == "cache_ops":
+                res = bench_cache_ops(args, ws, rank, local)
             else:
                 res = bench_gdn_decode(args, ws, rank, local)
                 res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
@@ -833,7 +956,11 @@ def main():
                 res["cpu_baseline"] = None
                 if ws == 1:  # the host sample runs at N=1 only
                     threads = os.cpu_count() or 1
-                    if args.config == "gdn_decode":
+                    if args.config == "cache_ops":
+                        v, sample = cpu_cache_ops_sample(threads)
+                        res["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
+                                               "sample": sample}
+                    elif args.config == "gdn_decode":
                         v = cpu_decode_sample(args.cpu_baseline_steps, threads)
                         res["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
                                                "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode "

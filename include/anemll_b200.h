@@ -70,8 +70,9 @@ int anemll_gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dt
 
 /*
  * Gated delta rule, chunked prefill: chunks of chunk_size tokens in the WY/UT
- * form on the tcgen05 tensor cores (fp16 operands, fp32 accumulators), the
- * fp32 state carried across chunks in tensor memory.  Replaces
+ * form on the tcgen05 tensor cores (q/k/v as given; the derived operands that
+ * multiply them split into hi and lo parts of the same type; fp32
+ * accumulators), the fp32 state carried across chunks in tensor memory.  Replaces
  * torch_chunk_gated_delta_rule (transformers 5.5.0 modeling_qwen3_5.py:234-311).
  * q/k/v are ANEMLL_F16 or ANEMLL_BF16; T may be any length (a ragged last
  * chunk is a shorter chunk).  chunk_size == 64, d_k == d_v == 128.
@@ -180,6 +181,42 @@ int anemll_kv_attention_noalloc(const void* q, const void* k_new, const void* v_
                                 void* out, int dtype,
                                 int B, int S, int H_q, int H_kv, int head_dim, int ctx,
                                 int current_pos, int window, int window_chunk_aligned, void* stream);
+
+/*
+ * Cache-management ops: ANEMLL-format caches (linear rows, oldest first) updated on the device.
+ * A "slab" is one (layer, kv head) slice of L rows x d elements; slabs are cache_slab_stride
+ * elements apart (new rows: new_slab_stride).  dtype: ANEMLL_F32 / F16 / BF16.
+ *
+ * anemll_kv_update_mask: the reference's one-hot update-mask write, in place:
+ *   cache[l] = cache[l] * (1 - min(sum_s mask[l][s], 1)) + sum_s new[s] * mask[l][s]  (fp32 math),
+ * with mask [L, S] (mask_row_stride elements between rows) shared by every slab.  Replaces
+ * Gemma3Model._apply_update_mask / _apply_update_mask_batch (anemll/models/gemma3_model.py:932-965)
+ * as used by _fill_kv_local / _store_kv_local_prefill_masked (967-1022).  For 0/1 masks the values
+ * equal the reference's (a zero may differ in sign); rows the mask does not touch are not written.
+ */
+int anemll_kv_update_mask(void* cache, const void* new_rows, int dtype, const void* mask, int mask_dtype,
+                          int64_t mask_row_stride, int64_t n_slabs, int L, int S, int d,
+                          int64_t cache_slab_stride, int64_t new_slab_stride, void* stream);
+
+/*
+ * Rotating sliding-window update, in place: every slab is shifted left by n rows (the oldest n
+ * dropped) and new rows [0, n) are stored at rows [L - n, L).  Replaces Gemma3Model._update_kv_local
+ * (n = 1, gemma3_model.py:1024-1066) and _update_kv_local_prefill (n = the prefill batch, 1167-1204).
+ * Windows up to 6400 rows (each CTA stages a 32-byte-wide strip of the L rows in shared memory);
+ * pointers and slab strides 16-byte aligned, rows whole 16-byte units.
+ */
+int anemll_kv_rotate_append(void* cache, const void* new_rows, int dtype, int64_t n_slabs, int L, int n, int d,
+                            int64_t cache_slab_stride, int64_t new_slab_stride, void* stream);
+
+/*
+ * KV-state transition between context sizes: dst [n_slabs][dst_len][d] receives rows
+ * [0, current_position) of src [n_slabs][src_len][d] converted to dst_dtype (round to nearest)
+ * and pad_value (an fp32 value, converted the same way) everywhere else.  Covers
+ * transition_kv_state (expand, anemll/utils/state_transition.py:62-152) and compact_kv_state
+ * (shrink with zero padding, 153-357).  dst must not overlap src; both contiguous.
+ */
+int anemll_kv_state_transition(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n_slabs,
+                               int src_len, int dst_len, int d, int current_position, float pad_value, void* stream);
 
 #ifdef __cplusplus
 }
