@@ -21,6 +21,7 @@ _c_int, _c_i64, _c_float, _vp, _c_size = ctypes.c_int, ctypes.c_int64, ctypes.c_
 _SIGS = {
     "anemll_last_error": ([], ctypes.c_char_p),
     "anemll_version": ([], _c_int),
+    "anemll_launch_count": ([], ctypes.c_longlong),
     "anemll_gdn_recurrent": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int,
                               _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp], _c_int),
     "anemll_gdn_chunked_prefill": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int,
@@ -73,6 +74,11 @@ def load() -> ctypes.CDLL:
 
 def exported_symbols():
     return list(_SIGS)
+
+
+def launch_count() -> int:
+    """Kernel launches issued through the library so far in this process (graph replays excluded)."""
+    return int(load().anemll_launch_count())
 
 
 def check(rc: int, what: str) -> None:

@@ -1,9 +1,12 @@
-// Error reporting shared by all entry points of the C ABI.
+// Error reporting shared by all entry points of the C ABI, and the count of kernel launches.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace anemll {
 
 static thread_local char g_last_error[512] = "";
+static std::atomic<long long> g_launches{0};
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -18,6 +21,7 @@ int launch_status(const char* what) {
     set_error("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
     return (int)e;
   }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return ANEMLL_OK;
 }
 
@@ -26,3 +30,5 @@ int launch_status(const char* what) {
 extern "C" const char* anemll_last_error(void) { return anemll::g_last_error; }
 
 extern "C" int anemll_version(void) { return 1; }
+
+extern "C" long long anemll_launch_count(void) { return anemll::g_launches.load(std::memory_order_relaxed); }

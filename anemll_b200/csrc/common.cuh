@@ -24,7 +24,7 @@ void set_error(const char* fmt, ...);
     }                                        \
   } while (0)
 
-// Map a launch/runtime error to the positive status range.
+// Map a launch/runtime error to the positive status range (success: counts one kernel launch).
 int launch_status(const char* what);
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

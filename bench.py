@@ -7,7 +7,7 @@ step of the whole batch = one kernel launch.  Weak scaling: every rank owns
 its own batch of 64 sequences; no collective on the data path.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer|cache_ops]
+                  [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer|cache_ops|stack]
 
 ``--impl reference`` times the CPU oracle of the same path on the host cores
 (the reference has no GPU implementation of this path), rank 0 only.
@@ -406,9 +406,12 @@ def bench_kv_attention(args, ws, rank, local):
 
     pre = list(zip(calls, outs[:len(calls)]))
     dcd = list(zip(dec, outs[len(calls):]))
+    from anemll_b200 import _lib
     for _ in range(args.warmup):
+        c0 = _lib.launch_count()
         run(pre)
         run(dcd)
+        launches_pass = _lib.launch_count() - c0  # the library's kernels of one pass (counted on the host)
     torch.cuda.synchronize(dev)
     # the 31 prefill calls and the 64 decode calls replay as CUDA graphs (as a serving loop would)
     g_pre, g_dec = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
@@ -508,7 +511,7 @@ def bench_kv_attention(args, ws, rank, local):
                                 "traffic_per_step": traffic_from_profiles("kv_decode_step") if not window else None}},
         "e2e": {"value": n_tok * e2e_passes / (e2e_ms / 1e3) * (1 if ws <= 2 else ws / 2), "unit": "tokens/s",
                 "passes": e2e_passes, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * (len(calls) + len(dec)) * 2,
+        "gpu_launches": args.steps * launches_pass,
         "clocks": clk.summary(),
     }
 
@@ -561,10 +564,13 @@ def bench_gdn_layer(args, ws, rank, local):
     def run_dec():
         return [layer(x, conv, rec, use_precomputed_states=True) for x in x_dec]
 
+    from anemll_b200 import _lib
     with torch.no_grad():
         for _ in range(args.warmup):
+            c0 = _lib.launch_count()
             run_pre()
             run_dec()
+            launches_pass = _lib.launch_count() - c0  # the library's kernels of one pass (counted on the host)
         torch.cuda.synchronize(dev)
         g_pre, g_dec = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_pre):
@@ -656,7 +662,7 @@ def bench_gdn_layer(args, ws, rank, local):
         "e2e": {"value": ws * n_tok * e2e_passes / (e2e_ms / 1e3), "unit": "tokens/s", "passes": e2e_passes,
                 "h2d_bytes_per_step": hx.numel() * hx.element_size(),
                 "d2h_bytes_per_step": hy.numel() * hy.element_size()},
-        "gpu_launches": args.steps * (1 + LAYER_DECODE) * 9,
+        "gpu_launches": args.steps * launches_pass,
         "clocks": clk.summary(),
     }
 
@@ -752,6 +758,152 @@ def bench_cache_ops(args, ws, rank, local):
     }
 
 
+# ------------------------------------------------------------- hybrid stack --
+STACK_B, STACK_PREFILL, STACK_DECODE, STACK_SEED = 128, 1024, 256, 4
+
+
+def stack_linear_params(cfg):
+    """Weights one token's pass multiplies (every layer's projections and MLP; LM head separate)."""
+    gdn = cfg.hidden * (2 * cfg.H_qk * cfg.d_k + 2 * cfg.H_v * cfg.d_v + 2 * cfg.H_v) + cfg.H_v * cfg.d_v * cfg.hidden
+    att = cfg.hidden * (2 * cfg.H_q * cfg.head_dim + 2 * cfg.H_kv * cfg.head_dim) + cfg.H_q * cfg.head_dim * cfg.hidden
+    mlp = 3 * cfg.hidden * cfg.ffn
+    n_att = sum(cfg.is_attention(i) for i in range(cfg.n_layers))
+    return (cfg.n_layers - n_att) * gdn + n_att * att + cfg.n_layers * mlp, n_att
+
+
+def stack_prefill_flop(cfg, B, T):
+    """Algorithmic FLOPs of the prefill: projections/MLP per token, the GDN core per token and head,
+    causal attention (4*hd per visible key per query head), the LM head once per sequence."""
+    lin, n_att = stack_linear_params(cfg)
+    n_gdn = cfg.n_layers - n_att
+    attn = n_att * 4 * cfg.head_dim * cfg.H_q * (T * (T + 1) // 2)
+    return B * (T * (2 * lin + n_gdn * cfg.H_v * PREFILL_FLOP_PER_TOKEN_HEAD) + attn + 2 * cfg.hidden * cfg.vocab)
+
+
+def stack_decode_bytes(cfg, B, pos):
+    """Algorithmic HBM bytes of one decode step at position ``pos``: bf16 weights (LM head included)
+    once, every GDN layer's f32 state read and written, every attention layer's K and V rows [0, pos]
+    read and row pos written, conv states read and written."""
+    lin, n_att = stack_linear_params(cfg)
+    n_gdn = cfg.n_layers - n_att
+    conv_dim = 2 * cfg.H_qk * cfg.d_k + cfg.H_v * cfg.d_v
+    w = 2 * (lin + cfg.hidden * cfg.vocab)
+    st = n_gdn * B * (2 * cfg.H_v * cfg.d_k * cfg.d_v * 4 + 2 * conv_dim * 4 * 2)
+    kv = n_att * B * 2 * cfg.H_kv * (pos + 2) * cfg.head_dim * 2
+    return w + st + kv
+
+
+def bench_stack(args, ws, rank, local):
+    """The hybrid decoder stack end to end: 24 layers (18 gated-DeltaNet, 6 gated full attention),
+    hidden 2048, SwiGLU 6144, vocab 151936, bf16, random N(0, 0.02) weights (seed 4).  Job: 128
+    sequences of 1024 uniform random prompt tokens, prefill, then 256 greedy decode steps.  The
+    sequences are split evenly over the ranks; after every step the ranks all-gather the next-token
+    ids (NCCL).  One step = one whole pass (prefill + 256 decode steps); the decode steps replay one
+    CUDA graph per position.  Strong scaling (the job is fixed)."""
+    from anemll_b200 import gdn
+    from anemll_b200.stack import GreedyDecoder, HybridStack, StackConfig, nccl_id_gather, shard
+    dev = torch.device("cuda", local)
+    cfg = StackConfig()
+    model = HybridStack(cfg, device=dev).init_weights(STACK_SEED)
+    g = torch.Generator().manual_seed(STACK_SEED)
+    prompt_job = torch.randint(0, cfg.vocab, (STACK_B, STACK_PREFILL), generator=g)
+    lo, hi = shard(STACK_B, rank, ws)
+    B = hi - lo
+    prompt = prompt_job[lo:hi].to(dev)
+    gather = nccl_id_gather() if ws > 1 else None
+    dec = GreedyDecoder(model, B, graphs=True)
+    for _ in range(args.warmup):  # the first pass runs every position eagerly and captures its graph
+        dec(prompt, STACK_DECODE, gather)
+    torch.cuda.synchronize(dev)
+    barrier(ws)
+    stream = torch.cuda.current_stream(dev)
+    e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    pre_ms = dec_ms = 0.0
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()  # outside the timed region
+            e[0].record(stream)
+            first = dec.prefill(prompt)
+            if gather:
+                gather(first)
+            e[1].record(stream)
+            dec.decode(STACK_PREFILL, STACK_DECODE, gather)
+            e[2].record(stream)
+            torch.cuda.synchronize(dev)
+            pre_ms += e[0].elapsed_time(e[1])
+            dec_ms += e[1].elapsed_time(e[2])
+    barrier(ws)
+    if gdn.chunked_device_error(reset=True):
+        raise RuntimeError("chunked prefill reported a device-side wait timeout")
+    tot_ms = max_over_ranks(pre_ms + dec_ms, ws, dev)
+    pre_max = max_over_ranks(pre_ms, ws, dev)
+    dec_max = max_over_ranks(dec_ms, ws, dev)
+
+    # end to end through the decoder: the prompt shard copied in from pinned host memory, the job's
+    # generated ids copied back, inside the timed region
+    h_prompt = prompt_job[lo:hi].clone().pin_memory()
+    h_out = torch.empty(STACK_B if gather else B, STACK_DECODE + 1, dtype=torch.long).pin_memory()
+    d_prompt = torch.empty_like(prompt)
+    e2e_passes = min(args.steps, 2)
+    e2e_ms = 0.0
+    for _ in range(e2e_passes):
+        flush.zero_()
+        e[0].record(stream)
+        d_prompt.copy_(h_prompt, non_blocking=True)
+        ids = dec(d_prompt, STACK_DECODE, gather)
+        h_out.copy_(ids, non_blocking=True)
+        e[1].record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_ms += e[0].elapsed_time(e[1])
+    e2e_ms = max_over_ranks(e2e_ms, ws, dev)
+
+    n_tok = STACK_B * (STACK_PREFILL + STACK_DECODE)
+    pk, how = peaks()
+    flop = stack_prefill_flop(cfg, B, STACK_PREFILL)
+    tflops = flop / (pre_ms / args.steps / 1e3) / 1e12
+    dbytes = sum(stack_decode_bytes(cfg, B, STACK_PREFILL + s) for s in range(STACK_DECODE))
+    gbs = dbytes / (dec_ms / args.steps / 1e3) / 1e9
+    n_att = sum(cfg.is_attention(i) for i in range(cfg.n_layers))
+    return {
+        "metric": "stack_tokens_per_s",
+        "value": n_tok * args.steps / (tot_ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tot_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16 activations and weights, f32 GDN states",
+        "data": "synthetic (uniform random prompt ids, seed 4; weights ~N(0,0.02), conv ~N(0,0.1), "
+                "A_log ~U(0, log 16))",
+        "config": {"workload": "hybrid_stack", "sequences": STACK_B, "sequences_per_gpu": B,
+                   "prefill": STACK_PREFILL, "decode_steps": STACK_DECODE, "layers": cfg.n_layers,
+                   "attention_layers": n_att, "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab,
+                   "ctx": cfg.ctx, "gdn": f"H_qk {cfg.H_qk}, H_v {cfg.H_v}, d {cfg.d_k}",
+                   "attention": f"H_q {cfg.H_q}, H_kv {cfg.H_kv}, hd {cfg.head_dim}",
+                   "l2": "flushed (256 MB write) before every timed pass; weights and states exceed L2",
+                   "parallelism": f"sequences split over {ws} GPUs, NCCL all-gather of next-token ids"},
+        "prefill_tokens_per_s": STACK_B * STACK_PREFILL * args.steps / (pre_max / 1e3),
+        "decode_steps_per_s": STACK_DECODE * args.steps / (dec_max / 1e3),
+        "prefill_ms": pre_max / args.steps,
+        "decode_ms_per_step": dec_max / args.steps / STACK_DECODE,
+        "roofline": {"bound": "tensor", "phase": "prefill", "achieved": tflops, "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": tflops / pk["bf16_tflops"], "peak_source": how,
+                     "algorithmic_flop_per_prefill": flop, "traffic": None,
+                     "decode": {"bound": "hbm", "achieved_gbs": gbs, "frac": gbs / pk["hbm_gbs"],
+                                "algorithmic_bytes_per_pass": dbytes}},
+        "e2e": {"value": n_tok * e2e_passes / (e2e_ms / 1e3), "unit": "tokens/s", "passes": e2e_passes,
+                "h2d_bytes_per_step": h_prompt.numel() * h_prompt.element_size(),
+                "d2h_bytes_per_step": h_out.numel() * h_out.element_size()},
+        "gpu_launches": args.steps * (dec.launches["prefill"] +
+                                      sum(dec.launches[STACK_PREFILL + s] for s in range(STACK_DECODE))),
+        "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------------------ CPU samples ---
 def cpu_prefill_sample(threads, T=2048):
     """Oracle chunked prefill of one sequence x T tokens x 32 heads on the host; returns tokens/s."""
@@ -838,6 +990,45 @@ def cpu_layer_sample(threads, n_dec=8):
                                           "projections with the CPU oracle core")
 
 
+def cpu_stack_sample(threads, T=64, n_dec=2):
+    """The stack's layers restated by the CPU oracle (fp32 GEMMs, the oracle's GDN core and attention over
+    the 4096-row cache) for one sequence: a T-token prefill and n_dec greedy steps through all 24
+    layers, the final norm and the LM head; returns tokens/s.  The weights are fp32 copies of a
+    random block tiled over each parameter (the values do not change the timing)."""
+    from anemll_b200.stack import HybridStack, StackConfig, rope_tables
+    from oracle import stack as ost
+    torch.set_num_threads(threads)
+    cfg = StackConfig()
+    model = HybridStack(cfg, device="meta", dtype=torch.float32).to_empty(device="cpu")
+    model.cos, model.sin = rope_tables(cfg.head_dim, cfg.ctx, cfg.rope_theta, "cpu")
+    base = torch.randn(1 << 20, generator=torch.Generator().manual_seed(STACK_SEED)) * 0.02
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            flat = p.view(-1)
+            if "norm" in name and p.dim() == 1:
+                p.fill_(1.0)
+            elif name.endswith("A_log") or name.endswith("dt_bias"):
+                p.fill_(0.5)
+            else:
+                for i in range(0, flat.numel(), base.numel()):
+                    n = min(base.numel(), flat.numel() - i)
+                    flat[i:i + n].copy_(base[:n] * (5.0 if name.endswith("conv_weight") else 1.0))
+    state = ost.new_state(model, 1)
+    ids = torch.randint(0, cfg.vocab, (1, T), generator=torch.Generator().manual_seed(STACK_SEED))
+    t0 = time.perf_counter()
+    pos, x_ids = 0, ids
+    for _ in range(1 + n_dec):
+        x = ost.bf(model.embed.weight[x_ids])
+        for i in range(cfg.n_layers):
+            x = ost.layer(model, i, x, state[i], pos)
+        logits = torch.nn.functional.linear(ost.rms_norm(x[:, -1], model.norm, cfg.eps), model.lm_head.weight)
+        pos += x_ids.shape[1]
+        x_ids = logits.argmax(-1, keepdim=True)
+    dt = time.perf_counter() - t0
+    return (T + n_dec) / dt, (f"1 sequence: a {T}-token prefill and {n_dec} greedy steps through the 24 layers, "
+                              "fp32 torch GEMMs with the CPU oracle's GDN core and attention")
+
+
 def traffic_from_profiles(name):
     """Per-launch DRAM bytes recorded from an ncu capture, if a summary is committed."""
     path = os.path.join(ROOT, "profiles", "traffic.txt")  # "<workload> <bytes per launch>" lines
@@ -886,6 +1077,8 @@ def reference_arm(args, ws, rank):
                 v1, sample = cpu_kv_sample(threads, args.window)
             elif args.config == "cache_ops":
                 v1, sample = cpu_cache_ops_sample(threads)
+            elif args.config == "stack":
+                v1, sample = cpu_stack_sample(threads)
             else:
                 v1, sample = cpu_layer_sample(threads)
             vals.append(v1)
@@ -893,14 +1086,17 @@ def reference_arm(args, ws, rank):
             v, unit = max(vals), "GB/s"
             ms = None
         else:
-            sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8}[args.config]
+            sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8,
+                             "stack": 66}[args.config]
             v, unit = max(vals), "tokens/s"
             ms = sample_tokens / v * 1e3  # one step = one bounded sample
         metric = {"gdn_prefill": "gdn_prefill_tokens_per_s", "kv_attention": "kv_attention_tokens_per_s",
-                  "gdn_layer": "gdn_layer_tokens_per_s", "cache_ops": "kv_cache_ops_bytes_per_s"}[args.config]
+                  "gdn_layer": "gdn_layer_tokens_per_s", "cache_ops": "kv_cache_ops_bytes_per_s",
+                  "stack": "stack_tokens_per_s"}[args.config]
         config = {"workload": {"gdn_prefill": "gdn_chunked_prefill", "kv_attention": "kv_cache_attention",
-                               "gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops"}[args.config], "sample": sample}
-        scaling = "strong" if args.config in ("gdn_prefill", "kv_attention") else "weak"
+                               "gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops",
+                               "stack": "hybrid_stack"}[args.config], "sample": sample}
+        scaling = "strong" if args.config in ("gdn_prefill", "kv_attention", "stack") else "weak"
         sample = sample + f", best of {len(vals)}"
     return {
         "impl": "reference",
@@ -925,16 +1121,20 @@ def reference_arm(args, ws, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2560)
-    ap.add_argument("--warmup", type=int, default=32)
+    ap.add_argument("--steps", type=int, default=None, help="default 2560 (stack: 3)")
+    ap.add_argument("--warmup", type=int, default=None, help="default 32 (stack: 3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="gdn_decode",
-                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer", "cache_ops"])
+                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer", "cache_ops", "stack"])
     ap.add_argument("--window", type=int, default=0, help="kv_attention: sliding window (0 = causal)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
     ap.add_argument("--prefill-len", type=int, default=PREFILL_T, help="gdn_prefill: tokens per sequence")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 3 if args.config == "stack" else 2560
+    if args.warmup is None:
+        args.warmup = 3 if args.config == "stack" else 32
     args.warmup = max(args.warmup, 3)
     ws, rank, local = init_dist(args)
     try:
@@ -949,6 +1149,8 @@ def main():
                 res = bench_gdn_layer(args, ws, rank, local)
             elif args.config == "cache_ops":
                 res = bench_cache_ops(args, ws, rank, local)
+            elif args.config == "stack":
+                res = bench_stack(args, ws, rank, local)
             else:
                 res = bench_gdn_decode(args, ws, rank, local)
                 res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
@@ -968,7 +1170,8 @@ def main():
                     else:
                         v, sample = {"gdn_prefill": lambda: cpu_prefill_sample(threads),
                                      "kv_attention": lambda: cpu_kv_sample(threads, args.window),
-                                     "gdn_layer": lambda: cpu_layer_sample(threads)}[args.config]()
+                                     "gdn_layer": lambda: cpu_layer_sample(threads),
+                                     "stack": lambda: cpu_stack_sample(threads)}[args.config]()
                         res["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                                                "sample": sample}
         if rank == 0 and res is not None:

@@ -51,6 +51,9 @@ extern "C" {
 
 const char* anemll_last_error(void);
 int anemll_version(void);
+/* Kernel launches this process has issued through the library (successful launches; a launch
+ * recorded into a CUDA graph counts once, when captured, not per replay). */
+long long anemll_launch_count(void);
 
 /*
  * Gated delta rule, token-by-token form: decode (T == 1) and recurrent prefill.
