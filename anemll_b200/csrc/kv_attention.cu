@@ -560,8 +560,14 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   const int G = p.Hq / p.Hkv;  // == 8
   const int bh = blockIdx.z, b = bh / p.Hkv, kvh = bh % p.Hkv;
   const int tile = blockIdx.x, split = blockIdx.y;
-  const int k_begin = p.key_lo + split * p.ks;
-  const int k_end = min(p.key_hi, k_begin + p.ks);
+  int k_begin = p.key_lo + split * p.ks;
+  int k_end = min(p.key_hi, k_begin + p.ks);
+  if (!p.mask) {
+    // positional visibility: no key past the tile's last query is visible, nor (per-query window)
+    // a key before its first query's window; a long chunk's early tiles scan only their own prefix
+    k_end = min(k_end, p.pos + min(p.S, tile * 16 + 16));
+    if (p.window > 0 && !p.aligned) k_begin = max(k_begin, p.pos + tile * 16 - p.window + 1);
+  }
   const int nblk = k_end > k_begin ? (k_end - k_begin + TC_KB - 1) / TC_KB : 0;
   const uint32_t sbase = tc::smem_u32(sm);
   const uint32_t bar = tc::smem_u32(&mbar), qb = tc::smem_u32(&qbar), kvb0 = tc::smem_u32(&kvbar[0]);
@@ -629,9 +635,10 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     pending = j + 1 < nblk ? j + 1 : -1;
     const int key0 = k_begin + j * TC_KB;
     if (p.has_new && key0 < p.pos + p.S && key0 + TC_KB > p.pos) {  // block-uniform
-      // the new rows of this block: from k_new / v_new into the landed tiles, and by row tile 0
-      // into the cache (other tiles of the split may have read those cache rows before or while
-      // they are written; their tiles are overwritten here as well)
+      // the new rows of this block: from k_new / v_new into the landed tiles, and into the cache by
+      // the row tile whose queries they are (every tile's scan covers its own rows; other tiles may
+      // have read those cache rows before or while they are written, and their tiles are overwritten
+      // here as well)
       const int j0 = max(key0, p.pos), j1 = min(min(key0 + TC_KB, k_end), p.pos + p.S);
       const T* kn = reinterpret_cast<const T*>(p.k_new) + (long long)bh * p.S * HD;
       const T* vn = reinterpret_cast<const T*>(p.v_new) + (long long)bh * p.S * HD;
@@ -643,7 +650,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         const uint4 vv = *reinterpret_cast<const uint4*>(vn + (long long)(jj - p.pos) * HD + ch * 8);
         *reinterpret_cast<uint4*>(sm + OFF_K + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = kv;
         *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = vv;
-        if (tile == 0) {
+        if (tile == (jj - p.pos) >> 4) {
           *reinterpret_cast<uint4*>(Kc + (long long)jj * HD + ch * 8) = kv;
           *reinterpret_cast<uint4*>(Vc + (long long)jj * HD + ch * 8) = vv;
         }

@@ -181,3 +181,56 @@ def test_unwritten_cache_rows_are_never_read():
         vc[:, pos + S:] = float("nan")
         out = attention.kv_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos, gate=gate.to(DEV))
         assert_close(out.float().cpu(), ref, f"hd {hd} S {S} pos {pos}")
+
+
+def test_tcgen05_prefill_with_batched_caches():
+    """Prefill chunks on the tcgen05 path (8 query heads per kv head, hd 256) over per-sequence caches
+    [B, H_kv, ctx, hd] (4-D tensor maps), new rows written in the same call; bit-exact cache, output
+    within tolerance, with and without a sliding window."""
+    torch.manual_seed(13)
+    B, Hq, Hkv, hd, ctx, S = 3, 16, 2, 256, 1024, 64
+    for pos, window in ((0, 0), (320, 0), (700, 128)):
+        kc = torch.randn(B, Hkv, ctx, hd).half()
+        vc = torch.randn(B, Hkv, ctx, hd).half()
+        q = torch.randn(B, Hq, S, hd).half()
+        kn = torch.randn(B, Hkv, S, hd).half()
+        vn = torch.randn(B, Hkv, S, hd).half()
+        gate = torch.randn(B, S, Hq * hd).half()
+        kd, vd = kc.to(DEV), vc.to(DEV)
+        out = attention.kv_attention(q.to(DEV), kd, vd, pos, k_new=kn.to(DEV), v_new=vn.to(DEV), gate=gate.to(DEV),
+                                     window=window)
+        kr, vr = kc.float().clone(), vc.float().clone()
+        kr[:, :, pos:pos + S] = kn.float()
+        vr[:, :, pos:pos + S] = vn.float()
+        ref = ok.attend(q, kr, vr, ok.additive_mask(S, ctx, pos, window), gate)
+        assert_close(out.float().cpu(), ref, f"pos {pos} window {window}")
+        assert torch.equal(kd.cpu().float(), kr) and torch.equal(vd.cpu().float(), vr)
+    assert attention.kv_device_error() == 0
+
+
+@pytest.mark.gpu
+def test_tcgen05_long_chunk_clips_keys_per_tile():
+    """A 512-token chunk on the tcgen05 path: each 16-query tile scans only the keys its queries can
+    see (causal prefix, per-query window start) and writes its own new rows into the cache; output
+    within tolerance and the cache bit-exact, for the causal, per-query window and chunk-aligned
+    window rules, from position 0 and from a later position."""
+    torch.manual_seed(17)
+    B, Hq, Hkv, hd, ctx, S = 2, 16, 2, 256, 1024, 512
+    for pos, window, aligned in ((0, 0, False), (256, 0, False), (0, 200, False), (300, 96, False),
+                                 (256, 600, True)):
+        kc = torch.randn(B, Hkv, ctx, hd).half()
+        vc = torch.randn(B, Hkv, ctx, hd).half()
+        q = torch.randn(B, Hq, S, hd).half()
+        kn = torch.randn(B, Hkv, S, hd).half()
+        vn = torch.randn(B, Hkv, S, hd).half()
+        gate = torch.randn(B, S, Hq * hd).half()
+        kd, vd = kc.to(DEV), vc.to(DEV)
+        out = attention.kv_attention(q.to(DEV), kd, vd, pos, k_new=kn.to(DEV), v_new=vn.to(DEV), gate=gate.to(DEV),
+                                     window=window, window_chunk_aligned=aligned)
+        kr, vr = kc.float().clone(), vc.float().clone()
+        kr[:, :, pos:pos + S] = kn.float()
+        vr[:, :, pos:pos + S] = vn.float()
+        ref = ok.attend(q, kr, vr, ok.additive_mask(S, ctx, pos, window, chunk_aligned=aligned), gate)
+        assert_close(out.float().cpu(), ref, f"pos {pos} window {window} aligned {aligned}")
+        assert torch.equal(kd.cpu().float(), kr) and torch.equal(vd.cpu().float(), vr)
+    assert attention.kv_device_error() == 0
