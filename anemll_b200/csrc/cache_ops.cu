@@ -16,33 +16,6 @@ __device__ __forceinline__ float mask_at(const void* m, int mdt, long long i) {
                            : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(m)[i]);
 }
 
-// 8 consecutive elements <-> fp32, as one 16-byte (2-byte types) or two 16-byte (fp32) accesses
-template <typename T>
-__device__ __forceinline__ void load8(const T* p, float* f) {
-  if constexpr (sizeof(T) == 4) {
-    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  } else {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
-    const T* h = reinterpret_cast<const T*>(&u);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = to_f32(h[e]);
-  }
-}
-template <typename T>
-__device__ __forceinline__ void store8(T* p, const float* f) {
-  if constexpr (sizeof(T) == 4) {
-    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
-    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
-  } else {
-    uint4 u;
-    T* h = reinterpret_cast<T*>(&u);
-#pragma unroll
-    for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(f[e]);
-    *reinterpret_cast<uint4*>(p) = u;
-  }
-}
-
 // One warp per (row l, slab).  The lanes read the mask row together; a row the mask leaves untouched
 // (all weights zero) is left alone, with no cache traffic.  For a touched row the lanes rewrite the
 // slab's d elements in 8-element groups: cache = cache (1 - min(sum_s m, 1)) + sum_s new_s m_s (fp32);

@@ -1,6 +1,8 @@
 // Gated RMSNorm over rows: out = weight * x * rsqrt(mean(x^2) + eps) * silu(z).
-// One warp per row; semantics of Qwen3_5RMSNormGated (transformers 5.5.0,
-// modeling_qwen3_5.py:175-190), evaluated in fp32.
+// Semantics of Qwen3_5RMSNormGated (transformers 5.5.0, modeling_qwen3_5.py:175-190), evaluated in
+// fp32.  Rows of up to 512 elements (d_v = 128 in every Qwen3.5 size): a half-warp per row, 8
+// elements per lane as 16-byte vectors, every load issued before the first use.  Longer rows: a
+// warp per row, element by element.
 #include "common.cuh"
 
 namespace anemll {
@@ -28,6 +30,48 @@ gated_rmsnorm_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const f
   }
 }
 
+// rows of d <= 16 * 8 * NC elements, d % 8 == 0; 16 rows per 256-thread CTA
+template <typename TX, typename TZ, typename TO, int NC>
+__global__ void __launch_bounds__(256)
+gated_rmsnorm_vec_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const float* __restrict__ w,
+                         TO* __restrict__ out, int64_t rows, int d, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
+  const int l = threadIdx.x & 15;
+  const unsigned hmask = 0xffffu << (threadIdx.x & 16);
+  if (row >= rows) return;  // whole half-warps leave together
+  float xv[NC][8], zv[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 16 + l) * 8;
+    if (col < d) {
+      load8(x + row * d + col, xv[c]);
+      load8(z + row * d + col, zv[c]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 16 + l) * 8;
+    if (col < d) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += xv[c][e] * xv[c][e];
+    }
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(hmask, ss, off);
+  const float r = rsqrtf(ss / (float)d + eps);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int col = (c * 16 + l) * 8;
+    if (col < d) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = w[col + e] * xv[c][e] * r * silu(zv[c][e]);
+      store8(out + row * d + col, o);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace anemll
 
@@ -44,8 +88,17 @@ extern "C" int anemll_gated_rmsnorm(const void* x, int x_dtype, const void* z, i
   return ANEMLL_DISPATCH_DTYPE(x_dtype, TX, [&] {
     return ANEMLL_DISPATCH_DTYPE(z_dtype, TZ, [&] {
       return ANEMLL_DISPATCH_DTYPE(out_dtype, TO, [&] {
-        gated_rmsnorm_kernel<TX, TZ, TO><<<blocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight, (TO*)out,
-                                                                 rows, d, eps);
+        const bool vec = d % 8 == 0 && d <= 512 && aligned(x, 16) && aligned(z, 16) && aligned(out, 16);
+        const unsigned vblocks = (unsigned)((rows + 15) / 16);
+        if (vec && d <= 128)
+          gated_rmsnorm_vec_kernel<TX, TZ, TO, 1><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
+                                                                          (TO*)out, rows, d, eps);
+        else if (vec)
+          gated_rmsnorm_vec_kernel<TX, TZ, TO, 4><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
+                                                                          (TO*)out, rows, d, eps);
+        else
+          gated_rmsnorm_kernel<TX, TZ, TO><<<blocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight, (TO*)out,
+                                                                   rows, d, eps);
         return launch_status("gated_rmsnorm");
       });
     });

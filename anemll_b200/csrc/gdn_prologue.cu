@@ -1,156 +1,309 @@
 // Fused GDN prologue: causal depthwise conv1d + SiLU, q/k l2-norm, gates.
 //
-// Grid: x = token tiles of TT tokens, y = 128-channel head groups
-// (H_qk q-heads, H_qk k-heads, H_v v-heads) plus one gate group, z = batch.
-// One thread per channel walks the tile's TT tokens with a conv_k-deep sliding
-// window in registers; the per-token l2 norm of a q/k head is a 128-channel
-// block reduction.  Reads and writes are coalesced along channels.
+// Channels come in 128-channel head groups (H_qk q-heads, H_qk k-heads, H_v v-heads).  Two kernels:
 //
-// The conv state (last conv_k raw inputs, newest last) is read only by the
-// tile-0 CTA of each channel group, which is also the only writer, so the
-// in-place update has no cross-CTA hazard; the copy is of raw input values and
-// therefore bit-exact.  Semantics: modeling_qwen3_5.py:210-226 (update),
-// 453-496 (prefill conv, split, gates) of transformers 5.5.0.
+// * Tile kernel (T > DEC_T): a CTA of 128 threads owns one sequence, one head group and TT = 64
+//   tokens.  Its input rows (the tile plus the conv_k - 1 rows before it) are copied into shared
+//   memory with 16-byte cp.async; each thread then runs the conv + SiLU of a channel pair over half
+//   the tile from shared memory into an fp32 tile, and the four warps finish row by row (a warp per
+//   token: the q/k l2 norm is a warp reduction, stores are whole 256-byte row segments).
+// * Short kernel (T <= DEC_T and conv_k == 4, the decode steps): a thread per channel, the conv
+//   window, weights and state in registers (one vector access each), the head's l2 norm a block
+//   reduction; one instantiation per T.
+//
+// The gates (g, beta) are computed by extra CTAs at the end of either grid.  The conv state (last
+// conv_k raw inputs per channel, newest last) is read only by the CTA that holds token 0, which is
+// also its only writer, so the in-place update has no cross-CTA hazard; the copy is of raw input
+// values and therefore bit-exact.  Semantics: modeling_qwen3_5.py:210-226 (update), 453-496
+// (prefill conv, split, gates) of transformers 5.5.0.
 #include "common.cuh"
+#include "mma_sync.cuh"
 
 namespace anemll {
 namespace {
 
-constexpr int CH = 128;     // channels per head group == threads per CTA
-constexpr int TT = 16;      // tokens per CTA
-constexpr int MAXK = 8;     // largest supported conv kernel
+constexpr int HDIM = 128;  // channels per head group (d_k == d_v); threads per CTA
+constexpr int TT = 64;     // tokens per tile
+constexpr int MAXK = 8;    // largest supported conv kernel
+constexpr int DEC_T = 4;   // longest call served by the short kernel
 
-template <typename TIn, typename TAB, typename TOut>
-__global__ void __launch_bounds__(CH)
-gdn_prologue_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn* __restrict__ conv_state,
-                    const TAB* __restrict__ a, const TAB* __restrict__ bgate,
-                    const float* __restrict__ A_log, const float* __restrict__ dt_bias,
-                    TOut* __restrict__ qo, TOut* __restrict__ ko, TOut* __restrict__ vo,
-                    float* __restrict__ go, float* __restrict__ betao,
-                    int T, int Hqk, int Hv, int K, int use_state) {
-  const int tile = blockIdx.x;
-  const int grp = blockIdx.y;
-  const int b = blockIdx.z;
-  const int c = threadIdx.x;
-  const int t0 = tile * TT;
-  const int ngroups = 2 * Hqk + Hv;
+__device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
+  return dt == ANEMLL_F32 ? reinterpret_cast<const float*>(p)[i]
+       : dt == ANEMLL_F16 ? __half2float(reinterpret_cast<const __half*>(p)[i])
+                          : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
 
-  if (grp == ngroups) {  // gates
-    for (int i = c; i < TT * Hv; i += CH) {
-      const int t = t0 + i / Hv;
-      const int h = i % Hv;
-      if (t >= T) continue;
-      const size_t idx = ((size_t)b * T + t) * Hv + h;
-      float av = to_f32(a[idx]);
-      if (dt_bias) av += dt_bias[h];
-      const float bv = to_f32(bgate[idx]);
-      go[idx] = -expf(A_log[h]) * softplus(av);
-      betao[idx] = 1.0f / (1.0f + expf(-bv));
-    }
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) for one (token, v-head)
+__device__ __forceinline__ void gate_elem(long long idx, int Hv, const void* a, const void* bgate, int ab_dt,
+                                          const float* A_log, const float* dt_bias, float* go, float* betao) {
+  const int h = (int)(idx % Hv);
+  float av = load_any(a, ab_dt, idx);
+  if (dt_bias) av += dt_bias[h];
+  const float bv = load_any(bgate, ab_dt, idx);
+  go[idx] = -expf(A_log[h]) * softplus(av);
+  betao[idx] = 1.0f / (1.0f + expf(-bv));
+}
+
+// x / (1 + e^-x) with the fast division (relative error a few ulp; the conv output is not rounded
+// to a storage type before the l2 norm, so this stays far inside fp32 tolerances)
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// two consecutive elements (4-byte aligned for 2-byte types, 8-byte for fp32) as fp32
+template <typename T>
+__device__ __forceinline__ float2 ld2f(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    return *reinterpret_cast<const float2*>(p);
+  } else {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    const T* h = reinterpret_cast<const T*>(&u);
+    return make_float2(to_f32(h[0]), to_f32(h[1]));
+  }
+}
+
+struct Dst {
+  void* p;
+  int H, h;
+};
+
+__device__ __forceinline__ Dst group_dst(int grp, int Hqk, int Hv, void* qo, void* ko, void* vo) {
+  if (grp < Hqk) return {qo, Hqk, grp};
+  if (grp < 2 * Hqk) return {ko, Hqk, grp - Hqk};
+  return {vo, Hv, grp - 2 * Hqk};
+}
+
+// ------------------------------------------------------------------ tile --
+// KT: conv_k as a compile-time constant (4, the conv of every Qwen3.5 size), or 0 for a runtime K.
+template <typename TIn, typename TOut, int KT>
+__global__ void __launch_bounds__(HDIM)
+prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn* __restrict__ conv_state,
+                     const void* __restrict__ a, const void* __restrict__ bgate, int ab_dt, const float* __restrict__ A_log,
+                     const float* __restrict__ dt_bias, TOut* __restrict__ qo, TOut* __restrict__ ko,
+                     TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao, int B, int T, int Hqk,
+                     int Hv, int K, int use_state, int n_tiles, int conv_ctas) {
+  if ((int)blockIdx.x >= conv_ctas) {
+    const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
+    if (idx < (long long)B * T * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, A_log, dt_bias, go, betao);
     return;
   }
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int ROWB = HDIM * sizeof(TIn);  // bytes of one input row segment
+  TIn* X = reinterpret_cast<TIn*>(smem);    // [TT + MAXK - 1][HDIM]: row r = position t0 - (K-1) + r
+  float* Y = reinterpret_cast<float*>(smem + (TT + MAXK - 1) * ROWB);  // [TT][HDIM]
 
-  const int C = ngroups * CH;
-  const int ch = grp * CH + c;
-  const float* wc = w + (size_t)ch * K;
-  float wr[MAXK];
-#pragma unroll
-  for (int j = 0; j < MAXK; ++j) wr[j] = j < K ? wc[j] : 0.f;
+  const int ngroups = 2 * Hqk + Hv;
+  const int C = ngroups * HDIM;
+  const int tile = blockIdx.x % n_tiles;
+  const int grp = (blockIdx.x / n_tiles) % ngroups;
+  const int b = blockIdx.x / (n_tiles * ngroups);
+  const int c = threadIdx.x;
+  const int t0 = tile * TT, nt = min(TT, T - t0);
+  const int nrows = nt + K - 1;
+  const TIn* xg = x + (long long)b * T * C + grp * HDIM;
+  TIn* cs = conv_state + ((long long)b * C + grp * HDIM) * K;
 
-  // history: raw inputs at relative positions t0-K+1 .. t0-1 (window slots 1..K-1)
-  float win[MAXK];
-  TIn* cs = conv_state + ((size_t)b * C + ch) * K;
-  TIn old_state[MAXK];
-  if (tile == 0) {
-#pragma unroll
-    for (int j = 0; j < MAXK; ++j) old_state[j] = j < K && use_state ? cs[j] : from_f32<TIn>(0.f);
+  // rows from x: 16-byte asynchronous copies; rows before token 0: the old state (or zeros)
+  constexpr int CPR = ROWB / 16;  // 16-byte chunks per row
+  for (int i = c; i < nrows * CPR; i += HDIM) {
+    const int r = i / CPR, ch = i % CPR;
+    const int pos = t0 - (K - 1) + r;
+    if (pos >= 0) cp_async16(reinterpret_cast<uint8_t*>(X) + r * ROWB + ch * 16,
+                             reinterpret_cast<const uint8_t*>(xg + (long long)pos * C) + ch * 16);
   }
-#pragma unroll
-  for (int j = 0; j < MAXK; ++j) {
-    // slot j holds position t0 - K + j  (slot K-1 is the newest before t0)
-    const int pos = t0 - K + j;
-    float val = 0.f;
-    if (j < K) {
-      if (pos >= 0) val = to_f32(x[((size_t)b * T + pos) * C + ch]);
-      else if (use_state) val = to_f32(old_state[K + pos]);  // pos in [-K, -1]; only tile 0 reaches here
-    }
-    win[j] = val;
+  cp_async_commit();
+  if (t0 == 0) {
+    for (int r = 0; r < K - 1; ++r)  // position r - (K-1) = state slot r + 1
+      X[r * HDIM + c] = use_state ? cs[(long long)c * K + r + 1] : from_f32<TIn>(0.f);
   }
+  // phase 1: thread = (channel pair cc, cc+1; half of the tile's tokens)
+  const int cc = 2 * (c & (HDIM / 2 - 1)), half = c / (HDIM / 2);
+  float2 wr[MAXK];
+#pragma unroll
+  for (int j = 0; j < MAXK; ++j)
+    wr[j] = j < K ? make_float2(w[(long long)(grp * HDIM + cc) * K + j], w[(long long)(grp * HDIM + cc + 1) * K + j])
+                  : make_float2(0.f, 0.f);
+  cp_async_wait<0>();
+  __syncthreads();
 
-  float y[TT];
+  // conv + SiLU over the tile from shared memory (taps j read rows t + j)
+  const int tb = half * (TT / 2), te = min(nt, tb + TT / 2);  // uniform per warp
+  if constexpr (KT == 4) {
+    // a register window over the rows: one shared-memory load per token
+    float2 x0 = ld2f(X + (tb + 0) * HDIM + cc), x1 = ld2f(X + (tb + 1) * HDIM + cc);
+    float2 x2 = ld2f(X + (tb + 2) * HDIM + cc);
 #pragma unroll
-  for (int i = 0; i < TT; ++i) {
-    const int t = t0 + i;
-    const float xn = t < T ? to_f32(x[((size_t)b * T + t) * C + ch]) : 0.f;
-    // shift the window left by one and append x[t]
-#pragma unroll
-    for (int j = 0; j < MAXK - 1; ++j) win[j] = (j + 1 < K) ? win[j + 1] : win[j];
-    if (K - 1 < MAXK) {
-#pragma unroll
-      for (int j = 0; j < MAXK; ++j) if (j == K - 1) win[j] = xn;
-    }
-    float acc = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAXK; ++j) if (j < K) acc += wr[j] * win[j];
-    y[i] = silu(acc);
-  }
-
-  const bool is_q = grp < Hqk;
-  const bool is_k = !is_q && grp < 2 * Hqk;
-  if (is_q || is_k) {
-    __shared__ float part[CH / 32][TT];
-    const int lane = c & 31, warp = c >> 5;
-#pragma unroll
-    for (int i = 0; i < TT; ++i) {
-      const float ss = warp_sum(y[i] * y[i]);
-      if (lane == 0) part[warp][i] = ss;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < TT; ++i) {
-      float ss = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < CH / 32; ++ww) ss += part[ww][i];
-      y[i] *= rsqrtf(ss + 1e-6f);
-    }
-    const int h = is_q ? grp : grp - Hqk;
-    TOut* dst = is_q ? qo : ko;
-#pragma unroll
-    for (int i = 0; i < TT; ++i) {
-      const int t = t0 + i;
-      if (t < T) dst[(((size_t)b * T + t) * Hqk + h) * CH + c] = from_f32<TOut>(y[i]);
+    for (int i = 0; i < TT / 2; ++i) {
+      const int t = tb + i;
+      if (t < te) {
+        const float2 x3 = ld2f(X + (t + 3) * HDIM + cc);
+        float a0 = wr[0].x * x0.x, a1 = wr[0].y * x0.y;
+        a0 += wr[1].x * x1.x; a1 += wr[1].y * x1.y;
+        a0 += wr[2].x * x2.x; a1 += wr[2].y * x2.y;
+        a0 += wr[3].x * x3.x; a1 += wr[3].y * x3.y;
+        *reinterpret_cast<float2*>(Y + t * HDIM + cc) = make_float2(silu_fast(a0), silu_fast(a1));
+        x0 = x1; x1 = x2; x2 = x3;
+      }
     }
   } else {
-    const int h = grp - 2 * Hqk;
+    for (int t = tb; t < te; ++t) {
+      float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < TT; ++i) {
-      const int t = t0 + i;
-      if (t < T) vo[(((size_t)b * T + t) * Hv + h) * CH + c] = from_f32<TOut>(y[i]);
+      for (int j = 0; j < MAXK; ++j) {
+        if (j < K) {
+          const float2 xv = ld2f(X + (t + j) * HDIM + cc);
+          a0 += wr[j].x * xv.x;
+          a1 += wr[j].y * xv.y;
+        }
+      }
+      *reinterpret_cast<float2*>(Y + t * HDIM + cc) = make_float2(silu_fast(a0), silu_fast(a1));
     }
   }
-
-  if (tile == 0) {
-    // new state = last K entries of cat(history, x): relative positions T-K .. T-1
+  if (t0 == 0) {
+    // new state = last K entries of cat(old state, x): positions T-K .. T-1; the old state's are in
+    // X rows 0 .. K-2 (only reached when T < K, and then the whole sequence is this tile)
+    TIn nv[MAXK];
 #pragma unroll
     for (int j = 0; j < MAXK; ++j) {
-      if (j >= K) break;
-      const int pos = T - K + j;
-      TIn val;
-      if (pos >= 0) val = x[((size_t)b * T + pos) * C + ch];
-      else val = old_state[K + pos];
-      cs[j] = val;
+      if (j < K) {
+        const int pos = T - K + j;
+        nv[j] = pos >= 0 ? xg[(long long)pos * C + c] : X[(pos + K - 1) * HDIM + c];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < MAXK; ++j)
+      if (j < K) cs[(long long)c * K + j] = nv[j];
+  }
+  __syncthreads();
+
+  // rows: warp per token, 4 channels per lane
+  const int lane = c & 31, warp = c >> 5;
+  const bool norm = grp < 2 * Hqk;
+  const Dst d = group_dst(grp, Hqk, Hv, qo, ko, vo);
+  TOut* dst = reinterpret_cast<TOut*>(d.p);
+  for (int t = warp; t < nt; t += HDIM / 32) {
+    float4 v = *reinterpret_cast<const float4*>(Y + t * HDIM + lane * 4);
+    if (norm) {
+      const float r = rsqrtf(warp_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w) + 1e-6f);
+      v.x *= r; v.y *= r; v.z *= r; v.w *= r;
+    }
+    TOut* o = dst + (((long long)b * T + t0 + t) * d.H + d.h) * HDIM + lane * 4;
+    if constexpr (sizeof(TOut) == 4) {
+      *reinterpret_cast<float4*>(o) = v;
+    } else {
+      TOut h4[4] = {from_f32<TOut>(v.x), from_f32<TOut>(v.y), from_f32<TOut>(v.z), from_f32<TOut>(v.w)};
+      *reinterpret_cast<uint2*>(o) = *reinterpret_cast<const uint2*>(h4);
     }
   }
 }
 
-template <typename TIn, typename TAB, typename TOut>
-int launch_prologue(const void* x, const float* w, void* cs, const void* a, const void* bg, const float* A_log,
-                    const float* dt_bias, void* qo, void* ko, void* vo, float* go, float* bo, int B, int T,
-                    int Hqk, int Hv, int K, int use_state, cudaStream_t st) {
-  dim3 grid((T + TT - 1) / TT, 2 * Hqk + Hv + 1, B);
-  gdn_prologue_kernel<TIn, TAB, TOut><<<grid, CH, 0, st>>>(
-      (const TIn*)x, w, (TIn*)cs, (const TAB*)a, (const TAB*)bg, A_log, dt_bias, (TOut*)qo, (TOut*)ko,
-      (TOut*)vo, go, bo, T, Hqk, Hv, K, use_state);
+// ----------------------------------------------------------------- short --
+// conv_k == 4, TS = T tokens (1 .. DEC_T): raw slot s holds position s - 4 (the old state in slots
+// 0..3, x[t] in slot 4 + t), so token t's taps are slots t+1 .. t+4 and the new state is slots
+// TS .. TS+3, all static register indices.
+template <typename TIn, typename TOut, int TS>
+__global__ void __launch_bounds__(HDIM)
+prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn* __restrict__ conv_state,
+                      const void* __restrict__ a, const void* __restrict__ bgate, int ab_dt,
+                      const float* __restrict__ A_log, const float* __restrict__ dt_bias, TOut* __restrict__ qo,
+                      TOut* __restrict__ ko, TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao,
+                      int B, int Hqk, int Hv, int use_state, int conv_ctas) {
+  if ((int)blockIdx.x >= conv_ctas) {
+    const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
+    if (idx < (long long)B * TS * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, A_log, dt_bias, go, betao);
+    return;
+  }
+  constexpr int K = 4;
+  const int ngroups = 2 * Hqk + Hv;
+  const int C = ngroups * HDIM;
+  const int grp = blockIdx.x % ngroups, b = blockIdx.x / ngroups;
+  const int c = threadIdx.x, ch = grp * HDIM + c;
+  TIn* cs = conv_state + ((long long)b * C + ch) * K;
+  const TIn* xg = x + (long long)b * TS * C + ch;
+
+  TIn raw[K + TS];
+  if constexpr (sizeof(TIn) == 2) {
+    if (use_state) {
+      const uint2 u = *reinterpret_cast<const uint2*>(cs);  // 4 x 2 bytes, 8-byte aligned
+      const TIn* s4 = reinterpret_cast<const TIn*>(&u);
+#pragma unroll
+      for (int j = 0; j < K; ++j) raw[j] = s4[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < K; ++j) raw[j] = from_f32<TIn>(0.f);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < K; ++j) raw[j] = use_state ? cs[j] : from_f32<TIn>(0.f);
+  }
+#pragma unroll
+  for (int t = 0; t < TS; ++t) raw[K + t] = xg[(long long)t * C];
+  const float4 w4 = *reinterpret_cast<const float4*>(w + (long long)ch * K);
+
+  float y[TS];
+#pragma unroll
+  for (int t = 0; t < TS; ++t)
+    y[t] = silu_fast(w4.x * to_f32(raw[t + 1]) + w4.y * to_f32(raw[t + 2]) + w4.z * to_f32(raw[t + 3]) +
+                     w4.w * to_f32(raw[t + 4]));
+
+  if (grp < 2 * Hqk) {  // q/k head: l2 norm over the 128 channels (4 warps)
+    __shared__ float part[HDIM / 32][TS];
+    const int lane = c & 31, warp = c >> 5;
+#pragma unroll
+    for (int t = 0; t < TS; ++t) {
+      const float ss = warp_sum(y[t] * y[t]);
+      if (lane == 0) part[warp][t] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < TS; ++t) y[t] *= rsqrtf(part[0][t] + part[1][t] + part[2][t] + part[3][t] + 1e-6f);
+  }
+  const Dst d = group_dst(grp, Hqk, Hv, qo, ko, vo);
+  TOut* dst = reinterpret_cast<TOut*>(d.p);
+#pragma unroll
+  for (int t = 0; t < TS; ++t) dst[(((long long)b * TS + t) * d.H + d.h) * HDIM + c] = from_f32<TOut>(y[t]);
+
+  if constexpr (sizeof(TIn) == 2) {  // new state: slots TS .. TS + 3
+    const TIn s4[4] = {raw[TS], raw[TS + 1], raw[TS + 2], raw[TS + 3]};
+    *reinterpret_cast<uint2*>(cs) = *reinterpret_cast<const uint2*>(s4);
+  } else {
+#pragma unroll
+    for (int j = 0; j < K; ++j) cs[j] = raw[TS + j];
+  }
+}
+
+template <typename TIn, typename TOut>
+int launch_prologue(const void* x, const float* w, void* cs, const void* a, const void* bg, int ab_dt,
+                    const float* A_log, const float* dt_bias, void* qo, void* ko, void* vo, float* go, float* bo,
+                    int B, int T, int Hqk, int Hv, int K, int use_state, cudaStream_t st) {
+  const int ngroups = 2 * Hqk + Hv;
+  const long long gate_ctas = ((long long)B * T * Hv + HDIM - 1) / HDIM;
+  if (T <= DEC_T && K == 4) {
+    const long long conv_ctas = (long long)B * ngroups;
+    ANEMLL_REQUIRE(conv_ctas + gate_ctas < (1LL << 31), ANEMLL_EINVAL, "gdn_prologue: problem too large");
+    const unsigned grid = (unsigned)(conv_ctas + gate_ctas);
+    auto go_short = [&](auto kern) {
+      kern<<<grid, HDIM, 0, st>>>((const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko,
+                                  (TOut*)vo, go, bo, B, Hqk, Hv, use_state, (int)conv_ctas);
+    };
+    switch (T) {
+      case 1: go_short(prologue_short_kernel<TIn, TOut, 1>); break;
+      case 2: go_short(prologue_short_kernel<TIn, TOut, 2>); break;
+      case 3: go_short(prologue_short_kernel<TIn, TOut, 3>); break;
+      default: go_short(prologue_short_kernel<TIn, TOut, 4>); break;
+    }
+  } else {
+    const int n_tiles = (T + TT - 1) / TT;
+    const long long conv_ctas = (long long)B * ngroups * n_tiles;
+    ANEMLL_REQUIRE(conv_ctas + gate_ctas < (1LL << 31), ANEMLL_EINVAL, "gdn_prologue: problem too large");
+    const size_t smem = (size_t)(TT + MAXK - 1) * HDIM * sizeof(TIn) + (size_t)TT * HDIM * sizeof(float);
+    auto go_tile = [&](auto kern) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      kern<<<(unsigned)(conv_ctas + gate_ctas), HDIM, smem, st>>>(
+          (const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko, (TOut*)vo, go, bo, B, T,
+          Hqk, Hv, K, use_state, n_tiles, (int)conv_ctas);
+    };
+    if (K == 4) go_tile(prologue_tile_kernel<TIn, TOut, 4>);
+    else go_tile(prologue_tile_kernel<TIn, TOut, 0>);
+  }
   return launch_status("gdn_prologue");
 }
 
@@ -170,17 +323,19 @@ extern "C" int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const fl
                      beta_out,
                  ANEMLL_EINVAL, "gdn_prologue: null pointer");
   ANEMLL_REQUIRE(B > 0 && T > 0 && H_qk > 0 && H_v > 0, ANEMLL_EINVAL, "gdn_prologue: bad sizes");
-  ANEMLL_REQUIRE(d_k == CH && d_v == CH, ANEMLL_EUNSUPPORTED, "gdn_prologue: d_k and d_v must be 128");
+  ANEMLL_REQUIRE(d_k == HDIM && d_v == HDIM, ANEMLL_EUNSUPPORTED, "gdn_prologue: d_k and d_v must be 128");
   ANEMLL_REQUIRE(conv_k >= 1 && conv_k <= MAXK, ANEMLL_EUNSUPPORTED, "gdn_prologue: conv_k must be in [1, %d]", MAXK);
   ANEMLL_REQUIRE(dtype_ok(in_dtype) && dtype_ok(ab_dtype) && dtype_ok(out_dtype), ANEMLL_EUNSUPPORTED,
                  "gdn_prologue: bad dtype");
+  ANEMLL_REQUIRE(aligned(mixed_qkv, 16) && aligned(conv_w, 16) && aligned(conv_state, 8) && aligned(q_out, 16) &&
+                     aligned(k_out, 16) && aligned(v_out, 16),
+                 ANEMLL_EINVAL, "gdn_prologue: mixed_qkv, conv_w and the outputs must be 16-byte aligned, "
+                                "conv_state 8-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
   return ANEMLL_DISPATCH_DTYPE(in_dtype, TIn, [&] {
-    return ANEMLL_DISPATCH_DTYPE(ab_dtype, TAB, [&] {
-      return ANEMLL_DISPATCH_DTYPE(out_dtype, TOut, [&] {
-        return launch_prologue<TIn, TAB, TOut>(mixed_qkv, conv_w, conv_state, a, b, A_log, dt_bias, q_out, k_out,
-                                               v_out, g_out, beta_out, B, T, H_qk, H_v, conv_k, use_state, st);
-      });
+    return ANEMLL_DISPATCH_DTYPE(out_dtype, TOut, [&] {
+      return launch_prologue<TIn, TOut>(mixed_qkv, conv_w, conv_state, a, b, ab_dtype, A_log, dt_bias, q_out, k_out,
+                                        v_out, g_out, beta_out, B, T, H_qk, H_v, conv_k, use_state, st);
     });
   });
 }

@@ -26,8 +26,8 @@ import torch.nn.functional as F
 
 from . import _lib, attention, gdn
 
-__all__ = ["StackConfig", "HybridStack", "GreedyDecoder", "nccl_id_gather", "shard", "rms_norm", "rope_tables",
-           "apply_rope"]
+__all__ = ["StackConfig", "HybridStack", "GreedyDecoder", "nccl_id_gather", "shard", "rms_norm", "silu_mul",
+           "rope_tables"]
 
 
 class StackConfig:
@@ -42,13 +42,48 @@ class StackConfig:
         return (i + 1) % 4 == 0
 
 
-def rms_norm(x, w, eps):
-    """x * rsqrt(mean(x^2) + eps) * w, in fp32, returned in x's dtype."""
-    xf = x.float()
-    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(x.dtype)
+def rms_norm(x, w, eps, residual=None):
+    """RMSNorm over the last dim (fp32 arithmetic, one rounding): ``anemll_rmsnorm``.  With
+    ``residual``: ``s = x + residual`` (rounded) first; returns ``(s, norm(s))``."""
+    _need_cuda(x)
+    d = x.shape[-1]
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    rows = x.numel() // d
+    lib = _lib.load()
+    if residual is None:
+        rc = lib.anemll_rmsnorm(_lib.ptr(x), None, None, _lib.ptr(w), _lib.ptr(out), _lib.dtype_code(x.dtype), rows, d,
+                                float(eps), _lib.stream_ptr(x.device))
+        _lib.check(rc, "anemll_rmsnorm")
+        return out
+    residual = residual.contiguous()
+    s = torch.empty_like(x)
+    rc = lib.anemll_rmsnorm(_lib.ptr(x), _lib.ptr(residual), _lib.ptr(s), _lib.ptr(w), _lib.ptr(out),
+                            _lib.dtype_code(x.dtype), rows, d, float(eps), _lib.stream_ptr(x.device))
+    _lib.check(rc, "anemll_rmsnorm")
+    return s, out
+
+
+def silu_mul(gate_up):
+    """SwiGLU of a ``[..., 2 ffn]`` gate|up projection: ``silu(gate) * up`` (``anemll_silu_mul``)."""
+    _need_cuda(gate_up)
+    gate_up = gate_up.contiguous()
+    ffn = gate_up.shape[-1] // 2
+    out = torch.empty(*gate_up.shape[:-1], ffn, dtype=gate_up.dtype, device=gate_up.device)
+    rc = _lib.load().anemll_silu_mul(_lib.ptr(gate_up), _lib.ptr(out), _lib.dtype_code(gate_up.dtype),
+                                     gate_up.numel() // (2 * ffn), ffn, _lib.stream_ptr(gate_up.device))
+    _lib.check(rc, "anemll_silu_mul")
+    return out
+
+
+def _need_cuda(*ts):
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("anemll_b200 ops take CUDA tensors (no CPU path)")
 
 
 def rope_tables(dim, n_pos, theta, device):
+    """cos/sin [n_pos, dim] (fp32, computed in fp64) of the rotary embedding, both halves equal."""
     inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64, device=device) / dim))
     t = torch.arange(n_pos, dtype=torch.float64, device=device)
     f = torch.outer(t, inv)
@@ -56,44 +91,50 @@ def rope_tables(dim, n_pos, theta, device):
     return emb.cos().float(), emb.sin().float()
 
 
-def apply_rope(x, cos, sin):
-    """x [B, H, T, d] with cos/sin [T, d] (fp32): x cos + rotate_half(x) sin, in fp32."""
-    x = x.float()
-    h = x.shape[-1] // 2
-    rot = torch.cat([-x[..., h:], x[..., :h]], dim=-1)
-    return x * cos + rot * sin
-
-
 class GatedAttention(nn.Module):
+    """Gated full attention.  q_proj, k_proj and v_proj are views of one fused [q|k|v] weight, so the
+    projections are one GEMM whose output feeds ``anemll_qk_norm_rope`` through row strides."""
+
     def __init__(self, cfg: StackConfig, device, dtype):
         super().__init__()
         fk = dict(device=device, dtype=dtype)
         self.cfg = cfg
         Hq, Hkv, hd = cfg.H_q, cfg.H_kv, cfg.head_dim
-        self.q_proj = nn.Linear(cfg.hidden, Hq * hd * 2, bias=False, **fk)  # per head: [query | gate]
-        self.k_proj = nn.Linear(cfg.hidden, Hkv * hd, bias=False, **fk)
-        self.v_proj = nn.Linear(cfg.hidden, Hkv * hd, bias=False, **fk)
+        self.n_q, self.n_kv = Hq * hd * 2, Hkv * hd  # q_proj rows per head: [query | gate]
+        self.w_qkv = torch.empty(self.n_q + 2 * self.n_kv, cfg.hidden, **fk)
+        self.q_proj = nn.Linear(cfg.hidden, self.n_q, bias=False, device="meta")
+        self.k_proj = nn.Linear(cfg.hidden, self.n_kv, bias=False, device="meta")
+        self.v_proj = nn.Linear(cfg.hidden, self.n_kv, bias=False, device="meta")
+        self.q_proj.weight = nn.Parameter(self.w_qkv[:self.n_q])
+        self.k_proj.weight = nn.Parameter(self.w_qkv[self.n_q:self.n_q + self.n_kv])
+        self.v_proj.weight = nn.Parameter(self.w_qkv[self.n_q + self.n_kv:])
         self.o_proj = nn.Linear(Hq * hd, cfg.hidden, bias=False, **fk)
         self.q_norm = nn.Parameter(torch.ones(hd, device=device))
         self.k_norm = nn.Parameter(torch.ones(hd, device=device))
 
-    def project(self, x, cos, sin):
+    def project(self, x, cos, sin, pos):
         """q [B, H_q, T, hd], k/v [B, H_kv, T, hd] (normed, rotated), gate [B, T, H_q*hd]."""
         B, T, _ = x.shape
         c = self.cfg
-        qg = self.q_proj(x).view(B, T, c.H_q, 2 * c.head_dim)
-        q, gate = qg[..., :c.head_dim], qg[..., c.head_dim:]
-        k = self.k_proj(x).view(B, T, c.H_kv, c.head_dim)
-        v = self.v_proj(x).view(B, T, c.H_kv, c.head_dim)
-        q = rms_norm(q, self.q_norm, c.eps).transpose(1, 2)
-        k = rms_norm(k, self.k_norm, c.eps).transpose(1, 2)
-        q = apply_rope(q, cos, sin).to(x.dtype).contiguous()
-        k = apply_rope(k, cos, sin).to(x.dtype).contiguous()
-        v = v.transpose(1, 2).contiguous()
-        return q, k, v, gate.reshape(B, T, c.H_q * c.head_dim).contiguous()
+        qkv = F.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
+        ld = qkv.shape[-1]
+        q = torch.empty(B, c.H_q, T, c.head_dim, dtype=x.dtype, device=x.device)
+        k = torch.empty(B, c.H_kv, T, c.head_dim, dtype=x.dtype, device=x.device)
+        v = torch.empty_like(k)
+        gate = torch.empty(B, T, c.H_q * c.head_dim, dtype=x.dtype, device=x.device)
+        base = qkv.data_ptr()
+        es = qkv.element_size()
+        rc = _lib.load().anemll_qk_norm_rope(
+            base, ld, base + self.n_q * es, ld, base + (self.n_q + self.n_kv) * es, ld, _lib.ptr(self.q_norm),
+            _lib.ptr(self.k_norm), _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(gate),
+            _lib.dtype_code(x.dtype), B, T, c.H_q, c.H_kv, c.head_dim, int(pos), float(c.eps),
+            _lib.stream_ptr(x.device))
+        _lib.check(rc, "anemll_qk_norm_rope")
+        return q, k, v, gate
 
     def forward(self, x, k_cache, v_cache, pos, cos, sin):
-        q, k, v, gate = self.project(x, cos, sin)
+        """``cos``/``sin``: the whole [ctx, hd] tables; this call's rows start at ``pos``."""
+        q, k, v, gate = self.project(x, cos, sin, pos)
         o = attention.kv_attention(q, k_cache, v_cache, pos, k_new=k, v_new=v, gate=gate)
         return self.o_proj(o)
 
@@ -154,30 +195,41 @@ class HybridStack(nn.Module):
                 st.append(m.new_states(B))
         return st
 
+    def mixer(self, i, h, state, pos):
+        """Layer i's attention or gated-DeltaNet block on its normed input h [B, T, hidden]."""
+        m = self.mixers[i]
+        if isinstance(m, GatedAttention):
+            return m(h, state[0], state[1], pos, self.cos, self.sin)
+        return m(h, state[0], state[1], use_precomputed_states=pos > 0)
+
+    def mlp(self, i, h):
+        return self.down[i](silu_mul(self.gate_up[i](h)))
+
     def layer(self, i, x, state, pos, with_mixer=False):
         """One decoder layer on x [B, T, hidden] at positions [pos, pos + T).  ``with_mixer``: also return
         the mixer's (attention or gated-DeltaNet) output before the residual add."""
         c = self.cfg
-        m = self.mixers[i]
-        h = rms_norm(x, self.norm1[i], c.eps)
-        T = x.shape[1]
-        if isinstance(m, GatedAttention):
-            h = m(h, state[0], state[1], pos, self.cos[pos:pos + T], self.sin[pos:pos + T])
-        else:
-            h = m(h, state[0], state[1], use_precomputed_states=pos > 0)
-        x = x + h
-        gu = self.gate_up[i](rms_norm(x, self.norm2[i], c.eps))
-        gate, up = gu.chunk(2, dim=-1)
-        y = x + self.down[i](F.silu(gate) * up)
+        h = self.mixer(i, rms_norm(x, self.norm1[i], c.eps), state, pos)
+        x2, n2 = rms_norm(x, self.norm2[i], c.eps, residual=h)
+        y = x2 + self.mlp(i, n2)
         return (y, h) if with_mixer else y
 
     @torch.no_grad()
     def forward_tokens(self, ids, state, pos):
-        """ids [B, T] at positions [pos, pos + T) -> logits of the last position [B, vocab]."""
+        """ids [B, T] at positions [pos, pos + T) -> logits of the last position [B, vocab].  The
+        residual adds ride on the next norm (one ``anemll_rmsnorm`` per add + norm)."""
+        c = self.cfg
         x = self.embed(ids)
-        for i in range(self.cfg.n_layers):
-            x = self.layer(i, x, state[i], pos)
-        return self.lm_head(rms_norm(x[:, -1], self.norm, self.cfg.eps))
+        h = rms_norm(x, self.norm1[0], c.eps)
+        for i in range(c.n_layers):
+            x, h = rms_norm(x, self.norm2[i], c.eps, residual=self.mixer(i, h, state[i], pos))
+            nxt = self.norm1[i + 1] if i + 1 < c.n_layers else self.norm
+            d = self.mlp(i, h)
+            if i + 1 < c.n_layers:
+                x, h = rms_norm(x, nxt, c.eps, residual=d)
+            else:  # the final norm: last position only
+                _, h = rms_norm(x[:, -1], nxt, c.eps, residual=d[:, -1])
+        return self.lm_head(h)
 
     @torch.no_grad()
     def generate(self, prompt, n_steps, gather=None, graphs=False):

@@ -221,6 +221,38 @@ int anemll_kv_rotate_append(void* cache, const void* new_rows, int dtype, int64_
 int anemll_kv_state_transition(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n_slabs,
                                int src_len, int dst_len, int d, int current_position, float pad_value, void* stream);
 
+/* ---- decoder-stack epilogues (the hybrid stack's glue between its GEMMs) ---- */
+
+/*
+ * RMSNorm over rows of d elements: out = x * rsqrt(mean(x^2) + eps) * weight (fp32 arithmetic, one
+ * rounding to dtype).  With residual != NULL the norm is of s = x + residual (rounded to dtype),
+ * and s is stored to sum_out (which may be x itself).  The stack's pre-norms and final norm
+ * (QwenRMSNorm, anemll/models/qwen_model.py:101-141, with the residual adds of QwenDecoderLayer,
+ * 559-577).  weight fp32 [d]; d a multiple of 8, at most 4096; pointers 16-byte aligned.
+ */
+int anemll_rmsnorm(const void* x, const void* residual, void* sum_out, const float* weight, void* out,
+                   int dtype, int64_t rows, int d, float eps, void* stream);
+
+/*
+ * SwiGLU activation of a [rows][2 ffn] gate|up GEMM output: out[r][j] = silu(gate) * up, with
+ * silu rounded to dtype before the product (QwenMLP.forward, qwen_model.py:286-298).
+ */
+int anemll_silu_mul(const void* gate_up, void* out, int dtype, int64_t rows, int ffn, void* stream);
+
+/*
+ * Attention-layer prologue after the q/k/v projections: per-head RMSNorm of q and k (QwenHeadNorm,
+ * qwen_model.py:143-184), rotary embedding at positions [pos, pos + T) from fp32 cos/sin tables
+ * [>= pos + T][head_dim] (apply_rotary_pos_emb, 186-261), and the layout change to the attention
+ * op's inputs.  q_gate: per token H_q x [query | gate] head_dim each (row stride qg_row_stride
+ * elements); k, v: per token H_kv x head_dim.  Outputs q [B][H_q][T][hd], k and v [B][H_kv][T][hd],
+ * gate [B][T][H_q hd].  fp16/bf16; head_dim 128 or 256; 16-byte aligned rows.
+ */
+int anemll_qk_norm_rope(const void* q_gate, int64_t qg_row_stride, const void* k, int64_t k_row_stride,
+                        const void* v, int64_t v_row_stride, const float* q_norm, const float* k_norm,
+                        const float* cos_table, const float* sin_table, void* q_out, void* k_out, void* v_out,
+                        void* gate_out, int dtype, int B, int T, int H_q, int H_kv, int head_dim, int pos,
+                        float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

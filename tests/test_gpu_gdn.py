@@ -119,13 +119,13 @@ def test_invalid_arguments_raise():
                                         torch.zeros(1, 1, 64, 64, device=DEV))
 
 
-def _prologue_case(B, T, use_state, seed):
+def _prologue_case(B, T, use_state, seed, K=4):
     torch.manual_seed(seed)
     Hqk, Hv = 16, 32
     C = 2 * Hqk * 128 + Hv * 128
     x = torch.randn(B, T, C).bfloat16()
-    w = 0.1 * torch.randn(C, 4)
-    cs = torch.randn(B, C, 4).bfloat16() if use_state else torch.zeros(B, C, 4).bfloat16()
+    w = 0.1 * torch.randn(C, K)
+    cs = torch.randn(B, C, K).bfloat16() if use_state else torch.zeros(B, C, K).bfloat16()
     a = torch.randn(B, T, Hv).bfloat16()
     bb = torch.randn(B, T, Hv).bfloat16()
     A_log = torch.empty(Hv).uniform_(0, 2.77)
@@ -133,9 +133,10 @@ def _prologue_case(B, T, use_state, seed):
     return Hqk, Hv, x, w, cs, a, bb, A_log, dtb
 
 
-@pytest.mark.parametrize("B,T,use_state", [(1, 512, False), (2, 37, True), (3, 1, True), (1, 2, True), (2, 3, False)])
-def test_prologue_matches_oracle(B, T, use_state):
-    Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(B, T, use_state, 10 + T)
+@pytest.mark.parametrize("B,T,use_state,K", [(1, 512, False, 4), (2, 37, True, 4), (3, 1, True, 4), (1, 2, True, 4),
+                                             (2, 3, False, 4), (2, 20, True, 6), (1, 3, True, 2), (2, 17, False, 8)])
+def test_prologue_matches_oracle(B, T, use_state, K):
+    Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(B, T, use_state, 10 + T, K)
     cs_dev = cs.to(DEV)
     q, k, v, g, beta = gdn.gdn_prologue(x.to(DEV), w.to(DEV), cs_dev, a.to(DEV), bb.to(DEV), A_log.to(DEV),
                                         dtb.to(DEV), Hqk, Hv, use_state=use_state, out_dtype=torch.float32)
