@@ -28,8 +28,10 @@ _SIGS = {
                                     _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp], _c_int),
     "anemll_gdn_chunked_error": ([_c_int], _c_int),
     "anemll_gdn_prologue": ([_vp, _c_int, _vp, _vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _vp, _c_int, _vp, _vp,
-                             _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp], _c_int),
-    "anemll_gated_rmsnorm": ([_vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_i64, _c_int, _c_float, _vp], _c_int),
+                             _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp],
+                            _c_int),
+    "anemll_gated_rmsnorm": ([_vp, _c_int, _vp, _c_int, _vp, _vp, _c_int, _c_i64, _c_int, _c_float, _c_i64, _c_i64,
+                              _vp], _c_int),
     "anemll_kv_attention_workspace_size": ([_c_int, _c_int, _c_int, _c_int, _c_int, _c_int], _c_size),
     "anemll_kv_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp, _c_int,
                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,

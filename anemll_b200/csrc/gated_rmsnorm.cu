@@ -8,15 +8,20 @@
 namespace anemll {
 namespace {
 
+// z row r: dense (zh == 0), or head r % zh of token r / zh with token rows z_ld elements apart
+__device__ __forceinline__ int64_t z_offset(int64_t r, int d, int64_t zh, int64_t z_ld) {
+  return zh ? (r / zh) * z_ld + (r % zh) * d : r * d;
+}
+
 template <typename TX, typename TZ, typename TO>
 __global__ void __launch_bounds__(256)
 gated_rmsnorm_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const float* __restrict__ w,
-                     TO* __restrict__ out, int64_t rows, int d, float eps) {
+                     TO* __restrict__ out, int64_t rows, int d, float eps, int64_t zh, int64_t z_ld) {
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const TX* xr = x + row * d;
-  const TZ* zr = z + row * d;
+  const TZ* zr = z + z_offset(row, d, zh, z_ld);
   float ss = 0.f;
   for (int i = lane; i < d; i += 32) {
     const float xv = to_f32(xr[i]);
@@ -34,7 +39,7 @@ gated_rmsnorm_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const f
 template <typename TX, typename TZ, typename TO, int NC>
 __global__ void __launch_bounds__(256)
 gated_rmsnorm_vec_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const float* __restrict__ w,
-                         TO* __restrict__ out, int64_t rows, int d, float eps) {
+                         TO* __restrict__ out, int64_t rows, int d, float eps, int64_t zh, int64_t z_ld) {
   const int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
   const int l = threadIdx.x & 15;
   const unsigned hmask = 0xffffu << (threadIdx.x & 16);
@@ -45,7 +50,7 @@ gated_rmsnorm_vec_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, con
     const int col = (c * 16 + l) * 8;
     if (col < d) {
       load8(x + row * d + col, xv[c]);
-      load8(z + row * d + col, zv[c]);
+      load8(z + z_offset(row, d, zh, z_ld) + col, zv[c]);
     }
   }
   float ss = 0.f;
@@ -79,26 +84,34 @@ using namespace anemll;
 
 extern "C" int anemll_gated_rmsnorm(const void* x, int x_dtype, const void* z, int z_dtype,
                                     const float* weight, void* out, int out_dtype,
-                                    int64_t rows, int d, float eps, void* stream) {
+                                    int64_t rows, int d, float eps, int64_t z_heads, int64_t z_row_stride,
+                                    void* stream) {
   ANEMLL_REQUIRE(x && z && weight && out, ANEMLL_EINVAL, "gated_rmsnorm: null pointer");
   ANEMLL_REQUIRE(rows >= 0 && d > 0, ANEMLL_EINVAL, "gated_rmsnorm: bad sizes");
+  ANEMLL_REQUIRE(z_heads >= 0 && (z_heads == 0 || z_row_stride >= z_heads * d), ANEMLL_EINVAL,
+                 "gated_rmsnorm: z row stride shorter than z_heads * d");
+  ANEMLL_REQUIRE(dtype_ok(x_dtype) && dtype_ok(z_dtype) && dtype_ok(out_dtype), ANEMLL_EUNSUPPORTED,
+                 "gated_rmsnorm: bad dtype");
   if (rows == 0) return ANEMLL_OK;
   cudaStream_t st = (cudaStream_t)stream;
   const unsigned blocks = (unsigned)((rows + 7) / 8);
+  const bool z_vec_ok = z_heads == 0 || (z_row_stride * dtype_size(z_dtype)) % 16 == 0;
   return ANEMLL_DISPATCH_DTYPE(x_dtype, TX, [&] {
     return ANEMLL_DISPATCH_DTYPE(z_dtype, TZ, [&] {
       return ANEMLL_DISPATCH_DTYPE(out_dtype, TO, [&] {
-        const bool vec = d % 8 == 0 && d <= 512 && aligned(x, 16) && aligned(z, 16) && aligned(out, 16);
+        const bool vec = d % 8 == 0 && d <= 512 && aligned(x, 16) && aligned(z, 16) && aligned(out, 16) && z_vec_ok;
         const unsigned vblocks = (unsigned)((rows + 15) / 16);
         if (vec && d <= 128)
           gated_rmsnorm_vec_kernel<TX, TZ, TO, 1><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
-                                                                          (TO*)out, rows, d, eps);
+                                                                          (TO*)out, rows, d, eps, z_heads,
+                                                                          z_row_stride);
         else if (vec)
           gated_rmsnorm_vec_kernel<TX, TZ, TO, 4><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
-                                                                          (TO*)out, rows, d, eps);
+                                                                          (TO*)out, rows, d, eps, z_heads,
+                                                                          z_row_stride);
         else
           gated_rmsnorm_kernel<TX, TZ, TO><<<blocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight, (TO*)out,
-                                                                   rows, d, eps);
+                                                                   rows, d, eps, z_heads, z_row_stride);
         return launch_status("gated_rmsnorm");
       });
     });

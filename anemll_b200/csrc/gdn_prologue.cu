@@ -33,13 +33,16 @@ __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
                           : __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
 }
 
-// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) for one (token, v-head)
+// g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b) for one (token, v-head); a and b rows
+// (tokens) are ab_ld elements apart, g and beta are dense
 __device__ __forceinline__ void gate_elem(long long idx, int Hv, const void* a, const void* bgate, int ab_dt,
-                                          const float* A_log, const float* dt_bias, float* go, float* betao) {
+                                          long long ab_ld, const float* A_log, const float* dt_bias, float* go,
+                                          float* betao) {
   const int h = (int)(idx % Hv);
-  float av = load_any(a, ab_dt, idx);
+  const long long src = (idx / Hv) * ab_ld + h;
+  float av = load_any(a, ab_dt, src);
   if (dt_bias) av += dt_bias[h];
-  const float bv = load_any(bgate, ab_dt, idx);
+  const float bv = load_any(bgate, ab_dt, src);
   go[idx] = -expf(A_log[h]) * softplus(av);
   betao[idx] = 1.0f / (1.0f + expf(-bv));
 }
@@ -79,10 +82,10 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
                      const void* __restrict__ a, const void* __restrict__ bgate, int ab_dt, const float* __restrict__ A_log,
                      const float* __restrict__ dt_bias, TOut* __restrict__ qo, TOut* __restrict__ ko,
                      TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao, int B, int T, int Hqk,
-                     int Hv, int K, int use_state, int n_tiles, int conv_ctas) {
+                     int Hv, int K, int use_state, int n_tiles, int conv_ctas, long long x_ld, long long ab_ld) {
   if ((int)blockIdx.x >= conv_ctas) {
     const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
-    if (idx < (long long)B * T * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, A_log, dt_bias, go, betao);
+    if (idx < (long long)B * T * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, ab_ld, A_log, dt_bias, go, betao);
     return;
   }
   extern __shared__ __align__(16) uint8_t smem[];
@@ -98,7 +101,7 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
   const int c = threadIdx.x;
   const int t0 = tile * TT, nt = min(TT, T - t0);
   const int nrows = nt + K - 1;
-  const TIn* xg = x + (long long)b * T * C + grp * HDIM;
+  const TIn* xg = x + (long long)b * T * x_ld + grp * HDIM;  // token rows are x_ld elements apart
   TIn* cs = conv_state + ((long long)b * C + grp * HDIM) * K;
 
   // rows from x: 16-byte asynchronous copies; rows before token 0: the old state (or zeros)
@@ -107,7 +110,7 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
     const int r = i / CPR, ch = i % CPR;
     const int pos = t0 - (K - 1) + r;
     if (pos >= 0) cp_async16(reinterpret_cast<uint8_t*>(X) + r * ROWB + ch * 16,
-                             reinterpret_cast<const uint8_t*>(xg + (long long)pos * C) + ch * 16);
+                             reinterpret_cast<const uint8_t*>(xg + (long long)pos * x_ld) + ch * 16);
   }
   cp_async_commit();
   if (t0 == 0) {
@@ -165,7 +168,7 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
     for (int j = 0; j < MAXK; ++j) {
       if (j < K) {
         const int pos = T - K + j;
-        nv[j] = pos >= 0 ? xg[(long long)pos * C + c] : X[(pos + K - 1) * HDIM + c];
+        nv[j] = pos >= 0 ? xg[(long long)pos * x_ld + c] : X[(pos + K - 1) * HDIM + c];
       }
     }
 #pragma unroll
@@ -205,10 +208,10 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
                       const void* __restrict__ a, const void* __restrict__ bgate, int ab_dt,
                       const float* __restrict__ A_log, const float* __restrict__ dt_bias, TOut* __restrict__ qo,
                       TOut* __restrict__ ko, TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao,
-                      int B, int Hqk, int Hv, int use_state, int conv_ctas) {
+                      int B, int Hqk, int Hv, int use_state, int conv_ctas, long long x_ld, long long ab_ld) {
   if ((int)blockIdx.x >= conv_ctas) {
     const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
-    if (idx < (long long)B * TS * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, A_log, dt_bias, go, betao);
+    if (idx < (long long)B * TS * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, ab_ld, A_log, dt_bias, go, betao);
     return;
   }
   constexpr int K = 4;
@@ -217,7 +220,7 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
   const int grp = blockIdx.x % ngroups, b = blockIdx.x / ngroups;
   const int c = threadIdx.x, ch = grp * HDIM + c;
   TIn* cs = conv_state + ((long long)b * C + ch) * K;
-  const TIn* xg = x + (long long)b * TS * C + ch;
+  const TIn* xg = x + (long long)b * TS * x_ld + ch;
 
   TIn raw[K + TS];
   if constexpr (sizeof(TIn) == 2) {
@@ -235,7 +238,7 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
     for (int j = 0; j < K; ++j) raw[j] = use_state ? cs[j] : from_f32<TIn>(0.f);
   }
 #pragma unroll
-  for (int t = 0; t < TS; ++t) raw[K + t] = xg[(long long)t * C];
+  for (int t = 0; t < TS; ++t) raw[K + t] = xg[(long long)t * x_ld];
   const float4 w4 = *reinterpret_cast<const float4*>(w + (long long)ch * K);
 
   float y[TS];
@@ -273,7 +276,8 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
 template <typename TIn, typename TOut>
 int launch_prologue(const void* x, const float* w, void* cs, const void* a, const void* bg, int ab_dt,
                     const float* A_log, const float* dt_bias, void* qo, void* ko, void* vo, float* go, float* bo,
-                    int B, int T, int Hqk, int Hv, int K, int use_state, cudaStream_t st) {
+                    int B, int T, int Hqk, int Hv, int K, int use_state, long long x_ld, long long ab_ld,
+                    cudaStream_t st) {
   const int ngroups = 2 * Hqk + Hv;
   const long long gate_ctas = ((long long)B * T * Hv + HDIM - 1) / HDIM;
   if (T <= DEC_T && K == 4) {
@@ -282,7 +286,7 @@ int launch_prologue(const void* x, const float* w, void* cs, const void* a, cons
     const unsigned grid = (unsigned)(conv_ctas + gate_ctas);
     auto go_short = [&](auto kern) {
       kern<<<grid, HDIM, 0, st>>>((const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko,
-                                  (TOut*)vo, go, bo, B, Hqk, Hv, use_state, (int)conv_ctas);
+                                  (TOut*)vo, go, bo, B, Hqk, Hv, use_state, (int)conv_ctas, x_ld, ab_ld);
     };
     switch (T) {
       case 1: go_short(prologue_short_kernel<TIn, TOut, 1>); break;
@@ -299,7 +303,7 @@ int launch_prologue(const void* x, const float* w, void* cs, const void* a, cons
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       kern<<<(unsigned)(conv_ctas + gate_ctas), HDIM, smem, st>>>(
           (const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko, (TOut*)vo, go, bo, B, T,
-          Hqk, Hv, K, use_state, n_tiles, (int)conv_ctas);
+          Hqk, Hv, K, use_state, n_tiles, (int)conv_ctas, x_ld, ab_ld);
     };
     if (K == 4) go_tile(prologue_tile_kernel<TIn, TOut, 4>);
     else go_tile(prologue_tile_kernel<TIn, TOut, 0>);
@@ -318,7 +322,7 @@ extern "C" int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const fl
                                    void* q_out, void* k_out, void* v_out, int out_dtype,
                                    float* g_out, float* beta_out,
                                    int B, int T, int H_qk, int H_v, int d_k, int d_v, int conv_k,
-                                   int use_state, void* stream) {
+                                   int use_state, int64_t x_row_stride, int64_t ab_row_stride, void* stream) {
   ANEMLL_REQUIRE(mixed_qkv && conv_w && conv_state && a && b && A_log && q_out && k_out && v_out && g_out &&
                      beta_out,
                  ANEMLL_EINVAL, "gdn_prologue: null pointer");
@@ -327,6 +331,11 @@ extern "C" int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const fl
   ANEMLL_REQUIRE(conv_k >= 1 && conv_k <= MAXK, ANEMLL_EUNSUPPORTED, "gdn_prologue: conv_k must be in [1, %d]", MAXK);
   ANEMLL_REQUIRE(dtype_ok(in_dtype) && dtype_ok(ab_dtype) && dtype_ok(out_dtype), ANEMLL_EUNSUPPORTED,
                  "gdn_prologue: bad dtype");
+  const long long C = (2LL * H_qk + H_v) * HDIM;
+  const long long x_ld = x_row_stride ? x_row_stride : C, ab_ld = ab_row_stride ? ab_row_stride : H_v;
+  ANEMLL_REQUIRE(x_ld >= C && ab_ld >= H_v, ANEMLL_EINVAL, "gdn_prologue: row strides shorter than the rows");
+  ANEMLL_REQUIRE(x_ld * dtype_size(in_dtype) % 16 == 0, ANEMLL_EINVAL,
+                 "gdn_prologue: the mixed_qkv row stride must be a multiple of 16 bytes");
   ANEMLL_REQUIRE(aligned(mixed_qkv, 16) && aligned(conv_w, 16) && aligned(conv_state, 8) && aligned(q_out, 16) &&
                      aligned(k_out, 16) && aligned(v_out, 16),
                  ANEMLL_EINVAL, "gdn_prologue: mixed_qkv, conv_w and the outputs must be 16-byte aligned, "
@@ -335,7 +344,7 @@ extern "C" int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const fl
   return ANEMLL_DISPATCH_DTYPE(in_dtype, TIn, [&] {
     return ANEMLL_DISPATCH_DTYPE(out_dtype, TOut, [&] {
       return launch_prologue<TIn, TOut>(mixed_qkv, conv_w, conv_state, a, b, ab_dtype, A_log, dt_bias, q_out, k_out,
-                                        v_out, g_out, beta_out, B, T, H_qk, H_v, conv_k, use_state, st);
+                                        v_out, g_out, beta_out, B, T, H_qk, H_v, conv_k, use_state, x_ld, ab_ld, st);
     });
   });
 }

@@ -21,6 +21,7 @@ import math
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib
 
@@ -143,18 +144,46 @@ def chunked_device_error(reset=True) -> int:
     return int(_lib.load().anemll_gdn_chunked_error(int(bool(reset))))
 
 
+def _token_stride(t):
+    """Elements between consecutive token rows of a [B, T, width] tensor whose rows are dense (unit
+    stride along the width) with one uniform token stride, e.g. a column slice of a wider projection
+    output; None for any other layout."""
+    B, T, W = t.shape
+    if t.stride(2) != 1 and W > 1:
+        return None
+    if T > 1:
+        ld = t.stride(1)
+        if B > 1 and t.stride(0) != ld * T:
+            return None
+    else:
+        ld = t.stride(0) if B > 1 else W
+    return ld if ld >= W else None
+
+
+def _rows_for_kernel(t, align):
+    """``t`` and its token stride, copied to a dense aligned tensor when its layout or alignment
+    (``align`` bytes for the pointer and the row stride) does not suit the kernel."""
+    ld = _token_stride(t)
+    if ld is None or t.data_ptr() % align or (ld * t.element_size()) % align:
+        t = t.contiguous()
+        if t.data_ptr() % align:
+            t = t.clone()
+        ld = t.shape[2]
+    return t, ld
+
+
 def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k_heads, num_v_heads,
                  head_k_dim=128, head_v_dim=128, use_state=True, out_dtype=torch.float16):
     """conv1d(+SiLU) over ``mixed_qkv`` [B,T,C], split, l2-normalise q/k, gates.
 
     ``conv_weight`` [C, K] fp32; ``conv_state`` [B, C, K] (dtype of ``mixed_qkv``)
     is read as history when ``use_state`` and always receives the last K raw
-    inputs.  Returns ``q, k`` [B,T,H_qk,d_k], ``v`` [B,T,H_v,d_v] (``out_dtype``),
-    ``g, beta`` [B,T,H_v] fp32.
+    inputs.  ``mixed_qkv``, ``a`` and ``b`` may be column slices of one wider
+    projection output (dense rows, uniform token stride).  Returns ``q, k``
+    [B,T,H_qk,d_k], ``v`` [B,T,H_v,d_v] (``out_dtype``), ``g, beta`` [B,T,H_v] fp32.
     """
     _need_cuda(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias)
-    for n, t in (("mixed_qkv", mixed_qkv), ("conv_weight", conv_weight), ("conv_state", conv_state),
-                 ("a", a), ("b", b), ("A_log", A_log)):
+    for n, t in (("conv_weight", conv_weight), ("conv_state", conv_state), ("A_log", A_log)):
         _need_contig(n, t)
     B, T, C = mixed_qkv.shape
     K = conv_weight.shape[1]
@@ -166,6 +195,12 @@ def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k
         raise TypeError("conv_weight and A_log must be float32")
     if a.dtype != b.dtype:
         raise TypeError("a and b must share a dtype")
+    mixed_qkv, x_ld = _rows_for_kernel(mixed_qkv, 16)
+    a, a_ld = _rows_for_kernel(a, 1)
+    b, b_ld = _rows_for_kernel(b, 1)
+    if a_ld != b_ld:
+        a, b = a.contiguous(), b.contiguous()
+        a_ld = num_v_heads
     dev = mixed_qkv.device
     q = torch.empty(B, T, num_k_heads, head_k_dim, dtype=out_dtype, device=dev)
     k = torch.empty_like(q)
@@ -177,24 +212,35 @@ def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k
         _lib.ptr(mixed_qkv), _lib.dtype_code(mixed_qkv.dtype), _lib.ptr(conv_weight), _lib.ptr(conv_state),
         _lib.ptr(a), _lib.ptr(b), _lib.dtype_code(a.dtype), _lib.ptr(A_log), _lib.ptr(dtb),
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.dtype_code(out_dtype), _lib.ptr(g), _lib.ptr(beta),
-        B, T, num_k_heads, num_v_heads, head_k_dim, head_v_dim, K, int(bool(use_state)), _lib.stream_ptr(dev))
+        B, T, num_k_heads, num_v_heads, head_k_dim, head_v_dim, K, int(bool(use_state)), x_ld, a_ld,
+        _lib.stream_ptr(dev))
     _lib.check(rc, "anemll_gdn_prologue")
     return q, k, v, g, beta
 
 
 def gated_rmsnorm(x, z, weight, eps=1e-6, out_dtype=None):
-    """``weight * x * rsqrt(mean(x^2)+eps) * silu(z)`` over the last dim."""
+    """``weight * x * rsqrt(mean(x^2)+eps) * silu(z)`` over the last dim.  ``z`` may be a column slice
+    of a wider projection output: [B, T, H, d] with dense heads and a uniform token stride."""
     _need_cuda(x, z, weight)
     _need_contig("x", x)
-    _need_contig("z", z)
     d = x.shape[-1]
     if z.shape != x.shape or weight.shape != (d,):
         raise ValueError("gated_rmsnorm: shape mismatch")
+    z_heads, z_ld = 0, 0
+    if not z.is_contiguous():
+        ok = z.dim() == 4 and z.stride(-1) == 1 and z.stride(-2) == d
+        if ok:
+            B, T, H = z.shape[:3]
+            z_ld = z.stride(1) if T > 1 else z.stride(0)
+            ok = (B == 1 or T == 1 or z.stride(0) == z_ld * T)
+            z_heads = H
+        if not ok:
+            z, z_heads, z_ld = z.contiguous(), 0, 0
     w = weight.float().contiguous()
     out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
     rc = _lib.load().anemll_gated_rmsnorm(_lib.ptr(x), _lib.dtype_code(x.dtype), _lib.ptr(z), _lib.dtype_code(z.dtype),
                                           _lib.ptr(w), _lib.ptr(out), _lib.dtype_code(out.dtype), x.numel() // d, d,
-                                          float(eps), _lib.stream_ptr(x.device))
+                                          float(eps), z_heads, z_ld, _lib.stream_ptr(x.device))
     _lib.check(rc, "anemll_gated_rmsnorm")
     return out
 
@@ -225,10 +271,16 @@ class GatedDeltaNet(nn.Module):
         self.core_dtype = core_dtype
         self.chunk_size = chunk_size
         fk = dict(device=device, dtype=dtype)
-        self.in_proj_qkv = nn.Linear(hidden_size, self.conv_dim, bias=False, **fk)
-        self.in_proj_z = nn.Linear(hidden_size, self.value_dim, bias=False, **fk)
-        self.in_proj_b = nn.Linear(hidden_size, num_v_heads, bias=False, **fk)
-        self.in_proj_a = nn.Linear(hidden_size, num_v_heads, bias=False, **fk)
+        # the four input projections are views of one [qkv | z | b | a] weight: one GEMM, whose column
+        # slices the prologue and the gated norm read in place
+        widths = (self.conv_dim, self.value_dim, num_v_heads, num_v_heads)
+        self.w_in = torch.empty(sum(widths), hidden_size, **fk)
+        off = 0
+        for name, n in zip(("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a"), widths):
+            lin = nn.Linear(hidden_size, n, bias=False, device="meta")
+            lin.weight = nn.Parameter(self.w_in[off:off + n])
+            setattr(self, name, lin)
+            off += n
         self.conv_weight = nn.Parameter(torch.zeros(self.conv_dim, conv_kernel, device=device, dtype=torch.float32))
         self.dt_bias = nn.Parameter(torch.zeros(num_v_heads, device=device, dtype=torch.float32))
         self.A_log = nn.Parameter(torch.zeros(num_v_heads, device=device, dtype=torch.float32))
@@ -248,8 +300,8 @@ class GatedDeltaNet(nn.Module):
         B, T, _ = mixed_qkv.shape
         if not use_precomputed_states:
             recurrent_state.zero_()
-        q, k, v, g, beta = gdn_prologue(mixed_qkv.contiguous(), self.conv_weight, conv_state, a.contiguous(),
-                                        b.contiguous(), self.A_log, self.dt_bias, self.num_k_heads,
+        q, k, v, g, beta = gdn_prologue(mixed_qkv, self.conv_weight, conv_state, a, b, self.A_log, self.dt_bias,
+                                        self.num_k_heads,
                                         self.num_v_heads, self.head_k_dim, self.head_v_dim,
                                         use_state=use_precomputed_states, out_dtype=self.core_dtype)
         if T > 1 and not use_precomputed_states:
@@ -257,15 +309,15 @@ class GatedDeltaNet(nn.Module):
                                         out_dtype=torch.float32)
         else:
             o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
-        normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim).contiguous(), self.norm_weight,
+        normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim), self.norm_weight,
                                self.eps, out_dtype=mixed_qkv.dtype)
         return o, normed
 
     def forward(self, hidden_states, conv_state, recurrent_state, use_precomputed_states=False):
         B, T, _ = hidden_states.shape
-        mixed_qkv = self.in_proj_qkv(hidden_states)
-        z = self.in_proj_z(hidden_states)
-        b = self.in_proj_b(hidden_states)
-        a = self.in_proj_a(hidden_states)
+        proj = F.linear(hidden_states, self.w_in)  # [B, T, conv_dim + value_dim + 2 H_v]
+        c, v = self.conv_dim, self.value_dim
+        mixed_qkv, z = proj[..., :c], proj[..., c:c + v]
+        b, a = proj[..., c + v:c + v + self.num_v_heads], proj[..., c + v + self.num_v_heads:]
         _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states)
         return self.out_proj(normed.reshape(B, T, self.value_dim))

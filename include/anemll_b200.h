@@ -104,6 +104,9 @@ int anemll_gdn_chunked_error(int reset);
  * conv_state.  conv_state always receives the last conv_k raw inputs.
  * conv_w [C, conv_k] fp32; A_log, dt_bias [H_v] fp32 (dt_bias may be NULL);
  * a, b [B, T, H_v] in ab_dtype.  q/k/v outputs in out_dtype, g/beta fp32.
+ * Token rows of mixed_qkv are x_row_stride elements apart (0: C, dense; a
+ * multiple of 16 bytes), those of a and b ab_row_stride (0: H_v), so that all
+ * four can be column slices of one fused projection output.
  */
 int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const float* conv_w, void* conv_state,
                         const void* a, const void* b, int ab_dtype,
@@ -111,15 +114,19 @@ int anemll_gdn_prologue(const void* mixed_qkv, int in_dtype, const float* conv_w
                         void* q_out, void* k_out, void* v_out, int out_dtype,
                         float* g_out, float* beta_out,
                         int B, int T, int H_qk, int H_v, int d_k, int d_v, int conv_k,
-                        int use_state, void* stream);
+                        int use_state, int64_t x_row_stride, int64_t ab_row_stride, void* stream);
 
 /*
  * Gated RMSNorm: out = weight * x * rsqrt(mean(x^2) + eps) * silu(z) over rows
  * of length d.  Replaces Qwen3_5RMSNormGated (modeling_qwen3_5.py:175-190).
+ * x and out are dense [rows][d].  z is dense too when z_heads == 0; otherwise
+ * row r of z is head r % z_heads of token r / z_heads, token rows
+ * z_row_stride elements apart (a column slice of a fused projection output).
  */
 int anemll_gated_rmsnorm(const void* x, int x_dtype, const void* z, int z_dtype,
                          const float* weight, void* out, int out_dtype,
-                         int64_t rows, int d, float eps, void* stream);
+                         int64_t rows, int d, float eps, int64_t z_heads, int64_t z_row_stride,
+                         void* stream);
 
 /*
  * KV-cache attention with the cache write fused in (one call = one prefill

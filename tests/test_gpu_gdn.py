@@ -194,3 +194,28 @@ def test_gdn_layer_prefill_then_decode_matches_oracle():
                              rel_l2=5e-3, max_abs=6.25e-2)
                 assert torch.equal(conv_state.cpu(), ref_conv.to(torch.bfloat16)), "conv state"
                 assert_close(rec_state, ref_state, f"state step {step}")
+
+
+@pytest.mark.parametrize("T,use_state", [(1, True), (3, True), (200, False)])
+def test_prologue_and_gated_norm_read_projection_slices(T, use_state):
+    """The layer's fused [qkv | z | b | a] projection output read in place (token-strided column
+    slices) gives bit-for-bit the results of dense copies of the same slices."""
+    Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(2, T, use_state, 50 + T)
+    C = x.shape[-1]
+    z = torch.randn(2, T, Hv * 128).bfloat16()
+    fused = torch.cat([x, z, bb, a], dim=-1).to(DEV)
+    xs, zs = fused[..., :C], fused[..., C:C + Hv * 128]
+    bs, as_ = fused[..., C + Hv * 128:C + Hv * 128 + Hv], fused[..., C + Hv * 128 + Hv:]
+    cs1, cs2 = cs.to(DEV), cs.to(DEV)
+    args = (w.to(DEV), A_log.to(DEV), dtb.to(DEV))
+    got = gdn.gdn_prologue(xs, args[0], cs1, as_, bs, args[1], args[2], Hqk, Hv, use_state=use_state)
+    ref = gdn.gdn_prologue(xs.contiguous(), args[0], cs2, as_.contiguous(), bs.contiguous(), args[1], args[2], Hqk,
+                           Hv, use_state=use_state)
+    for g_, r_ in zip(got, ref):
+        assert torch.equal(g_, r_)
+    assert torch.equal(cs1, cs2)
+    o = torch.randn(2, T, Hv, 128, device=DEV)
+    nw = torch.rand(128, device=DEV) + 0.5
+    n1 = gdn.gated_rmsnorm(o, zs.view(2, T, Hv, 128), nw, out_dtype=torch.bfloat16)
+    n2 = gdn.gated_rmsnorm(o, zs.contiguous().view(2, T, Hv, 128), nw, out_dtype=torch.bfloat16)
+    assert torch.equal(n1, n2)
