@@ -128,6 +128,15 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 
 // ------------------------------------------------------------------ TMA -----
+// 2-D tiled TMA load (no multicast) of one box into this CTA's shared memory.
+__device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const void* tmap, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+          "r"(smem_dst),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) of one box into shared memory; completion
 // is counted on `bar` in bytes.  The innermost coordinate x must make x *
 // element size a multiple of 16 bytes.

@@ -11,7 +11,9 @@ followed by a SwiGLU MLP, both pre-normed (RMSNorm) with residuals.
   k (``QwenHeadNorm``, ``anemll/models/qwen_model.py:143-184``), rotary embedding
   (``apply_rotary_pos_emb``, 186-261), then :func:`anemll_b200.attention.kv_attention` with the cache
   write fused in and the gate applied in its epilogue, then o_proj.
-* Projections, norms, RoPE, the MLP and the LM head are torch ops (bf16 GEMMs).
+* Projections and the LM head: ``dense.linear`` (the library's weight-streaming GEMM at decode, torch's
+  GEMM for the prefill's long inputs); norms, RoPE and the SwiGLU: the fused kernels of
+  ``stack_ops.cu``.
 
 Caches and states are per sequence: KV caches ``[B, H_kv, ctx, hd]`` per attention layer, conv and
 recurrent states per GDN layer.  Weights are random N(0, 0.02) (no checkpoints offline).
@@ -24,7 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _lib, attention, gdn
+from . import _lib, attention, dense, gdn
 
 __all__ = ["StackConfig", "HybridStack", "GreedyDecoder", "nccl_id_gather", "shard", "rms_norm", "silu_mul",
            "rope_tables"]
@@ -116,7 +118,7 @@ class GatedAttention(nn.Module):
         """q [B, H_q, T, hd], k/v [B, H_kv, T, hd] (normed, rotated), gate [B, T, H_q*hd]."""
         B, T, _ = x.shape
         c = self.cfg
-        qkv = F.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
+        qkv = dense.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
         ld = qkv.shape[-1]
         q = torch.empty(B, c.H_q, T, c.head_dim, dtype=x.dtype, device=x.device)
         k = torch.empty(B, c.H_kv, T, c.head_dim, dtype=x.dtype, device=x.device)
@@ -136,7 +138,7 @@ class GatedAttention(nn.Module):
         """``cos``/``sin``: the whole [ctx, hd] tables; this call's rows start at ``pos``."""
         q, k, v, gate = self.project(x, cos, sin, pos)
         o = attention.kv_attention(q, k_cache, v_cache, pos, k_new=k, v_new=v, gate=gate)
-        return self.o_proj(o)
+        return dense.linear(o, self.o_proj.weight)
 
 
 class HybridStack(nn.Module):
@@ -203,7 +205,7 @@ class HybridStack(nn.Module):
         return m(h, state[0], state[1], use_precomputed_states=pos > 0)
 
     def mlp(self, i, h):
-        return self.down[i](silu_mul(self.gate_up[i](h)))
+        return dense.linear(silu_mul(dense.linear(h, self.gate_up[i].weight)), self.down[i].weight)
 
     def layer(self, i, x, state, pos, with_mixer=False):
         """One decoder layer on x [B, T, hidden] at positions [pos, pos + T).  ``with_mixer``: also return
@@ -229,7 +231,7 @@ class HybridStack(nn.Module):
                 x, h = rms_norm(x, nxt, c.eps, residual=d)
             else:  # the final norm: last position only
                 _, h = rms_norm(x[:, -1], nxt, c.eps, residual=d[:, -1])
-        return self.lm_head(h)
+        return dense.linear(h, self.lm_head.weight)
 
     @torch.no_grad()
     def generate(self, prompt, n_steps, gather=None, graphs=False):

@@ -260,6 +260,19 @@ int anemll_qk_norm_rope(const void* q_gate, int64_t qg_row_stride, const void* k
                         void* gate_out, int dtype, int B, int T, int H_q, int H_kv, int head_dim, int pos,
                         float eps, void* stream);
 
+/*
+ * y[M][N] = x[M][K] . w[N][K]^T, fp16 or bf16 (dtype), fp32 accumulation, y in the same type; row
+ * strides ldx, ldw, ldy in elements (multiples of 8, pointers 16-byte aligned).  Built for few rows
+ * (the decode steps' projections, where the weights stream through once): 128 x 128 tcgen05 tiles
+ * fed by TMA, K split over a thread-block cluster of up to 8 CTAs whose fp32 partial tiles are summed
+ * through distributed shared memory.  Replaces the projections of the reference's layers at decode
+ * (the Conv2d / Linear projections of anemll/models/qwen_model.py, e.g. QwenMLP 272-298).
+ */
+int anemll_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
+                int dtype, void* stream);
+/* Non-zero if a GEMM launch stopped on a bounded wait (synchronous; reset != 0 clears it). */
+int anemll_gemm_error(int reset);
+
 #ifdef __cplusplus
 }
 #endif
