@@ -2,7 +2,7 @@
 //
 // Channels come in 128-channel head groups (H_qk q-heads, H_qk k-heads, H_v v-heads).  Two kernels:
 //
-// * Tile kernel (T > DEC_T): a CTA of 128 threads owns one sequence, one head group and TT = 64
+// * Tile kernel (T > DEC_T): a CTA of 128 threads owns one sequence, one head group and TT = 32
 //   tokens.  Its input rows (the tile plus the conv_k - 1 rows before it) are copied into shared
 //   memory with 16-byte cp.async; each thread then runs the conv + SiLU of a channel pair over half
 //   the tile from shared memory into an fp32 tile, and the four warps finish row by row (a warp per
@@ -23,7 +23,7 @@ namespace anemll {
 namespace {
 
 constexpr int HDIM = 128;  // channels per head group (d_k == d_v); threads per CTA
-constexpr int TT = 64;     // tokens per tile
+constexpr int TT = 32;     // tokens per tile (32: eight CTAs, 32 warps per SM)
 constexpr int MAXK = 8;    // largest supported conv kernel
 constexpr int DEC_T = 4;   // longest call served by the short kernel
 
@@ -95,8 +95,9 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
 
   const int ngroups = 2 * Hqk + Hv;
   const int C = ngroups * HDIM;
-  const int tile = blockIdx.x % n_tiles;
-  const int grp = (blockIdx.x / n_tiles) % ngroups;
+  // head groups fastest: neighbouring CTAs read neighbouring 256-byte segments of the same token rows
+  const int grp = blockIdx.x % ngroups;
+  const int tile = (blockIdx.x / ngroups) % n_tiles;
   const int b = blockIdx.x / (n_tiles * ngroups);
   const int c = threadIdx.x;
   const int t0 = tile * TT, nt = min(TT, T - t0);
