@@ -1264,6 +1264,36 @@ int launch_kv_dec(KvParams& p, const Plan& pl0, cudaStream_t st) {
   return rc;
 }
 
+// New rows k_new / v_new [B][H_kv][S][HD] -> cache rows [pos, pos + S), 16-byte vectors.  The tcgen05
+// prefill path runs this first for chunks of TC_PREWRITE_MIN tokens or more: its attention kernel
+// then reads every row, new or old, with TMA and no block has rows to patch.
+constexpr int TC_PREWRITE_MIN = 16;
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(256)
+kv_write_rows_kernel(const T* __restrict__ kn, const T* __restrict__ vn, T* __restrict__ kc, T* __restrict__ vc,
+                     int Hkv, int S, int pos, long long bs, long long hs, long long n_vec) {
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n_vec) return;
+  constexpr int VPR = HD / 8;  // 16-byte vectors per row
+  const long long row = i / VPR;  // (b, h, s)
+  const int v = (int)(i % VPR), s = (int)(row % S);
+  const long long bh = row / S;
+  const int h = (int)(bh % Hkv), b = (int)(bh / Hkv);
+  const long long dst = (long long)b * bs + (long long)h * hs + (long long)(pos + s) * HD + v * 8;
+  reinterpret_cast<uint4*>(kc + dst)[0] = reinterpret_cast<const uint4*>(kn + row * HD + v * 8)[0];
+  reinterpret_cast<uint4*>(vc + dst)[0] = reinterpret_cast<const uint4*>(vn + row * HD + v * 8)[0];
+}
+
+template <typename T, int HD>
+int launch_kv_write_rows(const KvParams& p, cudaStream_t st) {
+  const long long n_vec = (long long)p.B * p.Hkv * p.S * (HD / 8);
+  kv_write_rows_kernel<T, HD><<<(unsigned)((n_vec + 255) / 256), 256, 0, st>>>(
+      reinterpret_cast<const T*>(p.k_new), reinterpret_cast<const T*>(p.v_new), reinterpret_cast<T*>(p.kc),
+      reinterpret_cast<T*>(p.vc), p.Hkv, p.S, p.pos, p.bs, p.hs, n_vec);
+  return launch_status("kv_attention_write_rows");
+}
+
 bool tc_eligible(int S, int Hq, int Hkv, int hd, long long bs, long long hs, const void* out, const void* gate) {
   return Hq / Hkv == 8 && (hd == 128 || hd == 256) && S >= 16 && (hs * 2) % 16 == 0 && (bs * 2) % 16 == 0 &&
          aligned(out, 16) && (!gate || aligned(gate, 16));
@@ -1308,6 +1338,19 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
     rc = launch_combine<T, HD>(q, st);
   }
   return rc;
+}
+
+// tcgen05 prefill path: long chunks write their new rows with a copy kernel first (the attention
+// kernel, launched dependent on it, waits for it before its first load), short ones patch them in.
+template <typename T, int HD>
+int launch_kv_tc_rows(KvParams& p, const Plan& pl, cudaStream_t st) {
+  if (!p.has_new || p.S < TC_PREWRITE_MIN) return launch_kv_tc<T, HD>(p, pl, st);
+  int rc = launch_kv_write_rows<T, HD>(p, st);
+  if (rc) return rc;
+  KvParams q = p;
+  q.has_new = 0;
+  q.k_new = q.v_new = nullptr;
+  return launch_kv_tc<T, HD>(q, pl, st);
 }
 
 }  // namespace
@@ -1381,11 +1424,11 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
     switch (head_dim) {
       case 64: return use_dec ? launch_kv_dec<T, 64>(p, pl, st) : launch_kv<T, 64>(p, pl, st);
       case 128:
-        return use_tc ? launch_kv_tc<T, 128>(p, pl, st)
+        return use_tc ? launch_kv_tc_rows<T, 128>(p, pl, st)
                : use_dec ? launch_kv_dec<T, 128>(p, pl, st)
                          : launch_kv<T, 128>(p, pl, st);
       default:
-        return use_tc ? launch_kv_tc<T, 256>(p, pl, st)
+        return use_tc ? launch_kv_tc_rows<T, 256>(p, pl, st)
                : use_dec ? launch_kv_dec<T, 256>(p, pl, st)
                          : launch_kv<T, 256>(p, pl, st);
     }
