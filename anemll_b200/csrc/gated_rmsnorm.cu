@@ -71,7 +71,8 @@ gated_rmsnorm_vec_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, con
     if (col < d) {
       float o[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = w[col + e] * xv[c][e] * r * silu(zv[c][e]);
+      for (int e = 0; e < 8; ++e)
+        o[e] = w[col + e] * xv[c][e] * r * __fdividef(zv[c][e], 1.0f + __expf(-zv[c][e]));  // silu(z)
       store8(out + row * d + col, o);
     }
   }

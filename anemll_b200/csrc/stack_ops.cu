@@ -3,8 +3,10 @@
 // pass over their rows, 16-byte vectors.
 //
 //   rmsnorm      out = bf(x * rsqrt(mean(x^2) + eps) * w), optionally after the residual add
-//                s = bf(x + r) (s written back); a warp per row, or a CTA per row for few rows;
-//   silu_mul     out = bf(bf(silu(gate)) * up) for a [gate | up] GEMM output (SwiGLU);
+//                s = bf(x + r) (s written back); a CTA per row (a warp per row for rows of at
+//                most 256 elements);
+//   silu_mul     out = bf(bf(silu(gate)) * up) for a [gate | up] GEMM output (SwiGLU; the fast
+//                exponential and division, whose few-ulp error vanishes in the rounding to bf16);
 //   qk_norm_rope per-head RMSNorm of q and k (QwenHeadNorm, anemll/models/qwen_model.py:143-184)
 //                then the rotary embedding x cos + rotate_half(x) sin (apply_rotary_pos_emb,
 //                qwen_model.py:186-261), q/k/v moved to the head-major layout the attention op
@@ -96,7 +98,7 @@ __device__ __forceinline__ void rms_store(T* sum_out, bool has_res, const float*
   }
 }
 
-// many rows: a warp per row
+// short rows: a warp per row
 template <typename T, int NC>
 __global__ void __launch_bounds__(NT)
 rmsnorm_kernel(const T* x, const T* res, T* sum_out, const float* __restrict__ w, T* __restrict__ out,
@@ -110,7 +112,8 @@ rmsnorm_kernel(const T* x, const T* res, T* sum_out, const float* __restrict__ w
   rms_store<T, NC>(res ? sum_out + row * d : nullptr, res != nullptr, w, out + row * d, d, lane, 32, r, v);
 }
 
-// few rows (decode): a CTA per row, so that the rows spread over the SMs
+// a CTA per row: eight warps share the row, so that few rows (decode) spread over the SMs and many
+// rows keep several loads in flight per thread at low register use
 template <typename T>
 __global__ void __launch_bounds__(NT)
 rmsnorm_row_kernel(const T* x, const T* res, T* sum_out, const float* __restrict__ w, T* __restrict__ out, int d,
@@ -143,7 +146,7 @@ silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, long long rows, i
   load8(gu + row * 2 * ffn + ffn + col, u);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    const float s = to_f32(from_f32<T>(g[e] / (1.0f + expf(-g[e]))));
+    const float s = to_f32(from_f32<T>(__fdividef(g[e], 1.0f + __expf(-g[e]))));  // rounded to T, as stored
     o[e] = s * u[e];
   }
   store8(out + row * ffn + col, o);
@@ -247,12 +250,12 @@ extern "C" int anemll_rmsnorm(const void* x, const void* residual, void* sum_out
   return ANEMLL_DISPATCH_DTYPE(dtype, T, [&] {
     const T* xx = (const T*)x;
     const T* rr = (const T*)residual;
-    if (rows <= 2 * 148 || nc > 8)
+    // rows of more than 256 elements: a CTA per row (8 warps, a few loads in flight per thread, low
+    // register use); shorter rows: a warp per row
+    if (nc > 1)
       rmsnorm_row_kernel<T><<<(unsigned)rows, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, d, eps);
-    else if (nc <= 4)
-      rmsnorm_kernel<T, 4><<<blocks, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, rows, d, eps);
     else
-      rmsnorm_kernel<T, 8><<<blocks, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, rows, d, eps);
+      rmsnorm_kernel<T, 1><<<blocks, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, rows, d, eps);
     return launch_status("rmsnorm");
   });
 }

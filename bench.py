@@ -804,6 +804,8 @@ def bench_stack(args, ws, rank, local):
     from anemll_b200.stack import GreedyDecoder, HybridStack, StackConfig, nccl_id_gather, shard
     dev = torch.device("cuda", local)
     cfg = StackConfig()
+    # the job (128 x (1024 + 256)) unless a smaller profiling case is asked for
+    STACK_B, STACK_PREFILL, STACK_DECODE = args.stack_seqs, args.stack_prefill, args.stack_decode
     model = HybridStack(cfg, device=dev).init_weights(STACK_SEED)
     g = torch.Generator().manual_seed(STACK_SEED)
     prompt_job = torch.randint(0, cfg.vocab, (STACK_B, STACK_PREFILL), generator=g)
@@ -1130,6 +1132,9 @@ def main():
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
     ap.add_argument("--prefill-len", type=int, default=PREFILL_T, help="gdn_prefill: tokens per sequence")
+    ap.add_argument("--stack-seqs", type=int, default=STACK_B, help="stack: sequences (profiling cases)")
+    ap.add_argument("--stack-prefill", type=int, default=STACK_PREFILL, help="stack: prompt tokens")
+    ap.add_argument("--stack-decode", type=int, default=STACK_DECODE, help="stack: greedy decode steps")
     args = ap.parse_args()
     if args.steps is None:
         args.steps = 3 if args.config == "stack" else 2560
