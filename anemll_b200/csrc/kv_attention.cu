@@ -790,6 +790,25 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       p.ws_ml[row_id * 2 + 0] = m_run;
       p.ws_ml[row_id * 2 + 1] = l_run;
     }
+    // the tile's gate rows are copied into shared memory in one go (the Q and K regions are free:
+    // every MMA has completed), so that no store of the slices below waits on a global load
+    const bool gated = p.n_splits == 1 && p.gate != nullptr;
+    constexpr int GLD = HD + 8;  // staged gate row stride (elements): 16-byte units, banks spread
+    T* gs = reinterpret_cast<T*>(sm + OFF_Q);
+    static_assert(128 * GLD * (int)sizeof(T) <= OFF_V - OFF_Q, "the gate tile fits in the Q and K regions");
+    if (gated) {
+      for (int i = tid; i < 128 * (HD / 8); i += 128) {
+        const int r = i / (HD / 8), ch = i % (HD / 8);
+        const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
+        if (rs < p.S)
+          cp_async16(gs + r * GLD + ch * 8,
+                     reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD +
+                         ch * 8);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncthreads();
+    }
 #pragma unroll 1
     for (int c = 0; c < HD / 32; ++c) {
       float o[32];
@@ -822,16 +841,16 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         for (int it = 0; it < 4; ++it) {
           const int idx = tid + it * 128, r = idx >> 2, c8 = idx & 3;
           const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
+          const long long off = ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD + c * 32 + c8 * 8;
           if (rs < p.S) {
-            const long long off = ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD + c * 32 + c8 * 8;
             const float4 a = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8) ^ (r & 7)) << 2));
             const float4 bq = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8 + 1) ^ (r & 7)) << 2));
             float v[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
-            if (p.gate) {
-              const uint4 gu = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.gate) + off);
+            if (gated) {
+              const uint4 gu = *reinterpret_cast<const uint4*>(gs + r * GLD + c * 32 + c8 * 8);
               const T* gh = reinterpret_cast<const T*>(&gu);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] *= 1.f / (1.f + __expf(-to_f32(gh[e])));
+              for (int e = 0; e < 8; ++e) v[e] *= __frcp_rn(1.f + __expf(-to_f32(gh[e])));  // sigmoid
             }
             uint4 u;
             T* h = reinterpret_cast<T*>(&u);
