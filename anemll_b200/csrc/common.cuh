@@ -57,6 +57,9 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// 1 / (1 + e^-x) with the fast exponential and reciprocal (a few ulp; the IEEE division is a long
+// instruction sequence, and gates are applied to every output element)
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // 2^x with the hardware approximation instruction (PTX ex2.approx.ftz.f32;
 // relative error about 2^-22, -inf -> 0): the softmax exponent.

@@ -307,8 +307,8 @@ kv_attn_kernel(KvParams p) {
         const int d = i * 8 + t4 * 2;
         float v0 = o_acc[i][h * 2] * inv, v1 = o_acc[i][h * 2 + 1] * inv;
         if (grow) {
-          v0 *= 1.f / (1.f + __expf(-to_f32(grow[d])));
-          v1 *= 1.f / (1.f + __expf(-to_f32(grow[d + 1])));
+          v0 *= sigmoid_fast(to_f32(grow[d]));
+          v1 *= sigmoid_fast(to_f32(grow[d + 1]));
         }
         *reinterpret_cast<uint32_t*>(orow + d) = pack2<T>(v0, v1);
       }
@@ -413,7 +413,7 @@ kv_combine_kernel(KvParams p) {
     for (int w = 0; w < CB_WARPS; ++w) a += s_acc[w][d];
     const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
     float val = a / L;
-    if (p.gate) val *= 1.f / (1.f + __expf(-to_f32(reinterpret_cast<const T*>(p.gate)[o])));
+    if (p.gate) val *= sigmoid_fast(to_f32(reinterpret_cast<const T*>(p.gate)[o]));
     reinterpret_cast<T*>(p.out)[o] = from_f32<T>(val);
   }
 }
@@ -850,7 +850,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
               const uint4 gu = *reinterpret_cast<const uint4*>(gs + r * GLD + c * 32 + c8 * 8);
               const T* gh = reinterpret_cast<const T*>(&gu);
 #pragma unroll
-              for (int e = 0; e < 8; ++e) v[e] *= __frcp_rn(1.f + __expf(-to_f32(gh[e])));  // sigmoid
+              for (int e = 0; e < 8; ++e) v[e] *= sigmoid_fast(to_f32(gh[e]));
             }
             uint4 u;
             T* h = reinterpret_cast<T*>(&u);
@@ -1180,7 +1180,7 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
         const uint2 gu = *reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p.gate) + off);
         const T* gh = reinterpret_cast<const T*>(&gu);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] *= 1.f / (1.f + __expf(-to_f32(gh[e])));
+        for (int e = 0; e < 4; ++e) v[e] *= sigmoid_fast(to_f32(gh[e]));
       }
       uint2 u;
       T* hh = reinterpret_cast<T*>(&u);
