@@ -724,6 +724,32 @@ def bench_cache_ops(args, ws, rank, local):
             ms += e0.elapsed_time(e1)
     barrier(ws)
     ms_max = max_over_ranks(ms, ws, dev)
+
+    # end to end through the public ops: the step's new rows (key, value, the 64-token chunk) and
+    # the mask copied in from pinned host memory, the calls (eager), and the rows the step wrote into
+    # the local cache (its newest row and the mask-written rows of every slot) read back
+    h_in = [t.cpu().pin_memory() for t in (key, val, new, mask)]
+    d_in = (key, val, new, mask)
+    h_out = torch.empty(2 * nl, H, 65, hd, dtype=torch.half).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in h_in)
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        for d, h in zip(d_in, h_in):
+            d.copy_(h, non_blocking=True)
+        step()
+        h_out[:, :, :64].copy_(kv[:, :, 200:264], non_blocking=True)
+        h_out[:, :, 64:].copy_(kv[:, :, sw - 1:], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    e2e_steps = min(args.steps, 50)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
     es = 2
     b_rot = nl * 2 * H * 2 * sw * hd * es            # every slot read and written once
     b_mask = nl * 2 * H * 3 * 64 * hd * es            # new rows read, touched rows read and written
@@ -753,6 +779,8 @@ def bench_cache_ops(args, ws, rank, local):
                      "frac": gbs / pk["hbm_gbs"], "peak_source": how, "algorithmic_bytes_per_step": bytes_step,
                      "traffic": None,
                      "bytes": {"rotate": b_rot, "update_mask": b_mask, "transition": b_tr}},
+        "e2e": {"value": ws * bytes_step * e2e_steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s", "steps": e2e_steps,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps * (2 * nl + 2 * nl + 1),
         "clocks": clk.summary(),
     }
