@@ -1025,24 +1025,13 @@ def cpu_stack_sample(threads, T=64, n_dec=2):
     the 4096-row cache) for one sequence: a T-token prefill and n_dec greedy steps through all 24
     layers, the final norm and the LM head; returns tokens/s.  The weights are fp32 copies of a
     random block tiled over each parameter (the values do not change the timing)."""
-    from anemll_b200.stack import HybridStack, StackConfig, rope_tables
+    from anemll_b200.stack import StackConfig
     from oracle import stack as ost
     torch.set_num_threads(threads)
     cfg = StackConfig()
-    model = HybridStack(cfg, device="meta", dtype=torch.float32).to_empty(device="cpu")
-    model.cos, model.sin = rope_tables(cfg.head_dim, cfg.ctx, cfg.rope_theta, "cpu")
-    base = torch.randn(1 << 20, generator=torch.Generator().manual_seed(STACK_SEED)) * 0.02
-    with torch.no_grad():
-        for name, p in model.named_parameters():
-            flat = p.view(-1)
-            if "norm" in name and p.dim() == 1:
-                p.fill_(1.0)
-            elif name.endswith("A_log") or name.endswith("dt_bias"):
-                p.fill_(0.5)
-            else:
-                for i in range(0, flat.numel(), base.numel()):
-                    n = min(base.numel(), flat.numel() - i)
-                    flat[i:i + n].copy_(base[:n] * (5.0 if name.endswith("conv_weight") else 1.0))
+    model = _CPU_STACK.get("model")
+    if model is None:
+        model = _CPU_STACK["model"] = _cpu_stack_model(cfg)
     state = ost.new_state(model, 1)
     ids = torch.randint(0, cfg.vocab, (1, T), generator=torch.Generator().manual_seed(STACK_SEED))
     t0 = time.perf_counter()
@@ -1057,6 +1046,29 @@ def cpu_stack_sample(threads, T=64, n_dec=2):
     dt = time.perf_counter() - t0
     return (T + n_dec) / dt, (f"1 sequence: a {T}-token prefill and {n_dec} greedy steps through the 24 layers, "
                               "fp32 torch GEMMs with the CPU oracle's GDN core and attention")
+
+
+_CPU_STACK = {}  # the host model of the CPU samples, built once per process
+
+
+def _cpu_stack_model(cfg):
+    """The stack's shapes on the host in fp32, weights a random block tiled over each parameter."""
+    from anemll_b200.stack import HybridStack, rope_tables
+    model = HybridStack(cfg, device="meta", dtype=torch.float32).to_empty(device="cpu")
+    model.cos, model.sin = rope_tables(cfg.head_dim, cfg.ctx, cfg.rope_theta, "cpu")
+    base = torch.randn(1 << 20, generator=torch.Generator().manual_seed(STACK_SEED)) * 0.02
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            flat = p.view(-1)
+            if "norm" in name and p.dim() == 1:
+                p.fill_(1.0)
+            elif name.endswith("A_log") or name.endswith("dt_bias"):
+                p.fill_(0.5)
+            else:
+                for i in range(0, flat.numel(), base.numel()):
+                    n = min(base.numel(), flat.numel() - i)
+                    flat[i:i + n].copy_(base[:n] * (5.0 if name.endswith("conv_weight") else 1.0))
+    return model
 
 
 def traffic_from_profiles(name):
