@@ -14,6 +14,7 @@ import torch
 from . import build as _build
 
 F32, F16, BF16 = 0, 1, 2
+EUNSUPPORTED = -2  # ANEMLL_EUNSUPPORTED: the entry point does not take this shape
 _DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
 _c_int, _c_i64, _c_float, _vp, _c_size = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
@@ -36,6 +37,9 @@ _SIGS = {
     "anemll_kv_attention": ([_vp, _vp, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_i64, _vp, _c_int,
                              _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                              _vp, _c_size, _vp], _c_int),
+    "anemll_kv_attention_qkv": ([_vp, _c_i64, _vp, _vp, _vp, _vp, _c_float, _vp, _vp, _c_i64, _c_i64, _vp, _c_int,
+                                 _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _vp, _c_size,
+                                 _vp], _c_int),
     "anemll_kv_attention_noalloc_max_scratch": ([], _c_size),
     "anemll_kv_attention_error": ([_c_int], _c_int),
     "anemll_kv_update_mask": ([_vp, _vp, _c_int, _vp, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_i64, _c_i64,

@@ -124,6 +124,45 @@ def kv_attention(query_states, k_cache, v_cache, current_pos, k_new=None, v_new=
     return out
 
 
+def kv_attention_qkv(qkv, q_norm, k_norm, cos, sin, eps, k_cache, v_cache, current_pos, H_q, H_kv, head_dim,
+                     window=0, window_chunk_aligned=False, out=None, workspace=None):
+    """One attention call with the layer's prologue fused in (``anemll_kv_attention_qkv``).
+
+    ``qkv`` [B, S, H_q*2*hd + 2*H_kv*hd] is the fused projection output (per head ``[query | gate]``,
+    then k, then v; rows may be spaced by a stride); ``q_norm``/``k_norm`` fp32 [hd]; ``cos``/``sin``
+    fp32 [>= pos+S, hd].  The new K/V rows are written into ``k_cache``/``v_cache`` [B, H_kv, ctx, hd].
+    Returns the gated output [B, S, H_q*hd], or None when the shape needs the separate
+    ``anemll_qk_norm_rope`` kernel (see the C ABI)."""
+    for t in (qkv, q_norm, k_norm, cos, sin, k_cache, v_cache):
+        if not t.is_cuda:
+            raise RuntimeError("anemll_b200 ops take CUDA tensors (no CPU path)")
+    B, S, width = qkv.shape
+    if qkv.stride(-1) != 1 or (S > 1 and B > 1 and qkv.stride(0) != qkv.stride(1) * S):
+        raise ValueError("qkv rows must be dense with a uniform token stride")
+    ld = qkv.stride(1) if S > 1 else (qkv.stride(0) if B > 1 else width)
+    if k_cache.dim() == 3:
+        k_cache, v_cache = k_cache.unsqueeze(0), v_cache.unsqueeze(0)
+    _, Hkv2, ctx, hd2 = k_cache.shape
+    if Hkv2 != H_kv or hd2 != head_dim or k_cache.stride() != v_cache.stride():
+        raise ValueError("cache shape does not match the head configuration")
+    bstride = k_cache.stride(0) if k_cache.shape[0] == B and B > 1 else 0
+    if out is None:
+        out = torch.empty(B, S, H_q * head_dim, dtype=qkv.dtype, device=qkv.device)
+    need = kv_attention_workspace_size(B, S, H_q, H_kv, head_dim, ctx)
+    if workspace is None:
+        workspace = _workspace(qkv.device, need)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = _lib.load().anemll_kv_attention_qkv(
+        qkv.data_ptr(), ld, _lib.ptr(q_norm), _lib.ptr(k_norm), _lib.ptr(cos), _lib.ptr(sin), float(eps),
+        _lib.ptr(k_cache), _lib.ptr(v_cache), bstride, k_cache.stride(1), _lib.ptr(out), _lib.dtype_code(qkv.dtype),
+        B, S, H_q, H_kv, head_dim, ctx, int(current_pos), int(window), int(bool(window_chunk_aligned)),
+        _lib.ptr(workspace), ws_bytes, _lib.stream_ptr(qkv.device))
+    if rc == _lib.EUNSUPPORTED:
+        return None
+    _lib.check(rc, "anemll_kv_attention_qkv")
+    return out
+
+
 class QwenAttentionB200(nn.Module):
     """The attention core of ``QwenAttention`` with the reference's method signatures.
 

@@ -111,6 +111,55 @@ __device__ __forceinline__ void store8(T* p, const float* f) {
   }
 }
 
+
+// ---- per-head RMSNorm + rotary embedding (QwenHeadNorm then apply_rotary_pos_emb) ----
+// x = T(x * rsqrt(mean(x^2) + eps) * w) (fp32, one rounding to the storage type), then
+// y = x cos + rotate_half(x) sin with the products and the sum rounded separately in fp32.  The sum
+// of squares is a fixed tree: 32 partial sums of EPL consecutive squares (one per lane of a warp
+// that holds the row, lane l owning [l EPL, (l+1) EPL)), combined like warp_sum.  Every caller
+// (a warp per row, or one thread per row) follows it, so all produce the same bits.
+template <typename T>
+__device__ __forceinline__ float head_norm_round(float x, float rn, float w) {
+  return to_f32(from_f32<T>(__fmul_rn(__fmul_rn(x, rn), w)));
+}
+__device__ __forceinline__ float rope_one(float x, float partner_rot, float c, float s) {
+  return __fadd_rn(__fmul_rn(x, c), __fmul_rn(partner_rot, s));
+}
+
+// A warp holds the row: lane l has x[0..EPL) = elements [l EPL, (l+1) EPL); the rotation partner of
+// element i (i +- HD/2) sits in lane l ^ 16.  w, cr, sr point at element 0 of the weight and of this
+// position's cos/sin rows.
+template <typename T, int EPL>
+__device__ __forceinline__ void head_norm_rope_warp(float* x, const float* w, const float* cr, const float* sr,
+                                                    float eps, int lane) {
+  constexpr int HD = EPL * 32;
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
+  ss = warp_sum(ss);
+  const float rn = rsqrtf(ss / (float)HD + eps);
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) x[e] = head_norm_round<T>(x[e], rn, w[lane * EPL + e]);
+  const bool lower = lane < 16;  // first half: rotate_half gives -x[i + HD/2]
+  float y[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
+    y[e] = rope_one(x[e], lower ? -partner : partner, cr[lane * EPL + e], sr[lane * EPL + e]);
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) x[e] = y[e];
+}
+
+// The same result from one thread: rsqrt(mean(x^2) + eps) of a row given its 32 partial sums
+// (partial l = the sum of squares of elements [l EPL, (l+1) EPL), accumulated in order).
+__device__ __forceinline__ float head_norm_scale(float* part, int HD, float eps) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < o; ++i) part[i] = part[i] + part[i + o];
+  return rsqrtf(part[0] / (float)HD + eps);
+}
 }  // namespace anemll
 
 // Dispatch an element type code to a C++ type alias `T`.

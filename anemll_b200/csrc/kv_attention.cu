@@ -49,7 +49,22 @@ struct KvParams {
   float* ws_o;
   float* ws_ml;
   float scale_log2;
+  long long gate_ts, gate_hs;  // gate element (b, s, head, d) at (b S + s) gate_ts + head gate_hs + d
+  // fused head norm + RoPE: q, k_new, v_new and gate are column slices of one q/k/v projection output
+  // whose token rows are qkv_ld elements apart; q and k_new are normed and rotated on the way in
+  int fused;
+  long long qkv_ld;
+  const float* qnw;
+  const float* knw;
+  const float* cos_t;
+  const float* sin_t;
+  float eps;
 };
+
+// gate element (b, s, head hq, column d)
+__device__ __forceinline__ long long gate_index(const KvParams& p, int b, int s, int hq, int d) {
+  return ((long long)b * p.S + s) * p.gate_ts + (long long)hq * p.gate_hs + d;
+}
 
 __device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
 
@@ -299,9 +314,7 @@ kv_attn_kernel(KvParams p) {
     if (p.n_splits == 1) {
       const float inv = 1.f / l_run[h];
       T* orow = reinterpret_cast<T*>(p.out) + ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD;
-      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + s) * p.Hq * HD +
-                                   (long long)hq * HD
-                             : nullptr;
+      const T* grow = p.gate ? reinterpret_cast<const T*>(p.gate) + gate_index(p, b, s, hq, 0) : nullptr;
 #pragma unroll
       for (int i = 0; i < NTILE_O; ++i) {
         const int d = i * 8 + t4 * 2;
@@ -413,7 +426,7 @@ kv_combine_kernel(KvParams p) {
     for (int w = 0; w < CB_WARPS; ++w) a += s_acc[w][d];
     const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
     float val = a / L;
-    if (p.gate) val *= sigmoid_fast(to_f32(reinterpret_cast<const T*>(p.gate)[o]));
+    if (p.gate) val *= sigmoid_fast(to_f32(reinterpret_cast<const T*>(p.gate)[gate_index(p, b, s, hq, d)]));
     reinterpret_cast<T*>(p.out)[o] = from_f32<T>(val);
   }
 }
@@ -617,11 +630,87 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   if (tid == 0) {
     tc::mbar_arrive_expect_tx(qb, (uint32_t)(NKB * Q_BLK));
 #pragma unroll
-    for (int c = 0; c < NKB; ++c)
-      tc::tma_load_3d(sbase + OFF_Q + c * Q_BLK, &maps.q, c * 64, tile * 16, b * p.Hq + kvh * G, qb);
+    for (int c = 0; c < NKB; ++c) {
+      if (p.fused)  // straight from the q/k/v projection output: {column, token, head, sequence}
+        tc::tma_load_4d(sbase + OFF_Q + c * Q_BLK, &maps.q, c * 64, tile * 16, kvh * G, b, qb);
+      else
+        tc::tma_load_3d(sbase + OFF_Q + c * Q_BLK, &maps.q, c * 64, tile * 16, b * p.Hq + kvh * G, qb);
+    }
     if (nblk > 0) issue_kv(0);
   }
+  // fused head norm: this tile's cos/sin rows and the q_norm weights into shared memory while the Q
+  // tile is in flight (the second K and V buffers and the P tile are idle until the key loop)
+  constexpr int FLD = HD + 4;  // staged table row stride (floats): 16-byte units, banks spread
+  float* f_cos = reinterpret_cast<float*>(sm + OFF_K + NKB * KV_BLK);
+  float* f_sin = reinterpret_cast<float*>(sm + OFF_V + NKB * KV_BLK);
+  float* f_w = reinterpret_cast<float*>(sm + OFF_P);
+  static_assert(16 * FLD * 4 <= NKB * KV_BLK && HD * 4 <= 128 * 128, "staged tables fit the idle buffers");
+  if (p.fused) {
+    for (int i = tid; i < 2 * 16 * (HD / 4); i += 128) {
+      const int tb = i / (16 * (HD / 4)), rem = i % (16 * (HD / 4)), st = rem / (HD / 4), c4 = rem % (HD / 4);
+      if (tile * 16 + st < p.S)
+        cp_async16((tb ? f_sin : f_cos) + st * FLD + c4 * 4,
+                   (tb ? p.sin_t : p.cos_t) + (long long)(p.pos + tile * 16 + st) * HD + c4 * 4);
+    }
+    for (int i = tid; i < HD / 4; i += 128) cp_async16(f_w + i * 4, p.qnw + i * 4);
+    cp_async_commit();
+  }
   bool ok = __syncthreads_and(tc::mbar_wait(qb, 0));
+  if (p.fused) {
+    cp_async_wait<0>();
+    __syncthreads();
+  }
+  if (p.fused && ok) {
+    // head norm + RoPE of this thread's query row, in place in the swizzled tile (thread tid owns
+    // row tid: head tid / 16, token tile * 16 + tid % 16); same arithmetic as head_norm_rope_warp
+    const int srow = tile * 16 + (tid & 15);
+    if (srow < p.S) {
+      constexpr int EPL = HD / 32, PPC = 8 / EPL;  // elements per partial, partials per 8-element chunk
+      float part[32];
+#pragma unroll
+      for (int k = 0; k < HD / 8; ++k) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + OFF_Q + (k >> 3) * Q_BLK + swz128(tid, k & 7));
+        const T* h = reinterpret_cast<const T*>(&u);
+#pragma unroll
+        for (int q2 = 0; q2 < PPC; ++q2) {
+          float ss = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) {
+            const float v = to_f32(h[q2 * EPL + e]);
+            ss += v * v;
+          }
+          part[k * PPC + q2] = ss;
+        }
+      }
+      const float rn = head_norm_scale(part, HD, p.eps);
+      const float* cr = f_cos + (tid & 15) * FLD;
+      const float* sr = f_sin + (tid & 15) * FLD;
+#pragma unroll 1
+      for (int k = 0; k < HD / 16; ++k) {  // chunk k of the first half with chunk k + HD/16
+        const int k2 = k + HD / 16;
+        uint8_t* pl = sm + OFF_Q + (k >> 3) * Q_BLK + swz128(tid, k & 7);
+        uint8_t* ph = sm + OFF_Q + (k2 >> 3) * Q_BLK + swz128(tid, k2 & 7);
+        uint4 ul = *reinterpret_cast<const uint4*>(pl), uh = *reinterpret_cast<const uint4*>(ph);
+        T* hl = reinterpret_cast<T*>(&ul);
+        T* hh = reinterpret_cast<T*>(&uh);
+        float xl[8], xh[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xl[e] = head_norm_round<T>(to_f32(hl[e]), rn, f_w[k * 8 + e]);
+          xh[e] = head_norm_round<T>(to_f32(hh[e]), rn, f_w[k2 * 8 + e]);
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          hl[e] = from_f32<T>(rope_one(xl[e], -xh[e], cr[k * 8 + e], sr[k * 8 + e]));
+          hh[e] = from_f32<T>(rope_one(xh[e], xl[e], cr[k2 * 8 + e], sr[k2 * 8 + e]));
+        }
+        *reinterpret_cast<uint4*>(pl) = ul;
+        *reinterpret_cast<uint4*>(ph) = uh;
+      }
+    }
+    tc::fence_async_smem();  // generic writes before the tensor core reads the tile
+    __syncthreads();
+  }
   uint32_t phase = 0;
   float m_run = -INFINITY, l_run = 0.f;
   int pending = nblk > 0 ? 0 : -1;  // K/V block requested and not yet waited for
@@ -801,9 +890,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         const int r = i / (HD / 8), ch = i % (HD / 8);
         const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
         if (rs < p.S)
-          cp_async16(gs + r * GLD + ch * 8,
-                     reinterpret_cast<const T*>(p.gate) + ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD +
-                         ch * 8);
+          cp_async16(gs + r * GLD + ch * 8, reinterpret_cast<const T*>(p.gate) + gate_index(p, b, rs, hq, ch * 8));
       }
       cp_async_commit();
       cp_async_wait<0>();
@@ -957,6 +1044,35 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
     for (int c = 0; c < NS && c < nch; ++c) issue(c);
 
   // Q tile: 16 rows (rows >= R are zero), swizzled like the TMA tiles
+  if (p.fused) {  // S == 1: row r = head kvh G + r, read from the projection output, normed and rotated
+    constexpr int EPL = HD / 32;
+    for (int r = warp; r < 16; r += 4) {
+      float x[EPL];
+      if (r < R) {
+        const T* src = reinterpret_cast<const T*>(p.q) + (long long)b * p.qkv_ld + (long long)(kvh * G + r) * 2 * HD +
+                       lane * EPL;
+        if constexpr (EPL == 8) {
+          load8(src, x);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) x[e] = to_f32(src[e]);
+        }
+        head_norm_rope_warp<T, EPL>(x, p.qnw, p.cos_t + (long long)p.pos * HD, p.sin_t + (long long)p.pos * HD, p.eps,
+                                    lane);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) x[e] = 0.f;
+      }
+      const int ch = lane * EPL / 8;  // this lane's 16-byte chunk (half of it when EPL == 4)
+      uint8_t* dst = sm + L::OFF_Q + (ch >> 3) * 2048 + swz128(r, ch & 7) + (EPL == 4 ? (lane & 1) * 8 : 0);
+      if constexpr (EPL == 8) {
+        store8(reinterpret_cast<T*>(dst), x);
+      } else {
+        T h4[4] = {from_f32<T>(x[0]), from_f32<T>(x[1]), from_f32<T>(x[2]), from_f32<T>(x[3])};
+        *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(h4);
+      }
+    }
+  } else
   for (int i = tid; i < 16 * (HD / 8); i += 128) {
     const int r = i / (HD / 8), c = i % (HD / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
@@ -1003,7 +1119,42 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
 
     // new rows into the landed tiles (and the cache); V rows past the split end zeroed
     bool touched = false;
-    if (p.has_new) {
+    if (p.has_new && p.fused) {  // S == 1: the row at pos, K normed and rotated on the way in
+      if (p.pos >= kw0 && p.pos < min(kw0 + 16, k_end)) {
+        touched = true;
+        constexpr int EPL = HD / 32;
+        const long long src = (long long)b * p.qkv_ld + (long long)kvh * HD + lane * EPL;
+        float x[EPL];
+        const T* ks = reinterpret_cast<const T*>(p.k_new) + src;
+        const T* vs = reinterpret_cast<const T*>(p.v_new) + src;
+        if constexpr (EPL == 8) {
+          load8(ks, x);
+        } else {
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) x[e] = to_f32(ks[e]);
+        }
+        head_norm_rope_warp<T, EPL>(x, p.knw, p.cos_t + (long long)p.pos * HD, p.sin_t + (long long)p.pos * HD,
+                                    p.eps, lane);
+        const int r = p.pos - key0, ch = lane * EPL / 8;
+        const uint32_t so = (ch >> 3) * L::KV_BLK + swz128(r, ch & 7) + (EPL == 4 ? (lane & 1) * 8 : 0);
+        T* kc_row = Kc + (long long)p.pos * HD + lane * EPL;
+        T* vc_row = Vc + (long long)p.pos * HD + lane * EPL;
+        if constexpr (EPL == 8) {
+          store8(reinterpret_cast<T*>(Kt + so), x);
+          store8(kc_row, x);
+          const uint4 vv = *reinterpret_cast<const uint4*>(vs);
+          *reinterpret_cast<uint4*>(Vt + so) = vv;
+          *reinterpret_cast<uint4*>(vc_row) = vv;
+        } else {
+          T h4[4] = {from_f32<T>(x[0]), from_f32<T>(x[1]), from_f32<T>(x[2]), from_f32<T>(x[3])};
+          *reinterpret_cast<uint2*>(Kt + so) = *reinterpret_cast<const uint2*>(h4);
+          *reinterpret_cast<uint2*>(kc_row) = *reinterpret_cast<const uint2*>(h4);
+          const uint2 vv = *reinterpret_cast<const uint2*>(vs);
+          *reinterpret_cast<uint2*>(Vt + so) = vv;
+          *reinterpret_cast<uint2*>(vc_row) = vv;
+        }
+      }
+    } else if (p.has_new) {
       const int j0 = max(kw0, p.pos), j1 = min(min(kw0 + 16, k_end), p.pos + p.S);
       if (j1 > j0) {
         touched = true;
@@ -1177,7 +1328,7 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
       const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
       float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
       if (p.gate) {
-        const uint2 gu = *reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p.gate) + off);
+        const uint2 gu = *reinterpret_cast<const uint2*>(reinterpret_cast<const T*>(p.gate) + gate_index(p, b, s, hq, d));
         const T* gh = reinterpret_cast<const T*>(&gu);
 #pragma unroll
         for (int e = 0; e < 4; ++e) v[e] *= sigmoid_fast(to_f32(gh[e]));
@@ -1304,8 +1455,52 @@ kv_write_rows_kernel(const T* __restrict__ kn, const T* __restrict__ vn, T* __re
   reinterpret_cast<uint4*>(vc + dst)[0] = reinterpret_cast<const uint4*>(vn + row * HD + v * 8)[0];
 }
 
+// Fused form: a warp per new row; K rows normed (k_norm) and rotated at their position, V rows moved;
+// both read in place from the q/k/v projection output.
+template <typename T, int HD>
+__global__ void __launch_bounds__(256)
+kv_write_rows_fused_kernel(KvParams p) {
+  constexpr int EPL = HD / 32;
+  const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);  // (b, h, s), s fastest
+  const int lane = threadIdx.x & 31;
+  if (row >= (long long)p.B * p.Hkv * p.S) return;
+  const int s = (int)(row % p.S);
+  const long long bh = row / p.S;
+  const int h = (int)(bh % p.Hkv), b = (int)(bh / p.Hkv);
+  const long long src = ((long long)b * p.S + s) * p.qkv_ld + (long long)h * HD + lane * EPL;
+  const long long dst = (long long)b * p.bs + (long long)h * p.hs + (long long)(p.pos + s) * HD + lane * EPL;
+  float x[EPL];
+  const T* kn = reinterpret_cast<const T*>(p.k_new) + src;
+  if constexpr (EPL == 8) {
+    load8(kn, x);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) x[e] = to_f32(kn[e]);
+  }
+  head_norm_rope_warp<T, EPL>(x, p.knw, p.cos_t + (long long)(p.pos + s) * HD, p.sin_t + (long long)(p.pos + s) * HD,
+                              p.eps, lane);
+  T* kd = reinterpret_cast<T*>(p.kc) + dst;
+  T* vd = reinterpret_cast<T*>(p.vc) + dst;
+  const T* vs = reinterpret_cast<const T*>(p.v_new) + src;
+  if constexpr (EPL == 8) {
+    store8(kd, x);
+    *reinterpret_cast<uint4*>(vd) = *reinterpret_cast<const uint4*>(vs);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      kd[e] = from_f32<T>(x[e]);
+      vd[e] = vs[e];
+    }
+  }
+}
+
 template <typename T, int HD>
 int launch_kv_write_rows(const KvParams& p, cudaStream_t st) {
+  if (p.fused) {
+    const long long rows = (long long)p.B * p.Hkv * p.S;
+    kv_write_rows_fused_kernel<T, HD><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(p);
+    return launch_status("kv_attention_write_rows");
+  }
   const long long n_vec = (long long)p.B * p.Hkv * p.S * (HD / 8);
   kv_write_rows_kernel<T, HD><<<(unsigned)((n_vec + 255) / 256), 256, 0, st>>>(
       reinterpret_cast<const T*>(p.k_new), reinterpret_cast<const T*>(p.v_new), reinterpret_cast<T*>(p.kc),
@@ -1339,10 +1534,18 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
   }
   KvTcMaps maps;
   {
-    const cuuint64_t dq[3] = {(cuuint64_t)HD, (cuuint64_t)p.S, (cuuint64_t)p.B * p.Hq};
-    const cuuint64_t sq[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.S * HD * 2};
-    const cuuint32_t bq[3] = {64, 16, 8};
-    int rc = kv_encode(&maps.q, p.q, 3, dq, sq, bq);
+    int rc;
+    if (p.fused) {  // the projection output: {column, token (qkv_ld), head (2 HD), sequence (S qkv_ld)}
+      const cuuint64_t dq[4] = {(cuuint64_t)HD, (cuuint64_t)p.S, (cuuint64_t)p.Hq, (cuuint64_t)p.B};
+      const cuuint64_t sq[3] = {(cuuint64_t)p.qkv_ld * 2, (cuuint64_t)HD * 4, (cuuint64_t)p.S * p.qkv_ld * 2};
+      const cuuint32_t bq[4] = {64, 16, 8, 1};
+      rc = kv_encode(&maps.q, p.q, 4, dq, sq, bq);
+    } else {
+      const cuuint64_t dq[3] = {(cuuint64_t)HD, (cuuint64_t)p.S, (cuuint64_t)p.B * p.Hq};
+      const cuuint64_t sq[2] = {(cuuint64_t)HD * 2, (cuuint64_t)p.S * HD * 2};
+      const cuuint32_t bq[3] = {64, 16, 8};
+      rc = kv_encode(&maps.q, p.q, 3, dq, sq, bq);
+    }
     if (!rc) rc = kv_cache_maps(maps, p, HD);
     if (rc) return rc;
   }
@@ -1394,13 +1597,24 @@ extern "C" size_t anemll_kv_attention_workspace_size(int B, int S, int H_q, int 
   return workspace_bytes_for(pl.max_splits, B, S, H_q, H_kv, head_dim);
 }
 
-extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, const void* gate,
-                                   void* k_cache, void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
-                                   const void* mask, int mask_dtype, int64_t mask_row_stride,
-                                   void* out, int dtype,
-                                   int B, int S, int H_q, int H_kv, int head_dim, int ctx,
-                                   int current_pos, int window, int window_chunk_aligned,
-                                   void* workspace, size_t workspace_bytes, void* stream) {
+namespace anemll {
+namespace {
+
+// the fused q/k head norm + RoPE inputs of anemll_kv_attention_qkv
+struct FusedQkv {
+  long long ld;
+  const float* qn;
+  const float* kn;
+  const float* cos_t;
+  const float* sin_t;
+  float eps;
+};
+
+int kv_attention_run(const void* q, const void* k_new, const void* v_new, const void* gate, void* k_cache,
+                     void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride, const void* mask,
+                     int mask_dtype, int64_t mask_row_stride, void* out, int dtype, int B, int S, int H_q, int H_kv,
+                     int head_dim, int ctx, int current_pos, int window, int window_chunk_aligned, void* workspace,
+                     size_t workspace_bytes, void* stream, const FusedQkv* fz) {
   ANEMLL_REQUIRE(q && k_cache && v_cache && out, ANEMLL_EINVAL, "kv_attention: null pointer");
   ANEMLL_REQUIRE((k_new == nullptr) == (v_new == nullptr), ANEMLL_EINVAL,
                  "kv_attention: k_new and v_new must both be given or both be NULL");
@@ -1436,9 +1650,29 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
   p.ws_o = reinterpret_cast<float*>(workspace);
   p.ws_ml = p.ws_o ? p.ws_o + (size_t)B * H_kv * pl.n_splits * R * head_dim : nullptr;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)head_dim);
+  p.gate_ts = (long long)H_q * head_dim;
+  p.gate_hs = head_dim;
+  p.fused = 0;
+  p.qkv_ld = 0;
+  p.qnw = p.knw = p.cos_t = p.sin_t = nullptr;
+  p.eps = 0.f;
   cudaStream_t st = (cudaStream_t)stream;
   const bool use_tc = tc_eligible(S, H_q, H_kv, head_dim, cache_batch_stride, cache_head_stride, out, gate);
   const bool use_dec = !use_tc && dec_eligible(S, H_q, H_kv, cache_batch_stride, cache_head_stride, out, gate);
+  if (fz) {
+    ANEMLL_REQUIRE(use_tc || (use_dec && S == 1 && head_dim != 64), ANEMLL_EUNSUPPORTED,
+                   "kv_attention_qkv: fused head norm needs a tcgen05 prefill chunk (8 query heads per kv head, "
+                   "head_dim 128/256, 16+ tokens) or a one-token decode step");
+    p.fused = 1;
+    p.qkv_ld = fz->ld;
+    p.qnw = fz->qn;
+    p.knw = fz->kn;
+    p.cos_t = fz->cos_t;
+    p.sin_t = fz->sin_t;
+    p.eps = fz->eps;
+    p.gate_ts = fz->ld;  // gate columns of head h follow its query columns
+    p.gate_hs = 2LL * head_dim;
+  }
   return ANEMLL_DISPATCH_HALF(dtype, T, [&] {
     switch (head_dim) {
       case 64: return use_dec ? launch_kv_dec<T, 64>(p, pl, st) : launch_kv<T, 64>(p, pl, st);
@@ -1452,6 +1686,47 @@ extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void*
                          : launch_kv<T, 256>(p, pl, st);
     }
   });
+}
+
+}  // namespace
+}  // namespace anemll
+
+extern "C" int anemll_kv_attention(const void* q, const void* k_new, const void* v_new, const void* gate,
+                                   void* k_cache, void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                                   const void* mask, int mask_dtype, int64_t mask_row_stride,
+                                   void* out, int dtype,
+                                   int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                                   int current_pos, int window, int window_chunk_aligned,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  return kv_attention_run(q, k_new, v_new, gate, k_cache, v_cache, cache_batch_stride, cache_head_stride, mask,
+                          mask_dtype, mask_row_stride, out, dtype, B, S, H_q, H_kv, head_dim, ctx, current_pos, window,
+                          window_chunk_aligned, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int anemll_kv_attention_qkv(const void* qkv, int64_t qkv_row_stride, const float* q_norm,
+                                       const float* k_norm, const float* cos_table, const float* sin_table, float eps,
+                                       void* k_cache, void* v_cache, int64_t cache_batch_stride,
+                                       int64_t cache_head_stride, void* out, int dtype, int B, int S, int H_q,
+                                       int H_kv, int head_dim, int ctx, int current_pos, int window,
+                                       int window_chunk_aligned, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  ANEMLL_REQUIRE(qkv && q_norm && k_norm && cos_table && sin_table, ANEMLL_EINVAL, "kv_attention_qkv: null pointer");
+  ANEMLL_REQUIRE(aligned(q_norm, 16) && aligned(cos_table, 16) && aligned(sin_table, 16), ANEMLL_EALIGN,
+                 "kv_attention_qkv: q_norm and the cos/sin tables must be 16-byte aligned");
+  ANEMLL_REQUIRE(dtype == ANEMLL_F16 || dtype == ANEMLL_BF16, ANEMLL_EUNSUPPORTED, "kv_attention_qkv: fp16 or bf16");
+  ANEMLL_REQUIRE(H_q > 0 && H_kv > 0 && head_dim > 0 &&
+                     qkv_row_stride >= 2LL * H_q * head_dim + 2LL * H_kv * head_dim && qkv_row_stride % 8 == 0,
+                 ANEMLL_EINVAL, "kv_attention_qkv: the q/k/v row stride is shorter than a row or not 16-byte units");
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(qkv);
+  const long long es = 2;
+  const void* q = base;
+  const void* gate = base + (long long)head_dim * es;
+  const void* k_new = base + 2LL * H_q * head_dim * es;
+  const void* v_new = base + (2LL * H_q + H_kv) * head_dim * es;
+  const FusedQkv fz{qkv_row_stride, q_norm, k_norm, cos_table, sin_table, eps};
+  return kv_attention_run(q, k_new, v_new, gate, k_cache, v_cache, cache_batch_stride, cache_head_stride, nullptr, 0,
+                          0, out, dtype, B, S, H_q, H_kv, head_dim, ctx, current_pos, window, window_chunk_aligned,
+                          workspace, workspace_bytes, stream, &fz);
 }
 
 // ---------------------------------------------------------------------------

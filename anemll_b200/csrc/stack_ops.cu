@@ -169,9 +169,8 @@ qk_norm_rope_kernel(const T* __restrict__ qg, long long qg_ld, const T* __restri
   const int b = (int)(tok / T_len), t = (int)(tok % T_len);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nrows = 2 * Hq + 2 * Hkv;
-  const float* cr = cos_t + (long long)(pos + t) * HD + lane * EPL;
-  const float* sr = sin_t + (long long)(pos + t) * HD + lane * EPL;
-  const bool lower = lane < 16;  // first half of the head: rotate_half gives -x[i + HD/2]
+  const float* cr = cos_t + (long long)(pos + t) * HD;
+  const float* sr = sin_t + (long long)(pos + t) * HD;
   for (int r = warp; r < nrows; r += NT / 32) {
     const T* src;
     T* dst;
@@ -201,25 +200,7 @@ qk_norm_rope_kernel(const T* __restrict__ qg, long long qg_ld, const T* __restri
 #pragma unroll
       for (int e = 0; e < EPL; ++e) x[e] = to_f32(src[lane * EPL + e]);
     }
-    if (nw) {
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) ss += x[e] * x[e];
-      ss = warp_sum(ss);
-      const float rn = rsqrtf(ss / (float)HD + eps);
-#pragma unroll
-      for (int e = 0; e < EPL; ++e)  // the normed head, rounded to the storage type
-        x[e] = to_f32(from_f32<T>(__fmul_rn(__fmul_rn(x[e], rn), nw[lane * EPL + e])));
-      float y[EPL];
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const float partner = __shfl_xor_sync(0xffffffffu, x[e], 16);
-        const float rot = lower ? -partner : partner;
-        y[e] = __fadd_rn(__fmul_rn(x[e], cr[e]), __fmul_rn(rot, sr[e]));
-      }
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) x[e] = y[e];
-    }
+    if (nw) head_norm_rope_warp<T, EPL>(x, nw, cr, sr, eps, lane);
     if constexpr (EPL == 8) {
       store8(dst + lane * 8, x);
     } else {

@@ -7,13 +7,13 @@ followed by a SwiGLU MLP, both pre-normed (RMSNorm) with residuals.
 * Gated-DeltaNet layers: :class:`anemll_b200.gdn.GatedDeltaNet` (the library's prologue, chunked
   prefill / recurrent decode and gated RMSNorm kernels between torch projections).
 * Attention layers: the Qwen3.5 gated full attention in the reference's shape (H_q 16, H_kv 2,
-  head_dim 256): q/k/v projections (q_proj also yields the sigmoid gate), per-head RMSNorm of q and
-  k (``QwenHeadNorm``, ``anemll/models/qwen_model.py:143-184``), rotary embedding
-  (``apply_rotary_pos_emb``, 186-261), then :func:`anemll_b200.attention.kv_attention` with the cache
-  write fused in and the gate applied in its epilogue, then o_proj.
-* Projections and the LM head: ``dense.linear`` (the library's weight-streaming GEMM at decode, torch's
-  GEMM for the prefill's long inputs); norms, RoPE and the SwiGLU: the fused kernels of
-  ``stack_ops.cu``.
+  head_dim 256): one fused q/k/v projection (q_proj also yields the sigmoid gate), then
+  :func:`anemll_b200.attention.kv_attention_qkv`, which applies the per-head RMSNorm of q and k
+  (``QwenHeadNorm``, ``anemll/models/qwen_model.py:143-184``) and the rotary embedding
+  (``apply_rotary_pos_emb``, 186-261) inside the attention call, writes the new cache rows and applies
+  the gate in its epilogue; then o_proj.
+* Projections and the LM head: ``dense.linear`` (torch's GEMM for now); norms and the SwiGLU: the
+  one-pass kernels of ``stack_ops.cu``.
 
 Caches and states are per sequence: KV caches ``[B, H_kv, ctx, hd]`` per attention layer, conv and
 recurrent states per GDN layer.  Weights are random N(0, 0.02) (no checkpoints offline).
@@ -95,7 +95,8 @@ def rope_tables(dim, n_pos, theta, device):
 
 class GatedAttention(nn.Module):
     """Gated full attention.  q_proj, k_proj and v_proj are views of one fused [q|k|v] weight, so the
-    projections are one GEMM whose output feeds ``anemll_qk_norm_rope`` through row strides."""
+    projections are one GEMM whose output the attention call reads in place (head norm and RoPE
+    fused in), or ``anemll_qk_norm_rope`` for shapes the fused call does not take."""
 
     def __init__(self, cfg: StackConfig, device, dtype):
         super().__init__()
@@ -115,29 +116,40 @@ class GatedAttention(nn.Module):
         self.k_norm = nn.Parameter(torch.ones(hd, device=device))
 
     def project(self, x, cos, sin, pos):
-        """q [B, H_q, T, hd], k/v [B, H_kv, T, hd] (normed, rotated), gate [B, T, H_q*hd]."""
-        B, T, _ = x.shape
+        """q [B, H_q, T, hd], k/v [B, H_kv, T, hd] (normed, rotated), gate [B, T, H_q*hd], from one fused
+        q/k/v GEMM and ``anemll_qk_norm_rope`` (the unfused prologue)."""
+        return self._prologue(dense.linear(x, self.w_qkv), cos, sin, pos)
+
+    def _prologue(self, qkv, cos, sin, pos):
+        B, T, ld = qkv.shape
         c = self.cfg
-        qkv = dense.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
-        ld = qkv.shape[-1]
-        q = torch.empty(B, c.H_q, T, c.head_dim, dtype=x.dtype, device=x.device)
-        k = torch.empty(B, c.H_kv, T, c.head_dim, dtype=x.dtype, device=x.device)
+        q = torch.empty(B, c.H_q, T, c.head_dim, dtype=qkv.dtype, device=qkv.device)
+        k = torch.empty(B, c.H_kv, T, c.head_dim, dtype=qkv.dtype, device=qkv.device)
         v = torch.empty_like(k)
-        gate = torch.empty(B, T, c.H_q * c.head_dim, dtype=x.dtype, device=x.device)
+        gate = torch.empty(B, T, c.H_q * c.head_dim, dtype=qkv.dtype, device=qkv.device)
         base = qkv.data_ptr()
         es = qkv.element_size()
         rc = _lib.load().anemll_qk_norm_rope(
             base, ld, base + self.n_q * es, ld, base + (self.n_q + self.n_kv) * es, ld, _lib.ptr(self.q_norm),
             _lib.ptr(self.k_norm), _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(gate),
-            _lib.dtype_code(x.dtype), B, T, c.H_q, c.H_kv, c.head_dim, int(pos), float(c.eps),
-            _lib.stream_ptr(x.device))
+            _lib.dtype_code(qkv.dtype), B, T, c.H_q, c.H_kv, c.head_dim, int(pos), float(c.eps),
+            _lib.stream_ptr(qkv.device))
         _lib.check(rc, "anemll_qk_norm_rope")
         return q, k, v, gate
 
-    def forward(self, x, k_cache, v_cache, pos, cos, sin):
-        """``cos``/``sin``: the whole [ctx, hd] tables; this call's rows start at ``pos``."""
-        q, k, v, gate = self.project(x, cos, sin, pos)
-        o = attention.kv_attention(q, k_cache, v_cache, pos, k_new=k, v_new=v, gate=gate)
+    def forward(self, x, k_cache, v_cache, pos, cos, sin, fused=True):
+        """``cos``/``sin``: the whole [ctx, hd] tables; this call's rows start at ``pos``.  ``fused``: the
+        head norm and RoPE run inside the attention call (``anemll_kv_attention_qkv``) where it takes
+        the shape, else through the separate prologue kernel."""
+        c = self.cfg
+        qkv = dense.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
+        o = None
+        if fused:
+            o = attention.kv_attention_qkv(qkv, self.q_norm, self.k_norm, cos, sin, c.eps, k_cache, v_cache, pos,
+                                           c.H_q, c.H_kv, c.head_dim)
+        if o is None:
+            q, k, v, gate = self._prologue(qkv, cos, sin, pos)
+            o = attention.kv_attention(q, k_cache, v_cache, pos, k_new=k, v_new=v, gate=gate)
         return dense.linear(o, self.o_proj.weight)
 
 

@@ -228,6 +228,26 @@ int anemll_kv_rotate_append(void* cache, const void* new_rows, int dtype, int64_
 int anemll_kv_state_transition(const void* src, int src_dtype, void* dst, int dst_dtype, int64_t n_slabs,
                                int src_len, int dst_len, int d, int current_position, float pad_value, void* stream);
 
+/*
+ * anemll_kv_attention with the attention layer's prologue fused in: qkv is one q/k/v projection
+ * output, per token H_q x [query | gate] head_dim each, then H_kv x k, then H_kv x v (row stride
+ * qkv_row_stride elements, 16-byte units).  Query and key heads get their RMSNorm (q_norm / k_norm
+ * fp32 [head_dim], eps; QwenHeadNorm, qwen_model.py:143-184) and rotary embedding at their
+ * positions (fp32 cos/sin tables [>= current_pos + S][head_dim]; apply_rotary_pos_emb, 186-261)
+ * inside the attention call: the tcgen05 prefill kernel reads its query tile from qkv by TMA and
+ * normalises it in shared memory, the new K rows are normed on their way into the cache, the decode
+ * kernel normalises its query and key rows as it loads them, and the gate is read in place.  The
+ * arithmetic is that of anemll_qk_norm_rope, bit for bit.  Shapes: 8 query heads per kv head with
+ * head_dim 128 or 256 and S >= 16 (prefill chunks), or S == 1 (decode); anything else returns
+ * ANEMLL_EUNSUPPORTED (use anemll_qk_norm_rope + anemll_kv_attention).  No explicit mask.
+ */
+int anemll_kv_attention_qkv(const void* qkv, int64_t qkv_row_stride, const float* q_norm, const float* k_norm,
+                            const float* cos_table, const float* sin_table, float eps,
+                            void* k_cache, void* v_cache, int64_t cache_batch_stride, int64_t cache_head_stride,
+                            void* out, int dtype, int B, int S, int H_q, int H_kv, int head_dim, int ctx,
+                            int current_pos, int window, int window_chunk_aligned,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- decoder-stack epilogues (the hybrid stack's glue between its GEMMs) ---- */
 
 /*

@@ -77,3 +77,49 @@ def test_stack_op_errors():
         rms_norm(torch.zeros(2, 12, device=DEV, dtype=torch.bfloat16), torch.ones(12, device=DEV), 1e-6)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         rms_norm(torch.zeros(2, 16), torch.ones(16), 1e-6)
+
+
+@pytest.mark.parametrize("S,pos,B", [(64, 0, 2), (32, 100, 2), (1, 300, 3), (1, 0, 1), (256, 512, 1)])
+def test_fused_attention_prologue_is_bit_exact(S, pos, B):
+    """anemll_kv_attention_qkv (head norm + RoPE inside the attention call) gives the bits of the
+    separate prologue kernel followed by anemll_kv_attention: output and cache."""
+    from anemll_b200 import attention
+    from anemll_b200.stack import rope_tables
+    g = torch.Generator().manual_seed(S * 7 + pos)
+    Hq, Hkv, hd, ctx, eps = 16, 2, 256, 1024, 1e-6
+    n_q, n_kv = Hq * 2 * hd, Hkv * hd
+    wide = torch.randn(B, S, n_q + 2 * n_kv + 16, generator=g).bfloat16().to(DEV)  # rows spaced by 16 extra
+    qkv = wide[..., :n_q + 2 * n_kv]
+    qw = (1 + 0.1 * torch.randn(hd, generator=g)).to(DEV)
+    kw = (1 + 0.1 * torch.randn(hd, generator=g)).to(DEV)
+    cos, sin = (t.to(DEV) for t in rope_tables(hd, ctx, 1e7, "cpu"))
+    cache = torch.randn(2, B, Hkv, ctx, hd, generator=g).bfloat16().to(DEV)
+    ca, cb = cache.clone(), cache.clone()
+    out = attention.kv_attention_qkv(qkv, qw, kw, cos, sin, eps, ca[0], ca[1], pos, Hq, Hkv, hd)
+    assert out is not None
+    q = torch.empty(B, Hq, S, hd, dtype=torch.bfloat16, device=DEV)
+    k = torch.empty(B, Hkv, S, hd, dtype=torch.bfloat16, device=DEV)
+    v = torch.empty_like(k)
+    gate = torch.empty(B, S, Hq * hd, dtype=torch.bfloat16, device=DEV)
+    from anemll_b200 import _lib
+    base, ld = qkv.data_ptr(), qkv.stride(1) if S > 1 else qkv.stride(0)
+    rc = _lib.load().anemll_qk_norm_rope(base, ld, base + n_q * 2, ld, base + (n_q + n_kv) * 2, ld, _lib.ptr(qw),
+                                         _lib.ptr(kw), _lib.ptr(cos), _lib.ptr(sin), _lib.ptr(q), _lib.ptr(k),
+                                         _lib.ptr(v), _lib.ptr(gate), _lib.BF16, B, S, Hq, Hkv, hd, pos, eps,
+                                         _lib.stream_ptr(DEV))
+    _lib.check(rc, "anemll_qk_norm_rope")
+    ref = attention.kv_attention(q, cb[0], cb[1], pos, k_new=k, v_new=v, gate=gate)
+    assert torch.equal(out, ref)
+    assert torch.equal(ca, cb)
+    assert attention.kv_device_error() == 0
+
+
+def test_fused_attention_prologue_declines_other_shapes():
+    from anemll_b200 import attention
+    from anemll_b200.stack import rope_tables
+    Hq, Hkv, hd, ctx = 16, 2, 256, 256
+    qkv = torch.zeros(1, 4, Hq * 2 * hd + 2 * Hkv * hd, dtype=torch.bfloat16, device=DEV)  # 4 tokens: neither path
+    cos, sin = (t.to(DEV) for t in rope_tables(hd, ctx, 1e7, "cpu"))
+    cache = torch.zeros(2, 1, Hkv, ctx, hd, dtype=torch.bfloat16, device=DEV)
+    w = torch.ones(hd, device=DEV)
+    assert attention.kv_attention_qkv(qkv, w, w, cos, sin, 1e-6, cache[0], cache[1], 0, Hq, Hkv, hd) is None
