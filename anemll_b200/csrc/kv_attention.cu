@@ -733,15 +733,32 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       const T* vn = reinterpret_cast<const T*>(p.v_new) + (long long)bh * p.S * HD;
       T* Kc = reinterpret_cast<T*>(p.kc) + (long long)b * p.bs + (long long)kvh * p.hs;
       T* Vc = reinterpret_cast<T*>(p.vc) + (long long)b * p.bs + (long long)kvh * p.hs;
-      for (int i = tid; i < (j1 - j0) * (HD / 8); i += 128) {
-        const int jj = j0 + i / (HD / 8), ch = i % (HD / 8), r = jj - key0;
-        const uint4 kv = *reinterpret_cast<const uint4*>(kn + (long long)(jj - p.pos) * HD + ch * 8);
-        const uint4 vv = *reinterpret_cast<const uint4*>(vn + (long long)(jj - p.pos) * HD + ch * 8);
-        *reinterpret_cast<uint4*>(sm + OFF_K + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = kv;
-        *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = vv;
-        if (tile == (jj - p.pos) >> 4) {
-          *reinterpret_cast<uint4*>(Kc + (long long)jj * HD + ch * 8) = kv;
-          *reinterpret_cast<uint4*>(Vc + (long long)jj * HD + ch * 8) = vv;
+      // four vectors per thread in flight at a time (loads first, then stores)
+      constexpr int PU = 4;
+      const int n_items = (j1 - j0) * (HD / 8);
+      for (int i0 = tid; i0 < n_items; i0 += PU * 128) {
+        uint4 kv[PU], vv[PU];
+#pragma unroll
+        for (int u = 0; u < PU; ++u) {
+          const int i = i0 + u * 128;
+          if (i < n_items) {
+            const int jj = j0 + i / (HD / 8), ch = i % (HD / 8);
+            kv[u] = *reinterpret_cast<const uint4*>(kn + (long long)(jj - p.pos) * HD + ch * 8);
+            vv[u] = *reinterpret_cast<const uint4*>(vn + (long long)(jj - p.pos) * HD + ch * 8);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < PU; ++u) {
+          const int i = i0 + u * 128;
+          if (i < n_items) {
+            const int jj = j0 + i / (HD / 8), ch = i % (HD / 8), r = jj - key0;
+            *reinterpret_cast<uint4*>(sm + OFF_K + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = kv[u];
+            *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = vv[u];
+            if (tile == (jj - p.pos) >> 4) {
+              *reinterpret_cast<uint4*>(Kc + (long long)jj * HD + ch * 8) = kv[u];
+              *reinterpret_cast<uint4*>(Vc + (long long)jj * HD + ch * 8) = vv[u];
+            }
+          }
         }
       }
       tc::fence_async_smem();  // generic writes before the tensor core reads the tiles
@@ -1437,7 +1454,7 @@ int launch_kv_dec(KvParams& p, const Plan& pl0, cudaStream_t st) {
 // New rows k_new / v_new [B][H_kv][S][HD] -> cache rows [pos, pos + S), 16-byte vectors.  The tcgen05
 // prefill path runs this first for chunks of TC_PREWRITE_MIN tokens or more: its attention kernel
 // then reads every row, new or old, with TMA and no block has rows to patch.
-constexpr int TC_PREWRITE_MIN = 16;
+constexpr int TC_PREWRITE_MIN = 128;
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(256)
@@ -1566,7 +1583,7 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
 // kernel, launched dependent on it, waits for it before its first load), short ones patch them in.
 template <typename T, int HD>
 int launch_kv_tc_rows(KvParams& p, const Plan& pl, cudaStream_t st) {
-  if (!p.has_new || p.S < TC_PREWRITE_MIN) return launch_kv_tc<T, HD>(p, pl, st);
+  if (!p.has_new || (!p.fused && p.S < TC_PREWRITE_MIN)) return launch_kv_tc<T, HD>(p, pl, st);
   int rc = launch_kv_write_rows<T, HD>(p, st);
   if (rc) return rc;
   KvParams q = p;
