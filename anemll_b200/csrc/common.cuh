@@ -78,37 +78,6 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
-// The opening of a small kernel launched by launch_pdl: let the next kernel of the stream launch
-// now (it waits for this one in turn), then wait for the previous kernel before touching memory.
-__device__ __forceinline__ void pdl_enter() {
-  griddep_launch_dependents();
-  griddep_wait();
-}
-
-// Launch with programmatic stream serialisation, so that the kernel's launch overlaps the tail of the
-// previous kernel in the stream.  Every kernel launched this way calls griddep_wait() before its first
-// global-memory access.
-template <typename... KArgs, typename... Args>
-int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-               Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    set_error("%s: launch failed, CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
-    return (int)e;
-  }
-  return launch_status(what);
-}
 
 __device__ __forceinline__ float softplus(float x) {
   // log(1 + e^x), evaluated without overflow (same threshold behaviour as torch's softplus, beta=1, threshold=20)

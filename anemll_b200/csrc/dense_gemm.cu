@@ -282,25 +282,6 @@ int launch_gemm(const void* x, long long ldx, const void* w, long long ldw, void
   return launch_status("gemm");
 }
 
-// ------------------------------------------------------------- L2 prefetch --
-// The decode steps' projections read every weight once per step, and a GEMM of batch 128 spends a
-// few microseconds of its ~10 in start-up before its weight stream reaches full rate.  This kernel,
-// launched just before the small kernel that precedes a projection, requests that projection's
-// weight bytes [p, p + bytes) into L2 with bulk prefetches (cp.async.bulk.prefetch.L2: no
-// destination and no completion), one chunk per thread over every SM, so that the HBM stream
-// starts under the small kernel.  It lets the next kernel of the stream launch at once, then waits
-// for the previous kernel to finish (so that its requests do not queue behind that kernel's own
-// stream) before it issues them.
-__global__ void __launch_bounds__(64) l2_prefetch_kernel(const char* p, long long bytes, long long chunk) {
-  griddep_launch_dependents();
-  griddep_wait();
-  const long long off = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * chunk;
-  if (off < bytes) {
-    const long long n = bytes - off < chunk ? bytes - off : chunk;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p + off), "r"((unsigned)n) : "memory");
-  }
-}
-
 }  // namespace
 }  // namespace anemll
 
@@ -327,26 +308,4 @@ extern "C" int anemll_gemm_error(int reset) {
     cudaMemcpyToSymbol(g_gemm_error, &z, sizeof(int));
   }
   return h;
-}
-
-extern "C" int anemll_l2_prefetch(const void* ptr, int64_t bytes, void* stream) {
-  ANEMLL_REQUIRE(bytes >= 0 && (bytes == 0 || ptr), ANEMLL_EINVAL, "l2_prefetch: bad range");
-  // the whole 16-byte units inside the range: never a byte outside it
-  const uintptr_t a = ((uintptr_t)ptr + 15) & ~(uintptr_t)15, e = ((uintptr_t)ptr + (uintptr_t)bytes) & ~(uintptr_t)15;
-  if (bytes == 0 || e <= a) return ANEMLL_OK;
-  const long long n = (long long)(e - a);
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-  }
-  const long long per = (n + (long long)sms * 64 - 1) / ((long long)sms * 64);  // bytes per thread, 64 per SM
-  long long chunk = ((per + 15) / 16) * 16;
-  if (chunk < 2048) chunk = 2048;
-  if (chunk > (1ll << 30)) chunk = 1ll << 30;
-  const long long threads = (n + chunk - 1) / chunk;
-  const unsigned grid = (unsigned)((threads + 63) / 64);
-  return launch_pdl("l2_prefetch", l2_prefetch_kernel, dim3(grid), dim3(64), 0, (cudaStream_t)stream,
-                    (const char*)a, n, chunk);
 }

@@ -17,7 +17,6 @@ template <typename TX, typename TZ, typename TO>
 __global__ void __launch_bounds__(256)
 gated_rmsnorm_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const float* __restrict__ w,
                      TO* __restrict__ out, int64_t rows, int d, float eps, int64_t zh, int64_t z_ld) {
-  pdl_enter();
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -41,7 +40,6 @@ template <typename TX, typename TZ, typename TO, int NC>
 __global__ void __launch_bounds__(256)
 gated_rmsnorm_vec_kernel(const TX* __restrict__ x, const TZ* __restrict__ z, const float* __restrict__ w,
                          TO* __restrict__ out, int64_t rows, int d, float eps, int64_t zh, int64_t z_ld) {
-  pdl_enter();
   const int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
   const int l = threadIdx.x & 15;
   const unsigned hmask = 0xffffu << (threadIdx.x & 16);
@@ -104,13 +102,18 @@ extern "C" int anemll_gated_rmsnorm(const void* x, int x_dtype, const void* z, i
       return ANEMLL_DISPATCH_DTYPE(out_dtype, TO, [&] {
         const bool vec = d % 8 == 0 && d <= 512 && aligned(x, 16) && aligned(z, 16) && aligned(out, 16) && z_vec_ok;
         const unsigned vblocks = (unsigned)((rows + 15) / 16);
-        auto go = [&](auto kern, unsigned grid) {
-          return launch_pdl("gated_rmsnorm", kern, dim3(grid), dim3(256), 0, st, (const TX*)x, (const TZ*)z, weight,
-                            (TO*)out, rows, d, eps, z_heads, z_row_stride);
-        };
-        if (vec && d <= 128) return go(gated_rmsnorm_vec_kernel<TX, TZ, TO, 1>, vblocks);
-        if (vec) return go(gated_rmsnorm_vec_kernel<TX, TZ, TO, 4>, vblocks);
-        return go(gated_rmsnorm_kernel<TX, TZ, TO>, blocks);
+        if (vec && d <= 128)
+          gated_rmsnorm_vec_kernel<TX, TZ, TO, 1><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
+                                                                          (TO*)out, rows, d, eps, z_heads,
+                                                                          z_row_stride);
+        else if (vec)
+          gated_rmsnorm_vec_kernel<TX, TZ, TO, 4><<<vblocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight,
+                                                                          (TO*)out, rows, d, eps, z_heads,
+                                                                          z_row_stride);
+        else
+          gated_rmsnorm_kernel<TX, TZ, TO><<<blocks, 256, 0, st>>>((const TX*)x, (const TZ*)z, weight, (TO*)out,
+                                                                   rows, d, eps, z_heads, z_row_stride);
+        return launch_status("gated_rmsnorm");
       });
     });
   });

@@ -83,7 +83,6 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
                      const float* __restrict__ dt_bias, TOut* __restrict__ qo, TOut* __restrict__ ko,
                      TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao, int B, int T, int Hqk,
                      int Hv, int K, int use_state, int n_tiles, int conv_ctas, long long x_ld, long long ab_ld) {
-  pdl_enter();
   if ((int)blockIdx.x >= conv_ctas) {
     const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
     if (idx < (long long)B * T * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, ab_ld, A_log, dt_bias, go, betao);
@@ -211,7 +210,6 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
                       const float* __restrict__ A_log, const float* __restrict__ dt_bias, TOut* __restrict__ qo,
                       TOut* __restrict__ ko, TOut* __restrict__ vo, float* __restrict__ go, float* __restrict__ betao,
                       int B, int Hqk, int Hv, int use_state, int conv_ctas, long long x_ld, long long ab_ld) {
-  pdl_enter();
   if ((int)blockIdx.x >= conv_ctas) {
     const long long idx = (long long)(blockIdx.x - conv_ctas) * HDIM + threadIdx.x;
     if (idx < (long long)B * TS * Hv) gate_elem(idx, Hv, a, bgate, ab_dt, ab_ld, A_log, dt_bias, go, betao);
@@ -288,15 +286,14 @@ int launch_prologue(const void* x, const float* w, void* cs, const void* a, cons
     ANEMLL_REQUIRE(conv_ctas + gate_ctas < (1LL << 31), ANEMLL_EINVAL, "gdn_prologue: problem too large");
     const unsigned grid = (unsigned)(conv_ctas + gate_ctas);
     auto go_short = [&](auto kern) {
-      return launch_pdl("gdn_prologue", kern, dim3(grid), dim3(HDIM), 0, st, (const TIn*)x, w, (TIn*)cs, a, bg, ab_dt,
-                        A_log, dt_bias, (TOut*)qo, (TOut*)ko, (TOut*)vo, go, bo, B, Hqk, Hv, use_state,
-                        (int)conv_ctas, x_ld, ab_ld);
+      kern<<<grid, HDIM, 0, st>>>((const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko,
+                                  (TOut*)vo, go, bo, B, Hqk, Hv, use_state, (int)conv_ctas, x_ld, ab_ld);
     };
     switch (T) {
-      case 1: return go_short(prologue_short_kernel<TIn, TOut, 1>);
-      case 2: return go_short(prologue_short_kernel<TIn, TOut, 2>);
-      case 3: return go_short(prologue_short_kernel<TIn, TOut, 3>);
-      default: return go_short(prologue_short_kernel<TIn, TOut, 4>);
+      case 1: go_short(prologue_short_kernel<TIn, TOut, 1>); break;
+      case 2: go_short(prologue_short_kernel<TIn, TOut, 2>); break;
+      case 3: go_short(prologue_short_kernel<TIn, TOut, 3>); break;
+      default: go_short(prologue_short_kernel<TIn, TOut, 4>); break;
     }
   } else {
     const int n_tiles = (T + TT - 1) / TT;
@@ -305,13 +302,14 @@ int launch_prologue(const void* x, const float* w, void* cs, const void* a, cons
     const size_t smem = (size_t)(TT + MAXK - 1) * HDIM * sizeof(TIn) + (size_t)TT * HDIM * sizeof(float);
     auto go_tile = [&](auto kern) {
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      return launch_pdl("gdn_prologue", kern, dim3((unsigned)(conv_ctas + gate_ctas)), dim3(HDIM), smem, st,
-                        (const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko, (TOut*)vo, go,
-                        bo, B, T, Hqk, Hv, K, use_state, n_tiles, (int)conv_ctas, x_ld, ab_ld);
+      kern<<<(unsigned)(conv_ctas + gate_ctas), HDIM, smem, st>>>(
+          (const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko, (TOut*)vo, go, bo, B, T,
+          Hqk, Hv, K, use_state, n_tiles, (int)conv_ctas, x_ld, ab_ld);
     };
-    if (K == 4) return go_tile(prologue_tile_kernel<TIn, TOut, 4>);
-    return go_tile(prologue_tile_kernel<TIn, TOut, 0>);
+    if (K == 4) go_tile(prologue_tile_kernel<TIn, TOut, 4>);
+    else go_tile(prologue_tile_kernel<TIn, TOut, 0>);
   }
+  return launch_status("gdn_prologue");
 }
 
 }  // namespace

@@ -28,7 +28,6 @@ gdn_recurrent_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const
                      const float* __restrict__ g, const float* __restrict__ beta,
                      float* __restrict__ state, TOut* __restrict__ out,
                      int T, int Hqk, int Hv, int dv, float scale, int l2norm) {
-  pdl_enter();
   constexpr int CG = DVT / 4;   // float4 column groups per row
   constexpr int RG = NT / CG;   // row groups
   constexpr int RPT = DK / RG;  // rows per thread
@@ -166,13 +165,16 @@ int launch_recurrent(const void* q, const void* k, const void* v, const float* g
   // Narrow slices when there are few (b, h) pairs so the grid still covers the SMs.
   const long pairs = (long)B * Hv;
   const bool narrow = pairs * (dv / 32) < 2 * 148 && (dv % 16) == 0;
-  if (narrow)
-    return launch_pdl("gdn_recurrent", gdn_recurrent_kernel<TIn, TOut, 16, 128>, dim3(dv / 16, Hv, B), dim3(128), 0,
-                      st, (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv,
-                      scale, l2norm);
-  return launch_pdl("gdn_recurrent", gdn_recurrent_kernel<TIn, TOut, 32, 128>, dim3(dv / 32, Hv, B), dim3(128), 0, st,
-                    (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale,
-                    l2norm);
+  if (narrow) {
+    dim3 grid(dv / 16, Hv, B);
+    gdn_recurrent_kernel<TIn, TOut, 16, 128><<<grid, 128, 0, st>>>(
+        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm);
+  } else {
+    dim3 grid(dv / 32, Hv, B);
+    gdn_recurrent_kernel<TIn, TOut, 32, 128><<<grid, 128, 0, st>>>(
+        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm);
+  }
+  return launch_status("gdn_recurrent");
 }
 
 }  // namespace

@@ -431,6 +431,31 @@ kv_combine_kernel(KvParams p) {
   }
 }
 
+// Launch with programmatic stream serialisation, so that the kernel's launch overlaps the tail of the
+// previous kernel in the stream.  Every kernel launched this way calls griddep_wait() before its first
+// global-memory access.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: launch failed, CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
+    return (int)e;
+  }
+  return launch_status(what);
+}
+
 template <typename T, int HD>
 int launch_combine(const KvParams& q, cudaStream_t st) {
   const int R = q.S * (q.Hq / q.Hkv);

@@ -103,7 +103,6 @@ template <typename T, int NC>
 __global__ void __launch_bounds__(NT)
 rmsnorm_kernel(const T* x, const T* res, T* sum_out, const float* __restrict__ w, T* __restrict__ out,
                long long rows, int d, float eps) {
-  pdl_enter();
   const long long row = (long long)blockIdx.x * (NT / 32) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -119,7 +118,6 @@ template <typename T>
 __global__ void __launch_bounds__(NT)
 rmsnorm_row_kernel(const T* x, const T* res, T* sum_out, const float* __restrict__ w, T* __restrict__ out, int d,
                    float eps) {
-  pdl_enter();
   constexpr int NC = 2;  // d <= 2 * 8 * NT
   const long long row = blockIdx.x;
   __shared__ float part[NT / 32];
@@ -138,7 +136,6 @@ rmsnorm_row_kernel(const T* x, const T* res, T* sum_out, const float* __restrict
 template <typename T>
 __global__ void __launch_bounds__(NT)
 silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, long long rows, int ffn) {
-  pdl_enter();
   const int per_row = ffn / 8;
   const long long i = (long long)blockIdx.x * NT + threadIdx.x;
   if (i >= rows * per_row) return;
@@ -167,7 +164,6 @@ qk_norm_rope_kernel(const T* __restrict__ qg, long long qg_ld, const T* __restri
                     const float* __restrict__ kw, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                     T* __restrict__ qo, T* __restrict__ ko, T* __restrict__ vo, T* __restrict__ go,
                     int T_len, int Hq, int Hkv, int pos, float eps) {
-  pdl_enter();
   constexpr int HD = EPL * 32;
   const long long tok = blockIdx.x;  // b * T + t
   const int b = (int)(tok / T_len), t = (int)(tok % T_len);
@@ -238,10 +234,10 @@ extern "C" int anemll_rmsnorm(const void* x, const void* residual, void* sum_out
     // rows of more than 256 elements: a CTA per row (8 warps, a few loads in flight per thread, low
     // register use); shorter rows: a warp per row
     if (nc > 1)
-      return launch_pdl("rmsnorm", rmsnorm_row_kernel<T>, dim3((unsigned)rows), dim3(NT), 0, st, xx, rr,
-                        (T*)sum_out, weight, (T*)out, d, eps);
-    return launch_pdl("rmsnorm", rmsnorm_kernel<T, 1>, dim3(blocks), dim3(NT), 0, st, xx, rr, (T*)sum_out, weight,
-                      (T*)out, rows, d, eps);
+      rmsnorm_row_kernel<T><<<(unsigned)rows, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, d, eps);
+    else
+      rmsnorm_kernel<T, 1><<<blocks, NT, 0, st>>>(xx, rr, (T*)sum_out, weight, (T*)out, rows, d, eps);
+    return launch_status("rmsnorm");
   });
 }
 
@@ -255,8 +251,8 @@ extern "C" int anemll_silu_mul(const void* gate_up, void* out, int dtype, int64_
   const long long n = rows * (ffn / 8);
   ANEMLL_REQUIRE((n + NT - 1) / NT < (1LL << 31), ANEMLL_EINVAL, "silu_mul: too many rows");
   return ANEMLL_DISPATCH_DTYPE(dtype, T, [&] {
-    return launch_pdl("silu_mul", silu_mul_kernel<T>, dim3((unsigned)((n + NT - 1) / NT)), dim3(NT), 0, st,
-                      (const T*)gate_up, (T*)out, rows, ffn);
+    silu_mul_kernel<T><<<(unsigned)((n + NT - 1) / NT), NT, 0, st>>>((const T*)gate_up, (T*)out, rows, ffn);
+    return launch_status("silu_mul");
   });
 }
 
@@ -281,11 +277,14 @@ extern "C" int anemll_qk_norm_rope(const void* q_gate, int64_t qg_row_stride, co
   cudaStream_t st = (cudaStream_t)stream;
   return ANEMLL_DISPATCH_HALF(dtype, T_, [&] {
     const unsigned grid = (unsigned)((long long)B * T);
-    auto go = [&](auto kern) {
-      return launch_pdl("qk_norm_rope", kern, dim3(grid), dim3(NT), 0, st, (const T_*)q_gate, qg_row_stride,
-                        (const T_*)k, k_row_stride, (const T_*)v, v_row_stride, q_norm, k_norm, cos_table,
-                        sin_table, (T_*)q_out, (T_*)k_out, (T_*)v_out, (T_*)gate_out, T, H_q, H_kv, pos, eps);
-    };
-    return head_dim == 256 ? go(qk_norm_rope_kernel<T_, 8>) : go(qk_norm_rope_kernel<T_, 4>);
+    if (head_dim == 256)
+      qk_norm_rope_kernel<T_, 8><<<grid, NT, 0, st>>>(
+          (const T_*)q_gate, qg_row_stride, (const T_*)k, k_row_stride, (const T_*)v, v_row_stride, q_norm, k_norm,
+          cos_table, sin_table, (T_*)q_out, (T_*)k_out, (T_*)v_out, (T_*)gate_out, T, H_q, H_kv, pos, eps);
+    else
+      qk_norm_rope_kernel<T_, 4><<<grid, NT, 0, st>>>(
+          (const T_*)q_gate, qg_row_stride, (const T_*)k, k_row_stride, (const T_*)v, v_row_stride, q_norm, k_norm,
+          cos_table, sin_table, (T_*)q_out, (T_*)k_out, (T_*)v_out, (T_*)gate_out, T, H_q, H_kv, pos, eps);
+    return launch_status("qk_norm_rope");
   });
 }

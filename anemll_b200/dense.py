@@ -17,10 +17,7 @@ from . import _lib
 
 SKINNY_ROWS = 0  # rows up to which linear() uses anemll_gemm (see the module docstring)
 
-PREFETCH_ROWS = 512  # inputs of up to this many rows prefetch the next projection's weight into L2
-PREFETCH_MAX_BYTES = 48 << 20  # the leading bytes of a larger weight (the L2 holds 126 MB)
-
-__all__ = ["linear", "gemm", "gemm_device_error", "l2_prefetch", "SKINNY_ROWS", "PREFETCH_ROWS"]
+__all__ = ["linear", "gemm", "gemm_device_error", "SKINNY_ROWS"]
 
 
 def _fits(t):
@@ -59,20 +56,6 @@ def linear(x, weight):
             or x.dtype != weight.dtype or N % 8 or K % 8 or not _fits(weight)):
         return F.linear(x, weight)
     return gemm(x.reshape(M, K), weight).view(*x.shape[:-1], N)
-
-
-def l2_prefetch(weight, rows):
-    """Start streaming ``weight`` (its leading ``PREFETCH_MAX_BYTES``) into L2 ahead of its projection
-    (``anemll_l2_prefetch``), when that projection has at most ``PREFETCH_ROWS`` input rows: a batch
-    small enough that the GEMM is a weight stream whose start-up latency shows.  Call it right after
-    the kernel that precedes the small kernel before the projection; it changes no result."""
-    if rows > PREFETCH_ROWS or weight is None or not weight.is_contiguous():
-        return
-    if not weight.is_cuda:
-        raise RuntimeError("anemll_b200 ops take CUDA tensors (no CPU path)")
-    n = min(weight.numel() * weight.element_size(), PREFETCH_MAX_BYTES)
-    rc = _lib.load().anemll_l2_prefetch(_lib.ptr(weight), n, _lib.stream_ptr(weight.device))
-    _lib.check(rc, "anemll_l2_prefetch")
 
 
 def gemm_device_error(reset=True) -> int:

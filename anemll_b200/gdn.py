@@ -295,10 +295,8 @@ class GatedDeltaNet(nn.Module):
                           dtype=torch.float32)
         return conv, rec
 
-    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states, prefetch=None):
-        """Everything between the input and output projections (the hot path).  ``prefetch``: the
-        output projection's weight, whose L2 prefetch (few rows only) is issued once the recurrence
-        has finished, ahead of the gated norm."""
+    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states):
+        """Everything between the input and output projections (the hot path)."""
         B, T, _ = mixed_qkv.shape
         if not use_precomputed_states:
             recurrent_state.zero_()
@@ -311,8 +309,6 @@ class GatedDeltaNet(nn.Module):
                                         out_dtype=torch.float32)
         else:
             o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
-        if prefetch is not None:
-            dense.l2_prefetch(prefetch, B * T)
         normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim), self.norm_weight,
                                self.eps, out_dtype=mixed_qkv.dtype)
         return o, normed
@@ -323,6 +319,5 @@ class GatedDeltaNet(nn.Module):
         c, v = self.conv_dim, self.value_dim
         mixed_qkv, z = proj[..., :c], proj[..., c:c + v]
         b, a = proj[..., c + v:c + v + self.num_v_heads], proj[..., c + v + self.num_v_heads:]
-        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states,
-                              prefetch=self.out_proj.weight)
+        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states)
         return dense.linear(normed.reshape(B, T, self.value_dim), self.out_proj.weight)

@@ -216,16 +216,8 @@ class HybridStack(nn.Module):
             return m(h, state[0], state[1], pos, self.cos, self.sin)
         return m(h, state[0], state[1], use_precomputed_states=pos > 0)
 
-    def mlp(self, i, h, prefetch=False):
-        gu = dense.linear(h, self.gate_up[i].weight)
-        if prefetch:
-            dense.l2_prefetch(self.down[i].weight, h.numel() // self.cfg.hidden)
-        return dense.linear(silu_mul(gu), self.down[i].weight)
-
-    def in_weight(self, i):
-        """Layer i's fused input projection weight (attention q/k/v or gated-DeltaNet [qkv|z|b|a])."""
-        m = self.mixers[i]
-        return m.w_qkv if isinstance(m, GatedAttention) else m.w_in
+    def mlp(self, i, h):
+        return dense.linear(silu_mul(dense.linear(h, self.gate_up[i].weight)), self.down[i].weight)
 
     def layer(self, i, x, state, pos, with_mixer=False):
         """One decoder layer on x [B, T, hidden] at positions [pos, pos + T).  ``with_mixer``: also return
@@ -239,25 +231,17 @@ class HybridStack(nn.Module):
     @torch.no_grad()
     def forward_tokens(self, ids, state, pos):
         """ids [B, T] at positions [pos, pos + T) -> logits of the last position [B, vocab].  The
-        residual adds ride on the next norm (one ``anemll_rmsnorm`` per add + norm).  With few rows
-        (the decode steps) each projection's weight is prefetched into L2 just before the small
-        kernel that precedes the projection (``dense.l2_prefetch``)."""
+        residual adds ride on the next norm (one ``anemll_rmsnorm`` per add + norm)."""
         c = self.cfg
         x = self.embed(ids)
-        rows = ids.numel()
-        dense.l2_prefetch(self.in_weight(0), rows)
         h = rms_norm(x, self.norm1[0], c.eps)
         for i in range(c.n_layers):
-            m = self.mixer(i, h, state[i], pos)
-            dense.l2_prefetch(self.gate_up[i].weight, rows)
-            x, h = rms_norm(x, self.norm2[i], c.eps, residual=m)
+            x, h = rms_norm(x, self.norm2[i], c.eps, residual=self.mixer(i, h, state[i], pos))
             nxt = self.norm1[i + 1] if i + 1 < c.n_layers else self.norm
-            d = self.mlp(i, h, prefetch=True)
+            d = self.mlp(i, h)
             if i + 1 < c.n_layers:
-                dense.l2_prefetch(self.in_weight(i + 1), rows)
                 x, h = rms_norm(x, nxt, c.eps, residual=d)
             else:  # the final norm: last position only
-                dense.l2_prefetch(self.lm_head.weight, ids.shape[0])
                 _, h = rms_norm(x[:, -1], nxt, c.eps, residual=d[:, -1])
         return dense.linear(h, self.lm_head.weight)
 

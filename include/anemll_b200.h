@@ -293,16 +293,6 @@ int anemll_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
 /* Non-zero if a GEMM launch stopped on a bounded wait (synchronous; reset != 0 clears it). */
 int anemll_gemm_error(int reset);
 
-/*
- * Requests the bytes [ptr, ptr + bytes) (the whole 16-byte units inside the range) into L2 with bulk
- * prefetches spread over every SM, after the previous kernel of the stream has finished; the next
- * kernel may launch at once.  A scheduling hint for the decode steps: issued before the small kernel
- * that precedes a projection, it starts that projection's weight stream early.  No reference
- * counterpart (the reference's decode loop, anemll/models/qwen_model.py forward passes, issues its
- * projections back to back); it changes no result.
- */
-int anemll_l2_prefetch(const void* ptr, int64_t bytes, void* stream);
-
 #ifdef __cplusplus
 }
 #endif

@@ -44,25 +44,3 @@ def test_gemm_errors():
         dense.gemm(torch.zeros(2, 8, device=DEV), torch.zeros(8, 8, device=DEV))
     with pytest.raises(RuntimeError, match="CUDA"):
         dense.gemm(torch.zeros(2, 8).half(), torch.zeros(8, 8).half())
-
-
-def test_l2_prefetch_is_a_pure_hint():
-    """anemll_l2_prefetch only requests bytes into L2: any range (unaligned ends, shorter than one
-    16-byte unit, empty) is accepted, nothing is written, and the kernels after it in the stream see
-    the previous kernel's results."""
-    from anemll_b200 import _lib, dense
-    w = torch.randn(4096, 2048, device=DEV).bfloat16()
-    ref = w.clone()
-    lib = _lib.load()
-    st = _lib.stream_ptr(w.device)
-    base = w.data_ptr()
-    for off, n in ((0, w.numel() * 2), (3, 1000), (0, 15), (5, 0), (17, 70000)):
-        assert lib.anemll_l2_prefetch(base + off, n, st) == 0
-    x = torch.randn(128, 2048, device=DEV).bfloat16()
-    y = x * 2  # a kernel of the stream, then the prefetch, then a kernel that reads its output
-    dense.l2_prefetch(w, 128)
-    z = y + 1
-    dense.l2_prefetch(w, 10 ** 6)  # too many rows: no launch
-    torch.cuda.synchronize()
-    assert torch.equal(w, ref)
-    assert torch.equal(z, x * 2 + 1)
