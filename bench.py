@@ -971,11 +971,17 @@ def cpu_kv_sample(threads, window, n_chunks=4, n_dec=8):
                                                 "fp32 torch CPU oracle (the reference's own algorithm in fp32)")
 
 
+CPU_CACHE_NL, CPU_CACHE_H, CPU_CACHE_SW, CPU_CACHE_HD = 18, 1, 512, 256
+# bytes of one step of the CPU cache-op sample (the rotations, the mask writes and one state transition)
+CPU_CACHE_STEP_BYTES = (CPU_CACHE_NL * 2 * CPU_CACHE_H * 2 * CPU_CACHE_SW * CPU_CACHE_HD * 2
+                        + CPU_CACHE_NL * 2 * CPU_CACHE_H * 3 * 64 * CPU_CACHE_HD * 2 + 36 * (1000 * 256 + 4096 * 256) * 2)
+
+
 def cpu_cache_ops_sample(threads):
     """The same cache-op step with the oracle's torch ops on the host cores; returns GB/s."""
     from oracle import cache_ops as oc
     torch.set_num_threads(threads)
-    nl, H, sw, hd = 18, 1, 512, 256
+    nl, H, sw, hd = CPU_CACHE_NL, CPU_CACHE_H, CPU_CACHE_SW, CPU_CACHE_HD
     kv = torch.randn(2 * nl, H, sw, hd).half()
     key = torch.randn(1, H, 1, hd).half()
     new = torch.randn(1, H, 64, hd).half()
@@ -990,9 +996,7 @@ def cpu_cache_ops_sample(threads):
         kv[i:i + 1] = oc.update_mask_write(kv[i:i + 1], new, mask).half()
     oc.transition_state(st, 4096, 1000)
     dt = time.perf_counter() - t0
-    es = 2
-    byts = nl * 2 * H * 2 * sw * hd * es + nl * 2 * H * 3 * 64 * hd * es + 36 * (1000 * 256 + 4096 * 256) * es
-    return byts / dt / 1e9, "one step of the same cache ops with the oracle's torch CPU ops"
+    return CPU_CACHE_STEP_BYTES / dt / 1e9, "one step of the same cache ops with the oracle's torch CPU ops"
 
 
 def cpu_layer_sample(threads, n_dec=8):
@@ -1129,7 +1133,7 @@ def reference_arm(args, ws, rank):
             vals.append(v1)
         if args.config == "cache_ops":
             v, unit = max(vals), "GB/s"
-            ms = None
+            ms = CPU_CACHE_STEP_BYTES / (v * 1e9) * 1e3  # one step = one sample
         else:
             sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8,
                              "stack": 66}[args.config]
