@@ -26,6 +26,7 @@ constexpr int HDIM = 128;  // channels per head group (d_k == d_v); threads per 
 constexpr int TT = 32;     // tokens per tile (32: eight CTAs, 32 warps per SM)
 constexpr int MAXK = 8;    // largest supported conv kernel
 constexpr int DEC_T = 4;   // longest call served by the short kernel
+constexpr int SHORT_SB_MIN_B = 16;  // batches from which the short kernel takes four sequences per CTA
 
 __device__ __forceinline__ float load_any(const void* p, int dt, long long i) {
   return dt == ANEMLL_F32 ? reinterpret_cast<const float*>(p)[i]
@@ -202,8 +203,11 @@ prologue_tile_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn
 // ----------------------------------------------------------------- short --
 // conv_k == 4, TS = T tokens (1 .. DEC_T): raw slot s holds position s - 4 (the old state in slots
 // 0..3, x[t] in slot 4 + t), so token t's taps are slots t+1 .. t+4 and the new state is slots
-// TS .. TS+3, all static register indices.
-template <typename TIn, typename TOut, int TS>
+// TS .. TS+3, all static register indices.  A CTA takes one channel group of SB sequences (a
+// thread per channel): every sequence's loads are issued before the first is used, and the conv
+// weights are loaded once for all of them; each sequence's arithmetic (and its norm's reduction
+// order) is the same whatever SB is.
+template <typename TIn, typename TOut, int TS, int SB>
 __global__ void __launch_bounds__(HDIM)
 prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TIn* __restrict__ conv_state,
                       const void* __restrict__ a, const void* __restrict__ bgate, int ab_dt,
@@ -218,59 +222,78 @@ prologue_short_kernel(const TIn* __restrict__ x, const float* __restrict__ w, TI
   constexpr int K = 4;
   const int ngroups = 2 * Hqk + Hv;
   const int C = ngroups * HDIM;
-  const int grp = blockIdx.x % ngroups, b = blockIdx.x / ngroups;
+  const int grp = blockIdx.x % ngroups, b0 = (blockIdx.x / ngroups) * SB;
   const int c = threadIdx.x, ch = grp * HDIM + c;
-  TIn* cs = conv_state + ((long long)b * C + ch) * K;
-  const TIn* xg = x + (long long)b * TS * x_ld + ch;
-
-  TIn raw[K + TS];
-  if constexpr (sizeof(TIn) == 2) {
-    if (use_state) {
-      const uint2 u = *reinterpret_cast<const uint2*>(cs);  // 4 x 2 bytes, 8-byte aligned
-      const TIn* s4 = reinterpret_cast<const TIn*>(&u);
-#pragma unroll
-      for (int j = 0; j < K; ++j) raw[j] = s4[j];
-    } else {
-#pragma unroll
-      for (int j = 0; j < K; ++j) raw[j] = from_f32<TIn>(0.f);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < K; ++j) raw[j] = use_state ? cs[j] : from_f32<TIn>(0.f);
-  }
-#pragma unroll
-  for (int t = 0; t < TS; ++t) raw[K + t] = xg[(long long)t * x_ld];
   const float4 w4 = *reinterpret_cast<const float4*>(w + (long long)ch * K);
 
-  float y[TS];
+  TIn raw[SB][K + TS];
 #pragma unroll
-  for (int t = 0; t < TS; ++t)
-    y[t] = silu_fast(w4.x * to_f32(raw[t + 1]) + w4.y * to_f32(raw[t + 2]) + w4.z * to_f32(raw[t + 3]) +
-                     w4.w * to_f32(raw[t + 4]));
+  for (int s = 0; s < SB; ++s) {
+    const int b = b0 + s;
+#pragma unroll
+    for (int j = 0; j < K + TS; ++j) raw[s][j] = from_f32<TIn>(0.f);
+    if (b < B) {
+      const TIn* cs = conv_state + ((long long)b * C + ch) * K;
+      if constexpr (sizeof(TIn) == 2) {
+        if (use_state) {
+          const uint2 u = *reinterpret_cast<const uint2*>(cs);  // 4 x 2 bytes, 8-byte aligned
+          const TIn* s4 = reinterpret_cast<const TIn*>(&u);
+#pragma unroll
+          for (int j = 0; j < K; ++j) raw[s][j] = s4[j];
+        }
+      } else {
+        if (use_state) {
+#pragma unroll
+          for (int j = 0; j < K; ++j) raw[s][j] = cs[j];
+        }
+      }
+      const TIn* xg = x + (long long)b * TS * x_ld + ch;
+#pragma unroll
+      for (int t = 0; t < TS; ++t) raw[s][K + t] = xg[(long long)t * x_ld];
+    }
+  }
 
-  if (grp < 2 * Hqk) {  // q/k head: l2 norm over the 128 channels (4 warps)
-    __shared__ float part[HDIM / 32][TS];
+  float y[SB][TS];
+#pragma unroll
+  for (int s = 0; s < SB; ++s)
+#pragma unroll
+    for (int t = 0; t < TS; ++t)
+      y[s][t] = silu_fast(w4.x * to_f32(raw[s][t + 1]) + w4.y * to_f32(raw[s][t + 2]) +
+                          w4.z * to_f32(raw[s][t + 3]) + w4.w * to_f32(raw[s][t + 4]));
+
+  if (grp < 2 * Hqk) {  // q/k head: l2 norm over the 128 channels (4 warps), per sequence and token
+    __shared__ float part[HDIM / 32][SB][TS];
     const int lane = c & 31, warp = c >> 5;
 #pragma unroll
-    for (int t = 0; t < TS; ++t) {
-      const float ss = warp_sum(y[t] * y[t]);
-      if (lane == 0) part[warp][t] = ss;
-    }
+    for (int s = 0; s < SB; ++s)
+#pragma unroll
+      for (int t = 0; t < TS; ++t) {
+        const float ss = warp_sum(y[s][t] * y[s][t]);
+        if (lane == 0) part[warp][s][t] = ss;
+      }
     __syncthreads();
 #pragma unroll
-    for (int t = 0; t < TS; ++t) y[t] *= rsqrtf(part[0][t] + part[1][t] + part[2][t] + part[3][t] + 1e-6f);
+    for (int s = 0; s < SB; ++s)
+#pragma unroll
+      for (int t = 0; t < TS; ++t)
+        y[s][t] *= rsqrtf(part[0][s][t] + part[1][s][t] + part[2][s][t] + part[3][s][t] + 1e-6f);
   }
   const Dst d = group_dst(grp, Hqk, Hv, qo, ko, vo);
   TOut* dst = reinterpret_cast<TOut*>(d.p);
 #pragma unroll
-  for (int t = 0; t < TS; ++t) dst[(((long long)b * TS + t) * d.H + d.h) * HDIM + c] = from_f32<TOut>(y[t]);
-
-  if constexpr (sizeof(TIn) == 2) {  // new state: slots TS .. TS + 3
-    const TIn s4[4] = {raw[TS], raw[TS + 1], raw[TS + 2], raw[TS + 3]};
-    *reinterpret_cast<uint2*>(cs) = *reinterpret_cast<const uint2*>(s4);
-  } else {
+  for (int s = 0; s < SB; ++s) {
+    const int b = b0 + s;
+    if (b >= B) break;
 #pragma unroll
-    for (int j = 0; j < K; ++j) cs[j] = raw[TS + j];
+    for (int t = 0; t < TS; ++t) dst[(((long long)b * TS + t) * d.H + d.h) * HDIM + c] = from_f32<TOut>(y[s][t]);
+    TIn* cs = conv_state + ((long long)b * C + ch) * K;
+    if constexpr (sizeof(TIn) == 2) {  // new state: slots TS .. TS + 3
+      const TIn s4[4] = {raw[s][TS], raw[s][TS + 1], raw[s][TS + 2], raw[s][TS + 3]};
+      *reinterpret_cast<uint2*>(cs) = *reinterpret_cast<const uint2*>(s4);
+    } else {
+#pragma unroll
+      for (int j = 0; j < K; ++j) cs[j] = raw[s][TS + j];
+    }
   }
 }
 
@@ -282,18 +305,29 @@ int launch_prologue(const void* x, const float* w, void* cs, const void* a, cons
   const int ngroups = 2 * Hqk + Hv;
   const long long gate_ctas = ((long long)B * T * Hv + HDIM - 1) / HDIM;
   if (T <= DEC_T && K == 4) {
-    const long long conv_ctas = (long long)B * ngroups;
+    // four sequences per CTA once there are enough of them to fill the SMs
+    const int sb = B >= SHORT_SB_MIN_B ? 4 : 1;
+    const long long conv_ctas = (long long)((B + sb - 1) / sb) * ngroups;
     ANEMLL_REQUIRE(conv_ctas + gate_ctas < (1LL << 31), ANEMLL_EINVAL, "gdn_prologue: problem too large");
     const unsigned grid = (unsigned)(conv_ctas + gate_ctas);
     auto go_short = [&](auto kern) {
       kern<<<grid, HDIM, 0, st>>>((const TIn*)x, w, (TIn*)cs, a, bg, ab_dt, A_log, dt_bias, (TOut*)qo, (TOut*)ko,
                                   (TOut*)vo, go, bo, B, Hqk, Hv, use_state, (int)conv_ctas, x_ld, ab_ld);
     };
-    switch (T) {
-      case 1: go_short(prologue_short_kernel<TIn, TOut, 1>); break;
-      case 2: go_short(prologue_short_kernel<TIn, TOut, 2>); break;
-      case 3: go_short(prologue_short_kernel<TIn, TOut, 3>); break;
-      default: go_short(prologue_short_kernel<TIn, TOut, 4>); break;
+    if (sb == 4) {
+      switch (T) {
+        case 1: go_short(prologue_short_kernel<TIn, TOut, 1, 4>); break;
+        case 2: go_short(prologue_short_kernel<TIn, TOut, 2, 4>); break;
+        case 3: go_short(prologue_short_kernel<TIn, TOut, 3, 4>); break;
+        default: go_short(prologue_short_kernel<TIn, TOut, 4, 4>); break;
+      }
+    } else {
+      switch (T) {
+        case 1: go_short(prologue_short_kernel<TIn, TOut, 1, 1>); break;
+        case 2: go_short(prologue_short_kernel<TIn, TOut, 2, 1>); break;
+        case 3: go_short(prologue_short_kernel<TIn, TOut, 3, 1>); break;
+        default: go_short(prologue_short_kernel<TIn, TOut, 4, 1>); break;
+      }
     }
   } else {
     const int n_tiles = (T + TT - 1) / TT;

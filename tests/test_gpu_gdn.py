@@ -134,7 +134,8 @@ def _prologue_case(B, T, use_state, seed, K=4):
 
 
 @pytest.mark.parametrize("B,T,use_state,K", [(1, 512, False, 4), (2, 37, True, 4), (3, 1, True, 4), (1, 2, True, 4),
-                                             (2, 3, False, 4), (2, 20, True, 6), (1, 3, True, 2), (2, 17, False, 8)])
+                                             (2, 3, False, 4), (2, 20, True, 6), (1, 3, True, 2), (2, 17, False, 8),
+                                             (18, 1, True, 4), (33, 2, True, 4), (16, 4, False, 4)])
 def test_prologue_matches_oracle(B, T, use_state, K):
     Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(B, T, use_state, 10 + T, K)
     cs_dev = cs.to(DEV)
@@ -194,6 +195,25 @@ def test_gdn_layer_prefill_then_decode_matches_oracle():
                              rel_l2=5e-3, max_abs=6.25e-2)
                 assert torch.equal(conv_state.cpu(), ref_conv.to(torch.bfloat16)), "conv state"
                 assert_close(rec_state, ref_state, f"state step {step}")
+
+
+@pytest.mark.parametrize("T", [1, 3])
+def test_short_prologue_batch_equals_single_sequences(T):
+    """The decode-length prologue takes four sequences per CTA at batches of 16 or more: a batch of
+    21 (a ragged last group) gives bit for bit what 21 one-sequence calls give."""
+    B = 21
+    Hqk, Hv, x, w, cs, a, bb, A_log, dtb = _prologue_case(B, T, True, 70 + T)
+    args = (w.to(DEV), A_log.to(DEV), dtb.to(DEV))
+    cs_all = cs.to(DEV)
+    got = gdn.gdn_prologue(x.to(DEV), args[0], cs_all, a.to(DEV), bb.to(DEV), args[1], args[2], Hqk, Hv,
+                           use_state=True)
+    for b in range(B):
+        cs_b = cs[b:b + 1].to(DEV)
+        ref = gdn.gdn_prologue(x[b:b + 1].to(DEV), args[0], cs_b, a[b:b + 1].to(DEV), bb[b:b + 1].to(DEV), args[1],
+                               args[2], Hqk, Hv, use_state=True)
+        for g_, r_ in zip(got, ref):
+            assert torch.equal(g_[b:b + 1], r_), f"sequence {b}"
+        assert torch.equal(cs_all[b:b + 1], cs_b), f"conv state {b}"
 
 
 @pytest.mark.parametrize("T,use_state", [(1, True), (3, True), (200, False)])
