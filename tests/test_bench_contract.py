@@ -1,7 +1,7 @@
 """bench.py's output contract, checked on CPU through its reference arm (the CPU oracle timed on the
 host cores, which needs no GPU): one JSON line with the metric, the timing fields, the CPU-baseline
 description and an e2e entry with no host/device copies; under torchrun only rank 0 prints it and
-every rank exits 0."""
+every rank exits 0.  Our arm, with no GPU visible, exits non-zero without printing a line."""
 import json
 import os
 import socket
@@ -53,3 +53,12 @@ def test_reference_arm_under_torchrun_prints_once():
                   "--config", "cache_ops", "--steps", "1", "--warmup", "1"])
     assert len(lines) == 1
     _check_line(lines[0], "cache_ops")
+
+
+@pytest.mark.parametrize("config", ["gdn_decode", "stack"])
+def test_our_arm_fails_loudly_without_a_gpu(config):
+    """The library path has no CPU fallback: without a GPU our arm exits non-zero and prints no line."""
+    r = subprocess.run([sys.executable, "bench.py", "--config", config, "--steps", "1"], cwd=ROOT,
+                       capture_output=True, text=True, timeout=300, env=dict(os.environ, CUDA_VISIBLE_DEVICES=""))
+    assert r.returncode != 0
+    assert not any(l.startswith("{") for l in r.stdout.splitlines())
