@@ -45,8 +45,6 @@ _SIGS = {
     "anemll_kv_update_mask": ([_vp, _vp, _c_int, _vp, _c_int, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_i64, _c_i64,
                                _vp], _c_int),
     "anemll_kv_rotate_append": ([_vp, _vp, _c_int, _c_i64, _c_int, _c_int, _c_int, _c_i64, _c_i64, _vp], _c_int),
-    "anemll_gemm": ([_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _c_int, _vp], _c_int),
-    "anemll_gemm_error": ([_c_int], _c_int),
     "anemll_rmsnorm": ([_vp, _vp, _vp, _vp, _vp, _c_int, _c_i64, _c_int, _c_float, _vp], _c_int),
     "anemll_silu_mul": ([_vp, _vp, _c_int, _c_i64, _c_int, _vp], _c_int),
     "anemll_qk_norm_rope": ([_vp, _c_i64, _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int,

@@ -1639,8 +1639,9 @@ int kv_attention_run(const void* q, const void* k_new, const void* v_new, const 
   ANEMLL_REQUIRE(H_q % H_kv == 0, ANEMLL_EINVAL, "kv_attention: H_q %% H_kv != 0");
   ANEMLL_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, ANEMLL_EUNSUPPORTED,
                  "kv_attention: head_dim must be 64, 128 or 256 (got %d)", head_dim);
-  ANEMLL_REQUIRE(current_pos >= 0 && current_pos + S <= ctx, ANEMLL_EINVAL,
-                 "kv_attention: positions [%d, %d) exceed the cache length %d", current_pos, current_pos + S, ctx);
+  ANEMLL_REQUIRE(current_pos >= 0 && (int64_t)current_pos + S <= ctx, ANEMLL_EINVAL,
+                 "kv_attention: positions [%d, %lld) exceed the cache length %d", current_pos,
+                 (long long)current_pos + S, ctx);
   ANEMLL_REQUIRE(!mask || (mask_dtype == ANEMLL_F32 || mask_dtype == ANEMLL_F16 || mask_dtype == ANEMLL_BF16),
                  ANEMLL_EUNSUPPORTED, "kv_attention: bad mask dtype");
   ANEMLL_REQUIRE(!mask || mask_row_stride >= ctx, ANEMLL_EINVAL, "kv_attention: mask row stride < ctx");
@@ -1765,6 +1766,11 @@ extern "C" int anemll_kv_attention_qkv(const void* qkv, int64_t qkv_row_stride, 
 //   reads (every split writes all of its partial rows before the combine reads
 //   them), so nothing has to start at zero, but two calls that overlap on the
 //   GPU (different streams, or different host threads) race on the array.
+// - The size check uses the split count of the generic split-KV plan, the
+//   largest any path of this call can take; the tcgen05 and decode paths often
+//   use fewer splits, so a call can be refused although its path would fit.
+// - The cached address belongs to the device's primary context: do not use this
+//   entry point after a cudaDeviceReset in the same process.
 // - It never calls cudaMalloc, cudaFree or any allocating library routine.
 #include <mutex>
 
@@ -1818,6 +1824,9 @@ extern "C" int anemll_kv_attention_noalloc(const void* q, const void* k_new, con
   // sizes the plan needs; everything else is validated by anemll_kv_attention
   ANEMLL_REQUIRE(B > 0 && S > 0 && H_q > 0 && H_kv > 0 && H_q % H_kv == 0 && ctx > 0 && current_pos >= 0,
                  ANEMLL_EINVAL, "kv_attention_noalloc: bad sizes");
+  ANEMLL_REQUIRE((int64_t)current_pos + S <= ctx, ANEMLL_EINVAL,
+                 "kv_attention_noalloc: positions [%d, %lld) exceed the cache length %d", current_pos,
+                 (long long)current_pos + S, ctx);
   ANEMLL_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, ANEMLL_EUNSUPPORTED,
                  "kv_attention_noalloc: head_dim must be 64, 128 or 256 (got %d)", head_dim);
   const Plan pl = make_plan(B, S, H_q, H_kv, ctx, current_pos, window, window_chunk_aligned, mask != nullptr);

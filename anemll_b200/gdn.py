@@ -23,7 +23,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _lib, dense
+from . import _lib
 
 __all__ = [
     "recurrent_gated_delta_rule",
@@ -315,9 +315,9 @@ class GatedDeltaNet(nn.Module):
 
     def forward(self, hidden_states, conv_state, recurrent_state, use_precomputed_states=False):
         B, T, _ = hidden_states.shape
-        proj = dense.linear(hidden_states, self.w_in)  # [B, T, conv_dim + value_dim + 2 H_v]
+        proj = F.linear(hidden_states, self.w_in)  # [B, T, conv_dim + value_dim + 2 H_v]
         c, v = self.conv_dim, self.value_dim
         mixed_qkv, z = proj[..., :c], proj[..., c:c + v]
         b, a = proj[..., c + v:c + v + self.num_v_heads], proj[..., c + v + self.num_v_heads:]
         _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states)
-        return dense.linear(normed.reshape(B, T, self.value_dim), self.out_proj.weight)
+        return F.linear(normed.reshape(B, T, self.value_dim), self.out_proj.weight)

@@ -12,8 +12,8 @@ followed by a SwiGLU MLP, both pre-normed (RMSNorm) with residuals.
   (``QwenHeadNorm``, ``anemll/models/qwen_model.py:143-184``) and the rotary embedding
   (``apply_rotary_pos_emb``, 186-261) inside the attention call, writes the new cache rows and applies
   the gate in its epilogue; then o_proj.
-* Projections and the LM head: ``dense.linear`` (torch's GEMM for now); norms and the SwiGLU: the
-  one-pass kernels of ``stack_ops.cu``.
+* Projections and the LM head: torch's GEMM (``F.linear``); norms and the SwiGLU: the one-pass
+  kernels of ``stack_ops.cu``.
 
 Caches and states are per sequence: KV caches ``[B, H_kv, ctx, hd]`` per attention layer, conv and
 recurrent states per GDN layer.  Weights are random N(0, 0.02) (no checkpoints offline).
@@ -26,7 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _lib, attention, dense, gdn
+from . import _lib, attention, gdn
 
 __all__ = ["StackConfig", "HybridStack", "GreedyDecoder", "nccl_id_gather", "shard", "rms_norm", "silu_mul",
            "rope_tables"]
@@ -118,7 +118,7 @@ class GatedAttention(nn.Module):
     def project(self, x, cos, sin, pos):
         """q [B, H_q, T, hd], k/v [B, H_kv, T, hd] (normed, rotated), gate [B, T, H_q*hd], from one fused
         q/k/v GEMM and ``anemll_qk_norm_rope`` (the unfused prologue)."""
-        return self._prologue(dense.linear(x, self.w_qkv), cos, sin, pos)
+        return self._prologue(F.linear(x, self.w_qkv), cos, sin, pos)
 
     def _prologue(self, qkv, cos, sin, pos):
         B, T, ld = qkv.shape
@@ -142,7 +142,7 @@ class GatedAttention(nn.Module):
         head norm and RoPE run inside the attention call (``anemll_kv_attention_qkv``) where it takes
         the shape, else through the separate prologue kernel."""
         c = self.cfg
-        qkv = dense.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
+        qkv = F.linear(x, self.w_qkv)  # [B, T, n_q + 2 n_kv]
         o = None
         if fused:
             o = attention.kv_attention_qkv(qkv, self.q_norm, self.k_norm, cos, sin, c.eps, k_cache, v_cache, pos,
@@ -150,7 +150,7 @@ class GatedAttention(nn.Module):
         if o is None:
             q, k, v, gate = self._prologue(qkv, cos, sin, pos)
             o = attention.kv_attention(q, k_cache, v_cache, pos, k_new=k, v_new=v, gate=gate)
-        return dense.linear(o, self.o_proj.weight)
+        return F.linear(o, self.o_proj.weight)
 
 
 class HybridStack(nn.Module):
@@ -217,7 +217,7 @@ class HybridStack(nn.Module):
         return m(h, state[0], state[1], use_precomputed_states=pos > 0)
 
     def mlp(self, i, h):
-        return dense.linear(silu_mul(dense.linear(h, self.gate_up[i].weight)), self.down[i].weight)
+        return F.linear(silu_mul(F.linear(h, self.gate_up[i].weight)), self.down[i].weight)
 
     def layer(self, i, x, state, pos, with_mixer=False):
         """One decoder layer on x [B, T, hidden] at positions [pos, pos + T).  ``with_mixer``: also return
@@ -243,7 +243,7 @@ class HybridStack(nn.Module):
                 x, h = rms_norm(x, nxt, c.eps, residual=d)
             else:  # the final norm: last position only
                 _, h = rms_norm(x[:, -1], nxt, c.eps, residual=d[:, -1])
-        return dense.linear(h, self.lm_head.weight)
+        return F.linear(h, self.lm_head.weight)
 
     @torch.no_grad()
     def generate(self, prompt, n_steps, gather=None, graphs=False):

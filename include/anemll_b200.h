@@ -178,9 +178,13 @@ int anemll_kv_attention_error(int reset);
  * held on every GPU that loads the library until the process exits).
  * Same arguments as anemll_kv_attention minus the workspace; calls whose
  * scratch need exceeds the maximum return ANEMLL_EWORKSPACE without launching.
- * The first call on a device (with that device current) looks up the array's
- * device address; make it before any stream capture.  All calls share the
- * array: calls that overlap on the GPU race.  Allocates nothing.
+ * The size check uses the split count of the generic split-KV plan, the largest
+ * any path of the call can take, so a call whose chosen path needs less can
+ * still be refused.  The first call on a device (with that device current)
+ * looks up the array's device address and caches it; make it before any stream
+ * capture, and do not use the entry point after a cudaDeviceReset in the same
+ * process.  All calls share the array: calls that overlap on the GPU race.
+ * Allocates nothing.
  */
 size_t anemll_kv_attention_noalloc_max_scratch(void);
 
@@ -279,19 +283,6 @@ int anemll_qk_norm_rope(const void* q_gate, int64_t qg_row_stride, const void* k
                         const float* cos_table, const float* sin_table, void* q_out, void* k_out, void* v_out,
                         void* gate_out, int dtype, int B, int T, int H_q, int H_kv, int head_dim, int pos,
                         float eps, void* stream);
-
-/*
- * y[M][N] = x[M][K] . w[N][K]^T, fp16 or bf16 (dtype), fp32 accumulation, y in the same type; row
- * strides ldx, ldw, ldy in elements (multiples of 8, pointers 16-byte aligned).  Built for few rows
- * (the decode steps' projections, where the weights stream through once): 128 x 128 tcgen05 tiles
- * fed by TMA, K split over a thread-block cluster of up to 8 CTAs whose fp32 partial tiles are summed
- * through distributed shared memory.  Replaces the projections of the reference's layers at decode
- * (the Conv2d / Linear projections of anemll/models/qwen_model.py, e.g. QwenMLP 272-298).
- */
-int anemll_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int M, int N, int K,
-                int dtype, void* stream);
-/* Non-zero if a GEMM launch stopped on a bounded wait (synchronous; reset != 0 clears it). */
-int anemll_gemm_error(int reset);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,7 @@
 """Generate ``cache_ops.pt``: golden vectors of the cache-management ops, from the reference itself.
 
-Runs, on the CPU, the reference's own functions from the read-only checkout (``--reference``,
-default ``/root/reference``):
+Runs, on the CPU, the reference's own functions from the read-only checkout (``--reference PATH``
+or the ``ANEMLL_REFERENCE`` environment variable):
 
 * ``Gemma3Model._apply_update_mask`` / ``_apply_update_mask_batch``
   (``anemll/models/gemma3_model.py:932-965``), which use no model state, called unbound;
@@ -11,7 +11,7 @@ default ``/root/reference``):
 * ``transition_kv_state`` / ``compact_kv_state`` (``anemll/utils/state_transition.py:62-357``).
 
 All tensors are fp16, the reference's cache dtype, except the dtype-converting transition case.
-Usage: ``python tests/golden/make_cache_ops.py [--reference PATH]``.
+Usage: ``python tests/golden/make_cache_ops.py --reference PATH``.
 """
 from __future__ import annotations
 
@@ -94,5 +94,7 @@ def main(ref_root):
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ANEMLL_REFERENCE"),
+                    required="ANEMLL_REFERENCE" not in os.environ,
+                    help="checkout of the reference repository (or set ANEMLL_REFERENCE)")
     main(ap.parse_args().reference)

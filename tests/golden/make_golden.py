@@ -3,8 +3,8 @@
 Sources of truth:
 
 * KV-cache attention: the reference itself, ``anemll/models/qwen_model.py`` from
-  the read-only reference checkout (``--reference``, default
-  ``/root/reference``), imported with ``MODEL_DTYPE = torch.float32`` so the
+  the read-only reference checkout (``--reference PATH`` or the
+  ``ANEMLL_REFERENCE`` environment variable), imported with ``MODEL_DTYPE = torch.float32`` so the
   whole attention path runs in fp32 on fp16-rounded inputs.
   ``QwenAttention.forward_prefill`` (509-546) and ``forward_regular`` (469-507)
   are called with ``o_proj`` set to the identity, so the recorded output is the
@@ -24,7 +24,7 @@ Sources of truth:
   ``Qwen3_5GatedDeltaNet.forward`` (463-474) and ``Qwen3_5RMSNormGated``
   (175-190), all on CPU in fp32 (the chunk/recurrent rules in fp64 as well).
 
-Usage: ``python tests/golden/make_golden.py [--reference PATH]``.
+Usage: ``python tests/golden/make_golden.py --reference PATH``.
 The GPU tests and the oracle tests read only the ``.pt`` files written here.
 """
 from __future__ import annotations
@@ -198,7 +198,9 @@ def make_gdn():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("ANEMLL_REFERENCE"),
+                    required="ANEMLL_REFERENCE" not in os.environ,
+                    help="checkout of the reference repository (or set ANEMLL_REFERENCE)")
     args = ap.parse_args()
     make_kv(args.reference)
     make_gdn()

@@ -60,9 +60,48 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
         assert torch.equal(cache_a, cache_b), "cache writes differ"
 
 
+def test_noalloc_matches_workspace_entry_point_on_prefill_chunks():
+    """16-token chunks take the tcgen05 prefill path, whose partial rows sit at offsets set by its own
+    split count inside the scratch; two chunks in a row against the workspace entry point."""
+    lib = _lib.load()
+    torch.manual_seed(43)
+    S = 16
+    cache = torch.zeros(2, HKV, CTX, HD, dtype=torch.half)
+    cache[:, :, :2048] = torch.randn(2, HKV, 2048, HD).half()
+    cache_a, cache_b = cache.to(DEV), cache.clone().to(DEV)
+    # the workspace entry point is sized for any position (about 20 MB); at these positions the plan
+    # splits each key range about 17 ways, about 4.5 MB, which the built-in array holds
+    need = lib.anemll_kv_attention_workspace_size(1, S, HQ, HKV, HD, CTX)
+    ws = torch.empty(need, dtype=torch.uint8, device=DEV)
+    for pos in (2048, 2048 + S):
+        q = torch.randn(1, HQ, S, HD, dtype=torch.half, device=DEV)
+        kn = torch.randn(1, HKV, S, HD, dtype=torch.half, device=DEV)
+        vn = torch.randn(1, HKV, S, HD, dtype=torch.half, device=DEV)
+        gate = torch.randn(1, S, HQ * HD, dtype=torch.half, device=DEV)
+        out_a = torch.empty(1, S, HQ * HD, dtype=torch.half, device=DEV)
+        out_b = torch.full_like(out_a, float("nan"))
+        _lib.check(_call(lib, False, q, kn, vn, gate, cache_a[0], cache_a[1], out_a, pos, ws), "regular")
+        _lib.check(_call(lib, True, q, kn, vn, gate, cache_b[0], cache_b[1], out_b, pos), "noalloc")
+        torch.cuda.synchronize()
+        assert_close(out_b.float(), out_a.float(), f"chunk at {pos}")
+        assert torch.equal(cache_a, cache_b), "cache writes differ"
+
+
+def test_noalloc_rejects_positions_past_the_cache():
+    lib = _lib.load()
+    cache = torch.zeros(2, HKV, CTX, HD, dtype=torch.half, device=DEV)
+    q = torch.zeros(1, HQ, 1, HD, dtype=torch.half, device=DEV)
+    kn = torch.zeros(1, HKV, 1, HD, dtype=torch.half, device=DEV)
+    out = torch.empty(1, 1, HQ * HD, dtype=torch.half, device=DEV)
+    for pos in (CTX, 2**31 - 1):  # the second would overflow a 32-bit pos + S
+        assert _call(lib, True, q, kn, kn, None, cache[0], cache[1], out, pos) == -1
+        assert _call(lib, False, q, kn, kn, None, cache[0], cache[1], out, pos,
+                     torch.empty(1 << 20, dtype=torch.uint8, device=DEV)) == -1
+
+
 def test_noalloc_rejects_scratch_beyond_its_maximum():
     lib = _lib.load()
-    # a 64-token prefill chunk of this shape needs about 20 MB of split-KV scratch
+    # a 64-token prefill chunk of this shape needs about 18 MB of split-KV scratch
     S, pos = 64, 2048
     cache = torch.zeros(2, HKV, CTX, HD, dtype=torch.half, device=DEV)
     q = torch.zeros(1, HQ, S, HD, dtype=torch.half, device=DEV)
