@@ -1,20 +1,21 @@
 """Fixed-shape KV-cache attention on the sm_100a kernel, behind the reference's signatures.
 
 ``kv_attention`` is the fused op (cache write + GQA attention + sigmoid gate).
-``QwenAttentionB200`` keeps the method signatures of the reference's
-``QwenAttention`` (``anemll/models/qwen_model.py``):
+``QwenAttentionB200`` keeps the method signatures and results of the
+reference's ``QwenAttention`` (``anemll/models/qwen_model.py``):
 ``forward_prefill(hidden_states, query_states, kv_cache_layer, causal_mask)``
 (509-546) and ``forward_regular(hidden_states, query_states, kv_cache_layer,
 causal_mask, current_pos)`` (469-507), where the caller has already written
 the cache (``process_layer_prefill`` 669-675 / ``process_layer_regular``
-733-745); ``process_layer_step`` does write + attend in one launch on the
-unified cache ``kv_cache_0`` [2L, H_kv, ctx, hd].  Outputs are the attention
-output before ``o_proj`` (``o_proj`` stays a torch GEMM in the caller).
+733-745), both ending in ``o_proj`` (a torch GEMM on the kernel's output);
+``process_layer_step`` does write + attend in one launch on the unified cache
+``kv_cache_0`` [2L, H_kv, ctx, hd].
 """
 from __future__ import annotations
 
 import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from . import _lib
 
@@ -164,36 +165,86 @@ def kv_attention_qkv(qkv, q_norm, k_norm, cos, sin, eps, k_cache, v_cache, curre
 
 
 class QwenAttentionB200(nn.Module):
-    """The attention core of ``QwenAttention`` with the reference's method signatures.
+    """``QwenAttention``'s attention methods with the reference's signatures and results.
 
-    Holds no weights: projections, q/k norms and RoPE (``get_new_kv_cache*``,
-    qwen_model.py:362-415) and ``o_proj`` stay torch GEMMs in the caller, so the
-    methods return the attention output before ``o_proj`` ([B, S, H_q*hd]).
-    ``window`` > 0 selects the sliding-window rule when no mask is given.
+    ``forward_prefill(hidden_states, query_states, kv_cache_layer, causal_mask)``
+    (qwen_model.py:509-546) and ``forward_regular(hidden_states, query_states,
+    kv_cache_layer, causal_mask, current_pos)`` (469-507) attend over the
+    caller's fixed-shape cache (``kv_cache_layer`` = (K [H_kv, ctx, hd],
+    V [H_kv, ctx, hd]), already written by ``process_layer_*``, 669-675 /
+    733-745) and end in ``o_proj``, so they return what the reference returns:
+    [B, S, hidden].  ``o_proj`` is the reference's 1x1 ``Conv2d``
+    ([hidden, H_q*hd, 1, 1] weight), an ``nn.Linear``, or a weight tensor of
+    either shape; it runs as a torch GEMM on the kernel's output.
+    ``from_reference(attn)`` shares a reference module's ``o_proj``.  Without
+    ``o_proj`` the projection is the identity.  ``attention(...)`` is the
+    pre-projection core ([B, S, H_q*hd]).  ``window`` > 0 selects the
+    sliding-window rule when no mask is given; ``gate`` (optional) is the
+    sigmoid output gate's pre-activation [B, S, H_q*hd].
     """
 
-    def __init__(self, num_heads, num_kv_heads, head_dim, window=0, window_chunk_aligned=False):
+    def __init__(self, num_heads, num_kv_heads, head_dim, window=0, window_chunk_aligned=False, o_proj=None):
         super().__init__()
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
         self.window, self.window_chunk_aligned = window, window_chunk_aligned
+        self.o_proj = o_proj
+        self._w = None  # o_proj weight as [hidden, H_q*hd] in the activation dtype (cached)
+
+    @classmethod
+    def from_reference(cls, attn, window=0, window_chunk_aligned=False):
+        """Wrap a reference ``QwenAttention`` (its head shape and its ``o_proj`` module)."""
+        return cls(attn.num_heads, attn.num_kv_heads, attn.head_dim, window, window_chunk_aligned, attn.o_proj)
+
+    def _proj_weight(self, dtype, device):
+        p = self.o_proj
+        w = p if isinstance(p, torch.Tensor) else p.weight
+        qd = self.num_heads * self.head_dim
+        if w.dim() == 4:
+            if tuple(w.shape[1:]) != (qd, 1, 1):
+                raise ValueError(f"o_proj Conv2d weight must be [hidden, {qd}, 1, 1]")
+            w = w.reshape(w.shape[0], qd)
+        if w.dim() != 2 or w.shape[1] != qd:
+            raise ValueError(f"o_proj weight must be [hidden, {qd}]")
+        c = self._w
+        if c is None or c[0] is not w or c[1].dtype != dtype or c[1].device != device:
+            self._w = c = (w, w.detach().to(device=device, dtype=dtype).contiguous())
+        return c[1]
+
+    def project(self, attn_output):
+        """``o_proj`` of the attention output [B, S, H_q*hd] (identity without one)."""
+        if self.o_proj is None:
+            return attn_output
+        bias = getattr(self.o_proj, "bias", None)
+        return F.linear(attn_output, self._proj_weight(attn_output.dtype, attn_output.device),
+                        None if bias is None else bias.to(attn_output.dtype))
+
+    def attention(self, query_states, kv_cache_layer, causal_mask=None, current_pos=0, gate=None):
+        K, V = kv_cache_layer
+        return kv_attention(query_states, K, V, _position(current_pos), gate=gate, causal_mask=causal_mask,
+                            window=self.window, window_chunk_aligned=self.window_chunk_aligned)
 
     def forward_prefill(self, hidden_states, query_states, kv_cache_layer=None, causal_mask=None, gate=None,
                         current_pos=0):
-        K, V = kv_cache_layer
-        return kv_attention(query_states, K, V, current_pos, gate=gate, causal_mask=causal_mask,
-                            window=self.window, window_chunk_aligned=self.window_chunk_aligned)
+        return self.project(self.attention(query_states, kv_cache_layer, causal_mask, current_pos, gate))
 
     def forward_regular(self, hidden_states, query_states, kv_cache_layer=None, causal_mask=None, current_pos=None,
                         gate=None):
-        K, V = kv_cache_layer
-        pos = int(current_pos) if current_pos is not None else 0
-        return kv_attention(query_states, K, V, pos, gate=gate, causal_mask=causal_mask, window=self.window,
-                            window_chunk_aligned=self.window_chunk_aligned)
+        return self.project(self.attention(query_states, kv_cache_layer, causal_mask,
+                                           0 if current_pos is None else current_pos, gate))
 
     def process_layer_step(self, kv_cache, layer_idx, num_layers, query_states, key_states, value_states,
                            current_pos, gate=None, causal_mask=None):
-        """Fused cache write + attention on the unified cache (one launch)."""
+        """Fused cache write + attention on the unified cache (one launch), then ``o_proj``."""
         K, V = unified_cache_layer(kv_cache, layer_idx, num_layers)
-        return kv_attention(query_states, K, V, int(current_pos), k_new=key_states, v_new=value_states, gate=gate,
-                            causal_mask=causal_mask, window=self.window,
-                            window_chunk_aligned=self.window_chunk_aligned)
+        return self.project(kv_attention(query_states, K, V, _position(current_pos), k_new=key_states,
+                                         v_new=value_states, gate=gate, causal_mask=causal_mask, window=self.window,
+                                         window_chunk_aligned=self.window_chunk_aligned))
+
+
+def _position(current_pos) -> int:
+    """``current_pos`` as an int: the reference passes positions as one-element int tensors."""
+    if isinstance(current_pos, torch.Tensor):
+        if current_pos.numel() != 1:
+            raise ValueError("current_pos must hold one position")
+        return int(current_pos.reshape(()).item())
+    return int(current_pos)

@@ -249,11 +249,14 @@ class GatedDeltaNet(nn.Module):
     """Drop-in Qwen3.5 gated-DeltaNet layer (``Qwen3_5GatedDeltaNet``, modeling_qwen3_5.py:356-533).
 
     Same parameters and projections; the state lives in caller-owned tensors
-    that ``forward`` mutates in place (the reference's mutable-buffer
-    convention): ``conv_state`` [B, C, K] in the activation dtype and
-    ``recurrent_state`` [B, H_v, d_k, d_v] fp32.  ``use_precomputed_states``
-    selects decode semantics (history read from the states), otherwise the
-    call is a fresh prefill that overwrites them.
+    that ``forward(hidden_states, current_pos, conv_state, recurrent_state)``
+    mutates in place (the reference's mutable-buffer convention, like its
+    ``kv_cache_0`` buffer): ``conv_state`` [B, C, K] in the activation dtype and
+    ``recurrent_state`` [B, H_v, d_k, d_v] fp32.  ``current_pos`` is the
+    position of the first token of ``hidden_states`` (an int or a one-element
+    tensor): 0 starts a sequence (zero conv history, the recurrent state is
+    reset), a later position continues from the states.  Calls of 16 tokens
+    or more run the chunked prefill kernel, shorter ones the recurrent kernel.
     """
 
     def __init__(self, hidden_size=2048, num_k_heads=16, num_v_heads=32, head_k_dim=128, head_v_dim=128,
@@ -295,16 +298,20 @@ class GatedDeltaNet(nn.Module):
                           dtype=torch.float32)
         return conv, rec
 
-    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states):
-        """Everything between the input and output projections (the hot path)."""
+    CHUNKED_MIN_TOKENS = 16  # calls with at least this many tokens run the chunked prefill kernel
+
+    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos=0):
+        """Everything between the input and output projections (the hot path).  Returns the core
+        output (fp32) and the gated-normed output (activation dtype)."""
         B, T, _ = mixed_qkv.shape
-        if not use_precomputed_states:
+        cont = _position(current_pos) > 0
+        if not cont:
             recurrent_state.zero_()
         q, k, v, g, beta = gdn_prologue(mixed_qkv, self.conv_weight, conv_state, a, b, self.A_log, self.dt_bias,
                                         self.num_k_heads,
                                         self.num_v_heads, self.head_k_dim, self.head_v_dim,
-                                        use_state=use_precomputed_states, out_dtype=self.core_dtype)
-        if T > 1 and not use_precomputed_states:
+                                        use_state=cont, out_dtype=self.core_dtype)
+        if T >= self.CHUNKED_MIN_TOKENS:
             o = chunk_gated_delta_rule_(q, k, v, g, beta, recurrent_state, chunk_size=self.chunk_size,
                                         out_dtype=torch.float32)
         else:
@@ -313,11 +320,20 @@ class GatedDeltaNet(nn.Module):
                                self.eps, out_dtype=mixed_qkv.dtype)
         return o, normed
 
-    def forward(self, hidden_states, conv_state, recurrent_state, use_precomputed_states=False):
+    def forward(self, hidden_states, current_pos, conv_state, recurrent_state):
         B, T, _ = hidden_states.shape
         proj = F.linear(hidden_states, self.w_in)  # [B, T, conv_dim + value_dim + 2 H_v]
         c, v = self.conv_dim, self.value_dim
         mixed_qkv, z = proj[..., :c], proj[..., c:c + v]
         b, a = proj[..., c + v:c + v + self.num_v_heads], proj[..., c + v + self.num_v_heads:]
-        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, use_precomputed_states)
+        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos)
         return F.linear(normed.reshape(B, T, self.value_dim), self.out_proj.weight)
+
+
+def _position(current_pos) -> int:
+    """``current_pos`` as an int: the reference passes positions as one-element int tensors."""
+    if isinstance(current_pos, torch.Tensor):
+        if current_pos.numel() != 1:
+            raise ValueError("current_pos must hold one position")
+        return int(current_pos.reshape(()).item())
+    return int(current_pos)

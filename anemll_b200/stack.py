@@ -214,7 +214,7 @@ class HybridStack(nn.Module):
         m = self.mixers[i]
         if isinstance(m, GatedAttention):
             return m(h, state[0], state[1], pos, self.cos, self.sin)
-        return m(h, state[0], state[1], use_precomputed_states=pos > 0)
+        return m(h, pos, state[0], state[1])
 
     def mlp(self, i, h):
         return F.linear(silu_mul(F.linear(h, self.gate_up[i].weight)), self.down[i].weight)

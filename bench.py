@@ -9,6 +9,11 @@ its own batch of 64 sequences; no collective on the data path.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer|cache_ops|stack]
 
+Without ``--config`` the decode line also carries, as secondary lines, the
+chunked prefill (8 x 32768 tokens, the tensor-core kernel) and the KV-cache
+attention pass (causal and with a 512-token window), each with its own
+roofline, e2e leg and CPU baseline.  ``--config X`` prints X's line alone.
+
 ``--impl reference`` times the CPU oracle of the same path on the host cores
 (the reference has no GPU implementation of this path), rank 0 only.
 """
@@ -164,12 +169,22 @@ def cpu_decode_sample(n_steps, threads):
     return n_steps / dt
 
 
+def decode_config(ws):
+    return {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
+            "d_k": DK, "d_v": DV, "state_bytes": DECODE_B * H_V * DK * DV * 4, "tokens_cycled": DECODE_STEPS,
+            "l2": "no flush: two batch-64 states (2 x 128 MiB) alternate step by step, so no step reads "
+                  "state the previous one left in the 126 MB L2",
+            "parallelism": f"weak, {ws} independent batch shards"}
+
+
 def bench_gdn_decode(args, ws, rank, local):
     from anemll_b200 import _lib, gdn, inputs
     dev = torch.device("cuda", local)
     from anemll_b200 import shard
     w = inputs.gdn_decode(seed=shard.decode_seed(1, rank), B=DECODE_B, steps=DECODE_STEPS)
-    state = w["state"].to(dev)
+    # two batches' states alternate step by step, so no step reads state that the previous step left in
+    # the 126 MB L2 (one state is 128 MiB, but L2 still holds the tail the previous step wrote)
+    states = [w["state"].to(dev), w["state"].to(dev)]
     q, k, v, g, beta = (w[n].to(dev) for n in ("q", "k", "v", "g", "beta"))
     out = torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
@@ -178,11 +193,11 @@ def bench_gdn_decode(args, ws, rank, local):
     # pre-resolved raw pointers: the timed loop is one C call per step
     ptrs = [(_lib.ptr(q[t]), _lib.ptr(k[t]), _lib.ptr(v[t]), _lib.ptr(g[t]), _lib.ptr(beta[t]))
             for t in range(DECODE_STEPS)]
-    sptr, optr = _lib.ptr(state), _lib.ptr(out)
+    sptrs, optr = [_lib.ptr(x) for x in states], _lib.ptr(out)
 
     def step(i):
         pq, pk, pv, pg, pb = ptrs[i % DECODE_STEPS]
-        rc = lib.anemll_gdn_recurrent(pq, pk, pv, _lib.BF16, pg, pb, sptr, optr, _lib.BF16,
+        rc = lib.anemll_gdn_recurrent(pq, pk, pv, _lib.BF16, pg, pb, sptrs[i & 1], optr, _lib.BF16,
                                       DECODE_B, 1, H_QK, H_V, DK, DV, 0.0, 0, sp)
         if rc:
             _lib.check(rc, "anemll_gdn_recurrent")
@@ -219,7 +234,7 @@ def bench_gdn_decode(args, ws, rank, local):
         dv_.copy_(hv[t], non_blocking=True)
         dg.copy_(hg[t], non_blocking=True)
         db.copy_(hb[t], non_blocking=True)
-        gdn.recurrent_gated_delta_rule_(dq, dk_, dv_, dg, db, state, out=out)
+        gdn.recurrent_gated_delta_rule_(dq, dk_, dv_, dg, db, states[i & 1], out=out)
         hout.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -250,14 +265,15 @@ def bench_gdn_decode(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "f32 state, bf16 q/k/v/out",
         "data": "synthetic (seeded; state ~N(0,0.01), q/k l2-normalised N(0,1), v ~N(0,1))",
-        "config": {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
-                   "d_k": DK, "d_v": DV, "state_bytes": DECODE_B * H_V * DK * DV * 4,
-                   "tokens_cycled": DECODE_STEPS, "l2": "no flush: the 128 MiB state exceeds the 126 MB L2",
-                   "parallelism": f"weak, {ws} independent batch shards"},
+        "config": decode_config(ws),
         "tokens_per_s": ws * args.steps * DECODE_B / (ms_max / 1e3),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "peak_source": how,
-                     "algorithmic_bytes_per_launch": decode_bytes_per_step(), "traffic": None},
+                     "algorithmic_bytes_per_launch": decode_bytes_per_step(),
+                     # ncu DRAM bytes (read + write) of one launch; the write-back of part of a step's
+                     # state is deferred into the next launch, so a lone launch shows less than it moves
+                     # in steady state
+                     "traffic": traffic_from_profiles("gdn_recurrent_decode")},
         "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
@@ -268,6 +284,13 @@ def bench_gdn_decode(args, ws, rank, local):
 
 PREFILL_B, PREFILL_T, CHUNK = 8, 32768, 64
 PREFILL_FLOP_PER_TOKEN_HEAD = (2 * CHUNK * CHUNK * (3 * DK + 2 * DV) + 6 * CHUNK * DK * DV) // CHUNK  # 180,224
+
+
+def prefill_config(ws, nseq=PREFILL_B, seqlen=PREFILL_T):
+    return {"workload": "gdn_chunked_prefill", "batch": nseq, "seq_len": seqlen, "chunk": CHUNK,
+            "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV,
+            "l2": "no flush: 4.3 GB of inputs per step exceed the 126 MB L2",
+            "parallelism": f"{ws} ranks, sequences x value heads, no collective"}
 
 
 def bench_gdn_prefill(args, ws, rank, local):
@@ -349,10 +372,7 @@ def bench_gdn_prefill(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "bf16 (inputs as tensor-core operands; derived operands split hi+lo), f32 accumulate/state, bf16 in/out",
         "data": "synthetic (seeded on device; q/k l2-normalised N(0,1), v ~N(0,1))",
-        "config": {"workload": "gdn_chunked_prefill", "batch": nseq, "seq_len": seqlen, "chunk": CHUNK,
-                   "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV,
-                   "l2": "no flush: 4.3 GB of inputs per step exceed the 126 MB L2",
-                   "parallelism": f"{ws} ranks, sequences x value heads, no collective"},
+        "config": prefill_config(ws, nseq, seqlen),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / pk["bf16_tflops"], "peak_source": how,
                      "algorithmic_flop_per_launch": flop_launch,
@@ -364,6 +384,14 @@ def bench_gdn_prefill(args, ws, rank, local):
         "gpu_launches": args.steps,
         "clocks": clk.summary(),
     }
+
+
+def kv_config(ws, window):
+    return {"workload": "kv_cache_attention", "H_q": 16, "H_kv": 2, "head_dim": 256, "ctx": 4096,
+            "prefill_chunks": 31, "chunk": 64, "decode_steps": 64, "window": window,
+            "l2": "flushed (256 MB write) before the prefill chunks and before the decode steps of every timed "
+                  "pass; within a pass the one-layer cache (8 MiB) stays L2-resident",
+            "parallelism": f"{ws} ranks: kv heads split over up to 2, replicas beyond"}
 
 
 def bench_kv_attention(args, ws, rank, local):
@@ -496,10 +524,7 @@ def bench_kv_attention(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded; cache prefilled N(0,1) at 0..2047)",
-        "config": {"workload": "kv_cache_attention", "H_q": 16, "H_kv": 2, "head_dim": 256, "ctx": 4096,
-                   "prefill_chunks": len(calls), "chunk": 64, "decode_steps": len(dec), "window": window,
-                   "l2": "flushed (256 MB write) before the prefill chunks and before the decode steps of every timed pass; within a pass the one-layer cache (8 MiB) stays L2-resident",
-                   "parallelism": f"{ws} ranks, kv heads {kv0}..{kv0 + nkv - 1}"},
+        "config": kv_config(ws, window),
         "prefill_us_per_chunk": pre_ms_max / args.steps / len(calls) * 1e3,
         "decode_us_per_step": dec_ms_max / args.steps / len(dec) * 1e3,
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -559,10 +584,10 @@ def bench_gdn_layer(args, ws, rank, local):
     x_dec = [h[:, LAYER_PREFILL + i:LAYER_PREFILL + i + 1].contiguous() for i in range(LAYER_DECODE)]
 
     def run_pre():
-        return layer(x_pre, conv, rec, use_precomputed_states=False)
+        return layer(x_pre, 0, conv, rec)
 
     def run_dec():
-        return [layer(x, conv, rec, use_precomputed_states=True) for x in x_dec]
+        return [layer(x, LAYER_PREFILL + i, conv, rec) for i, x in enumerate(x_dec)]
 
     from anemll_b200 import _lib
     with torch.no_grad():
@@ -611,11 +636,11 @@ def bench_gdn_layer(args, ws, rank, local):
 
     def e2e_pass():
         dx.copy_(hx, non_blocking=True)
-        ya = layer(dx[:, :LAYER_PREFILL], conv, rec, use_precomputed_states=False)
+        ya = layer(dx[:, :LAYER_PREFILL], 0, conv, rec)
         hy[:, :LAYER_PREFILL].copy_(ya, non_blocking=True)
         for i in range(LAYER_DECODE):
             t = LAYER_PREFILL + i
-            yb = layer(dx[:, t:t + 1], conv, rec, use_precomputed_states=True)
+            yb = layer(dx[:, t:t + 1], t, conv, rec)
             hy[:, t:t + 1].copy_(yb, non_blocking=True)
 
     with torch.no_grad():
@@ -1092,64 +1117,83 @@ def traffic_from_profiles(name):
     return None
 
 
-def reference_arm(args, ws, rank):
-    """The CPU path (the oracle port: the reference has no implementation of this path) on the host cores,
-    on the same config, metric and unit as our arm; rank 0 only."""
-    if rank != 0:
-        return None
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    if args.config == "gdn_decode":
-        from anemll_b200 import inputs
-        from oracle import gdn as og
-        w = inputs.gdn_decode(B=DECODE_B, steps=DECODE_STEPS)
-        S = w["state"]
-        for i in range(args.warmup):
-            t = i % DECODE_STEPS
-            _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            t = i % DECODE_STEPS
-            _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
-        dt = time.perf_counter() - t0
-        v, unit, metric, ms = args.steps / dt, "steps/s", "gdn_decode_steps_per_s", dt * 1e3 / args.steps
-        sample = f"{args.steps} full-batch decode steps of the fp32 torch CPU oracle"
-        config = {"workload": "gdn_recurrent_decode", "batch_per_gpu": DECODE_B, "H_qk": H_QK, "H_v": H_V,
-                  "d_k": DK, "d_v": DV}
-        scaling = "weak"
-    else:
-        vals = []
-        for _ in range(max(1, min(args.steps, 3))):
-            if args.config == "gdn_prefill":
-                v1, sample = cpu_prefill_sample(threads)
-            elif args.config == "kv_attention":
-                v1, sample = cpu_kv_sample(threads, args.window)
-            elif args.config == "cache_ops":
-                v1, sample = cpu_cache_ops_sample(threads)
-            elif args.config == "stack":
-                v1, sample = cpu_stack_sample(threads)
-            else:
-                v1, sample = cpu_layer_sample(threads)
-            vals.append(v1)
-        if args.config == "cache_ops":
-            v, unit = max(vals), "GB/s"
-            ms = CPU_CACHE_STEP_BYTES / (v * 1e9) * 1e3  # one step = one sample
+SUB_KEYS = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "scaling", "dtype", "config", "roofline",
+            "e2e", "gpu_launches", "clocks", "cpu_baseline", "prefill_us_per_chunk", "decode_us_per_step")
+
+
+def sub_args(args, steps, warmup):
+    """The argument set of a secondary line of the default run: its own step counts, capped by the run's."""
+    a = argparse.Namespace(**vars(args))
+    a.steps = max(3, min(args.steps, steps))
+    a.warmup = max(3, min(args.warmup, warmup))
+    return a
+
+
+def cpu_line(config, threads, window=0, steps=3):
+    """The CPU oracle port of one config on the host cores: (value, unit, ms per step, sample)."""
+    vals = []
+    for _ in range(max(1, min(steps, 3))):
+        if config == "gdn_prefill":
+            v1, sample = cpu_prefill_sample(threads)
+        elif config == "kv_attention":
+            v1, sample = cpu_kv_sample(threads, window)
+        elif config == "cache_ops":
+            v1, sample = cpu_cache_ops_sample(threads)
+        elif config == "stack":
+            v1, sample = cpu_stack_sample(threads)
         else:
-            sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8,
-                             "stack": 66}[args.config]
-            v, unit = max(vals), "tokens/s"
-            ms = sample_tokens / v * 1e3  # one step = one bounded sample
-        metric = {"gdn_prefill": "gdn_prefill_tokens_per_s", "kv_attention": "kv_attention_tokens_per_s",
-                  "gdn_layer": "gdn_layer_tokens_per_s", "cache_ops": "kv_cache_ops_bytes_per_s",
-                  "stack": "stack_tokens_per_s"}[args.config]
-        config = {"workload": {"gdn_prefill": "gdn_chunked_prefill", "kv_attention": "kv_cache_attention",
-                               "gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops",
-                               "stack": "hybrid_stack"}[args.config], "sample": sample}
-        scaling = "strong" if args.config in ("gdn_prefill", "kv_attention", "stack") else "weak"
-        sample = sample + f", best of {len(vals)}"
+            v1, sample = cpu_layer_sample(threads)
+        vals.append(v1)
+    if config == "cache_ops":
+        v, unit = max(vals), "GB/s"
+        ms = CPU_CACHE_STEP_BYTES / (v * 1e9) * 1e3  # one step = one sample
+    else:
+        sample_tokens = {"gdn_prefill": 2048, "kv_attention": 4 * 64 + 8, "gdn_layer": LAYER_PREFILL + 8,
+                         "stack": 66}[config]
+        v, unit = max(vals), "tokens/s"
+        ms = sample_tokens / v * 1e3  # one step = one bounded sample
+    return v, unit, ms, sample + f", best of {len(vals)}"
+
+
+def cpu_decode_line(threads, steps, warmup):
+    from anemll_b200 import inputs
+    from oracle import gdn as og
+    w = inputs.gdn_decode(B=DECODE_B, steps=DECODE_STEPS)
+    S = w["state"]
+    for i in range(warmup):
+        t = i % DECODE_STEPS
+        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        t = i % DECODE_STEPS
+        _, S = og.recurrent_gated_delta_rule(w["q"][t], w["k"][t], w["v"][t], w["g"][t], w["beta"][t], S)
+    dt = time.perf_counter() - t0
+    return steps / dt, "steps/s", dt * 1e3 / steps, f"{steps} full-batch decode steps of the fp32 torch CPU oracle"
+
+
+METRICS = {"gdn_decode": "gdn_decode_steps_per_s", "gdn_prefill": "gdn_prefill_tokens_per_s",
+           "kv_attention": "kv_attention_tokens_per_s", "gdn_layer": "gdn_layer_tokens_per_s",
+           "cache_ops": "kv_cache_ops_bytes_per_s", "stack": "stack_tokens_per_s"}
+
+
+def reference_config(config, ws, window):
+    if config == "gdn_decode":
+        return decode_config(ws)
+    if config == "gdn_prefill":
+        return prefill_config(ws)
+    if config == "kv_attention":
+        return kv_config(ws, window)
+    return {"workload": {"gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops", "stack": "hybrid_stack"}[config]}
+
+
+def reference_line(config, args, ws, threads, window=0):
+    if config == "gdn_decode":
+        v, unit, ms, sample = cpu_decode_line(threads, args.steps, args.warmup)
+    else:
+        v, unit, ms, sample = cpu_line(config, threads, window, args.steps)
     return {
         "impl": "reference",
-        "metric": metric,
+        "metric": METRICS[config],
         "value": v,
         "unit": unit,
         "n_gpus": ws,
@@ -1157,14 +1201,62 @@ def reference_arm(args, ws, rank):
         "warmup": args.warmup,
         "ms_per_step": ms,
         "higher_is_better": True,
-        "scaling": scaling,
+        "scaling": "weak" if config in ("gdn_decode", "gdn_layer", "cache_ops") else "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded)",
-        "config": config,
+        "config": reference_config(config, ws, window),
         "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def reference_arm(args, ws, rank):
+    """The CPU path (the oracle port: the reference has no implementation of this path) on the host cores,
+    on the same config, metric and unit as our arm; rank 0 only.  The default run also times the chunked
+    prefill and the KV attention (causal and windowed) samples, as secondary lines."""
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    res = reference_line(args.config, args, ws, threads, args.window)
+    if args.default_run:
+        for key, cfg, window in SECONDARY:
+            sub = reference_line(cfg, sub_args(args, 3, 3), ws, threads, window)
+            res[key] = {k: sub[k] for k in SUB_KEYS if k in sub}
+    return res
+
+
+# the secondary lines of the default run: (key, config, window, steps, warmup)
+SECONDARY = (("prefill", "gdn_prefill", 0), ("kv_attention", "kv_attention", 0),
+             ("kv_attention_window", "kv_attention", 512))
+SECONDARY_STEPS = {"gdn_prefill": (20, 5), "kv_attention": (50, 5)}
+
+
+def cpu_baseline_for(config, args, threads, window=0):
+    if config == "gdn_decode":
+        v = cpu_decode_sample(args.cpu_baseline_steps, threads)
+        return {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
+                "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode steps of the fp32 torch CPU oracle"}
+    if config == "cache_ops":
+        v, sample = cpu_cache_ops_sample(threads)
+        return {"value": v, "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample}
+    v, sample = {"gdn_prefill": lambda: cpu_prefill_sample(threads),
+                 "kv_attention": lambda: cpu_kv_sample(threads, window),
+                 "gdn_layer": lambda: cpu_layer_sample(threads),
+                 "stack": lambda: cpu_stack_sample(threads)}[config]()
+    return {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample}
+
+
+def run_ours(config, args, ws, rank, local):
+    fn = {"kv_attention": bench_kv_attention, "gdn_prefill": bench_gdn_prefill, "gdn_layer": bench_gdn_layer,
+          "cache_ops": bench_cache_ops, "stack": bench_stack, "gdn_decode": bench_gdn_decode}[config]
+    res = fn(args, ws, rank, local)
+    if rank == 0:
+        res["cpu_baseline"] = None
+        if ws == 1:  # the host sample runs at N=1 only
+            res["cpu_baseline"] = cpu_baseline_for(config, args, os.cpu_count() or 1, args.window)
+    return res
 
 
 def main():
@@ -1173,8 +1265,10 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="default 2560 (stack: 3)")
     ap.add_argument("--warmup", type=int, default=None, help="default 32 (stack: 3)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="gdn_decode",
-                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer", "cache_ops", "stack"])
+    ap.add_argument("--config", default=None,
+                    choices=["gdn_decode", "gdn_prefill", "kv_attention", "gdn_layer", "cache_ops", "stack"],
+                    help="one workload's line alone; without it: the decode line carrying the prefill and KV "
+                         "attention lines")
     ap.add_argument("--window", type=int, default=0, help="kv_attention: sliding window (0 = causal)")
     ap.add_argument("--cpu-baseline-steps", type=int, default=8)
     ap.add_argument("--prefill-seqs", type=int, default=PREFILL_B, help="gdn_prefill: sequences (profiling cases)")
@@ -1183,6 +1277,9 @@ def main():
     ap.add_argument("--stack-prefill", type=int, default=STACK_PREFILL, help="stack: prompt tokens")
     ap.add_argument("--stack-decode", type=int, default=STACK_DECODE, help="stack: greedy decode steps")
     args = ap.parse_args()
+    args.default_run = args.config is None
+    if args.default_run:
+        args.config = "gdn_decode"
     if args.steps is None:
         args.steps = 3 if args.config == "stack" else 2560
     if args.warmup is None:
@@ -1193,39 +1290,18 @@ def main():
         if args.impl == "reference":
             res = reference_arm(args, ws, rank)
         else:
-            if args.config == "kv_attention":
-                res = bench_kv_attention(args, ws, rank, local)
-            elif args.config == "gdn_prefill":
-                res = bench_gdn_prefill(args, ws, rank, local)
-            elif args.config == "gdn_layer":
-                res = bench_gdn_layer(args, ws, rank, local)
-            elif args.config == "cache_ops":
-                res = bench_cache_ops(args, ws, rank, local)
-            elif args.config == "stack":
-                res = bench_stack(args, ws, rank, local)
-            else:
-                res = bench_gdn_decode(args, ws, rank, local)
-                res["roofline"]["traffic"] = traffic_from_profiles("gdn_recurrent_decode")
-            if rank == 0:
-                res["cpu_baseline"] = None
-                if ws == 1:  # the host sample runs at N=1 only
-                    threads = os.cpu_count() or 1
-                    if args.config == "cache_ops":
-                        v, sample = cpu_cache_ops_sample(threads)
-                        res["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
-                                               "sample": sample}
-                    elif args.config == "gdn_decode":
-                        v = cpu_decode_sample(args.cpu_baseline_steps, threads)
-                        res["cpu_baseline"] = {"value": v, "unit": "steps/s", "cores": threads, "kind": "port",
-                                               "sample": f"{args.cpu_baseline_steps} full-batch (B=64) decode "
-                                                         "steps of the fp32 torch CPU oracle"}
-                    else:
-                        v, sample = {"gdn_prefill": lambda: cpu_prefill_sample(threads),
-                                     "kv_attention": lambda: cpu_kv_sample(threads, args.window),
-                                     "gdn_layer": lambda: cpu_layer_sample(threads),
-                                     "stack": lambda: cpu_stack_sample(threads)}[args.config]()
-                        res["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                                               "sample": sample}
+            res = run_ours(args.config, args, ws, rank, local)
+            if args.default_run:  # the other hot-path kernels as secondary lines
+                for key, cfg, window in SECONDARY:
+                    sa = sub_args(args, *SECONDARY_STEPS[cfg])
+                    sa.window = window
+                    sub = run_ours(cfg, sa, ws, rank, local)
+                    if rank == 0:
+                        res[key] = {k: sub[k] for k in SUB_KEYS if k in sub}
+                    torch.cuda.empty_cache()
+                if rank == 0:
+                    res["gpu_launches_all_lines"] = res["gpu_launches"] + sum(res[k]["gpu_launches"]
+                                                                              for k, _, _ in SECONDARY)
         if rank == 0 and res is not None:
             print(json.dumps(res), flush=True)
     finally:

@@ -39,20 +39,34 @@ def _w(p):
     return p.detach().float().cpu()
 
 
-def attention_layer(m, cfg, h, kc, vc, pos, cos, sin):
-    """h [B, T, hidden] (bf16-valued fp32) -> o_proj output; kc/vc [B, H_kv, ctx, hd] fp32, updated."""
-    B, T, _ = h.shape
-    qg = bf(F.linear(h, _w(m.q_proj.weight))).view(B, T, cfg.H_q, 2 * cfg.head_dim)
+def attention_core(m, cfg, qkv, kc, vc, pos, cos, sin, with_k=False):
+    """The attention call of a gated full-attention layer on its fused projection output ``qkv``
+    [B, T, H_q*2*hd + 2*H_kv*hd] (per query head ``[query | gate]``, then k, then v; bf16-valued fp32):
+    per-head RMSNorm of q and k, RoPE, the cache write into ``kc``/``vc`` [B, H_kv, ctx, hd] (fp32,
+    updated in place), attention over the cache with the causal mask and the sigmoid gate.  Returns
+    the gated output [B, T, H_q*hd] in fp32, before its bf16 rounding and ``o_proj`` (and with
+    ``with_k`` the new K rows [B, H_kv, T, hd] before their bf16 rounding)."""
+    B, T, _ = qkv.shape
+    n_q, n_kv = cfg.H_q * 2 * cfg.head_dim, cfg.H_kv * cfg.head_dim
+    qg = qkv[..., :n_q].reshape(B, T, cfg.H_q, 2 * cfg.head_dim)
     q, gate = qg[..., :cfg.head_dim], qg[..., cfg.head_dim:]
-    k = bf(F.linear(h, _w(m.k_proj.weight))).view(B, T, cfg.H_kv, cfg.head_dim)
-    v = bf(F.linear(h, _w(m.v_proj.weight))).view(B, T, cfg.H_kv, cfg.head_dim)
+    k = qkv[..., n_q:n_q + n_kv].reshape(B, T, cfg.H_kv, cfg.head_dim)
+    v = qkv[..., n_q + n_kv:].reshape(B, T, cfg.H_kv, cfg.head_dim)
     q = bf(rms_norm(q, _w(m.q_norm), cfg.eps)).transpose(1, 2)
     k = bf(rms_norm(k, _w(m.k_norm), cfg.eps)).transpose(1, 2)
     q = bf(rope(q, cos, sin))
-    k = bf(rope(k, cos, sin))
-    kc[:, :, pos:pos + T] = k
+    k_f = rope(k, cos, sin)
+    kc[:, :, pos:pos + T] = bf(k_f)
     vc[:, :, pos:pos + T] = v.transpose(1, 2)
     o = ok.attend(q, kc, vc, ok.additive_mask(T, cfg.ctx, pos), gate.reshape(B, T, -1))
+    return (o, k_f) if with_k else o
+
+
+def attention_layer(m, cfg, h, kc, vc, pos, cos, sin):
+    """h [B, T, hidden] (bf16-valued fp32) -> o_proj output; kc/vc [B, H_kv, ctx, hd] fp32, updated."""
+    qkv = bf(torch.cat([F.linear(h, _w(m.q_proj.weight)), F.linear(h, _w(m.k_proj.weight)),
+                        F.linear(h, _w(m.v_proj.weight))], dim=-1))
+    o = attention_core(m, cfg, qkv, kc, vc, pos, cos, sin)
     return bf(F.linear(bf(o), _w(m.o_proj.weight)))
 
 
@@ -91,6 +105,19 @@ def layer(model, i, x, state, pos, with_mixer=False):
     gate, up = gu.chunk(2, dim=-1)
     y = bf(x + bf(F.linear(bf(bf(F.silu(gate)) * up), _w(model.down[i].weight))))
     return (y, h) if with_mixer else y
+
+
+def host_model(model):
+    """An fp32 copy of a device ``HybridStack`` on the host (built once; the layer functions above then
+    read its weights without device copies)."""
+    from anemll_b200.stack import HybridStack
+    host = HybridStack(model.cfg, device="meta", dtype=torch.float32).to_empty(device="cpu")
+    with torch.no_grad():
+        src = dict(model.named_parameters())
+        for name, p in host.named_parameters():
+            p.copy_(src[name].detach().float().cpu())
+    host.cos, host.sin = model.cos.cpu(), model.sin.cpu()
+    return host
 
 
 def new_state(model, B):

@@ -8,7 +8,8 @@ Sources of truth:
   whole attention path runs in fp32 on fp16-rounded inputs.
   ``QwenAttention.forward_prefill`` (509-546) and ``forward_regular`` (469-507)
   are called with ``o_proj`` set to the identity, so the recorded output is the
-  pre-projection attention output.  The cache write is recorded by running
+  pre-projection attention output; ``kv_attention_oproj.pt`` records the same
+  methods with a random ``o_proj``, i.e. the reference's full return value.  The cache write is recorded by running
   ``QwenModel.process_layer_prefill`` (647-696) / ``process_layer_regular``
   (698-839) on a tiny random model and capturing ``kv_cache_0`` before and after.
   Masks: ``tests/chat.py`` ``make_causal_mask`` (977-983) rule; sliding windows
@@ -196,6 +197,43 @@ def make_gdn():
     torch.save(dict(gdn=gdn, conv=conv_fx, norm=norm_fx), os.path.join(HERE, "gdn.pt"))
 
 
+def make_kv_oproj(ref_root):
+    """``kv_attention_oproj.pt``: the reference's ``QwenAttention.forward_prefill`` / ``forward_regular``
+    with a random ``o_proj`` (a 1x1 Conv2d from H_q*hd = 256 to hidden 320), so the drop-in module's
+    projected output is compared with exactly what the reference returns."""
+    sys.path.insert(0, ref_root)
+    import anemll.models.qwen_model as qm  # noqa: E402
+
+    qm.MODEL_DTYPE = torch.float32
+    torch.manual_seed(23)
+    Hq, Hkv, hd, ctx, hidden = 4, 2, 64, 256, 320
+    cfg = qm.QwenConfig(hidden_size=hidden, num_attention_heads=Hq, num_key_value_heads=Hkv,
+                        head_dim=hd, context_length=ctx, state_length=ctx, num_hidden_layers=1,
+                        intermediate_size=64, vocab_size=32)
+    attn = qm.QwenAttention(cfg)
+    with torch.no_grad():  # fp16-representable weights, so both sides project with the same values
+        attn.o_proj.weight.copy_(_r16(0.05 * torch.randn_like(attn.o_proj.weight)))
+    cases = []
+    for name, S, pos in [("prefill", 16, 100), ("decode", 1, 200)]:
+        K = torch.zeros(Hkv, ctx, hd)
+        V = torch.zeros(Hkv, ctx, hd)
+        K[:, :pos + S] = _r16(torch.randn(Hkv, pos + S, hd))
+        V[:, :pos + S] = _r16(torch.randn(Hkv, pos + S, hd))
+        q = _r16(torch.randn(1, Hq, S, hd))
+        mask = causal_mask_ref_rule(S, ctx, pos)
+        hs = torch.zeros(1, S, hidden)
+        with torch.no_grad():
+            if S == 1:
+                out = attn.forward_regular(hs, q, (K, V), mask, torch.tensor([pos]))
+            else:
+                out = attn.forward_prefill(hs, q, (K, V), mask)
+        cases.append(dict(name=name, S=S, pos=pos, q=q.half(), K=K[:, :pos + S].half(), V=V[:, :pos + S].half(),
+                          out=out.float()))
+    torch.save(dict(Hq=Hq, Hkv=Hkv, hd=hd, ctx=ctx, hidden=hidden,
+                    o_proj_weight=attn.o_proj.weight.detach().clone(), cases=cases),
+               os.path.join(HERE, "kv_attention_oproj.pt"))
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("ANEMLL_REFERENCE"),
@@ -203,6 +241,7 @@ if __name__ == "__main__":
                     help="checkout of the reference repository (or set ANEMLL_REFERENCE)")
     args = ap.parse_args()
     make_kv(args.reference)
+    make_kv_oproj(args.reference)
     make_gdn()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):

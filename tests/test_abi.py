@@ -6,6 +6,7 @@ import os
 import re
 
 import pytest
+import torch
 
 from anemll_b200 import _lib
 from tests.conftest import ROOT
@@ -72,3 +73,13 @@ def test_product_fails_loudly_without_cuda():
     q = torch.zeros(1, 1, 1, 128)
     with pytest.raises(RuntimeError):
         gdn.recurrent_gated_delta_rule(q, q, q, torch.zeros(1, 1, 1), torch.zeros(1, 1, 1))
+
+
+def test_torch_ops_are_registered_and_refuse_cpu_tensors():
+    import anemll_b200.ops  # noqa: F401  (registers torch.ops.anemll_b200.*)
+    for name in ("gdn_chunked_prefill", "gdn_recurrent", "gdn_prologue", "kv_attention"):
+        assert hasattr(torch.ops.anemll_b200, name)
+    z = torch.zeros(1, 1, 1, 128, dtype=torch.half)
+    with pytest.raises(NotImplementedError):
+        torch.ops.anemll_b200.gdn_recurrent(z, z, z, torch.zeros(1, 1, 1), torch.zeros(1, 1, 1),
+                                            torch.zeros(1, 1, 128, 128))

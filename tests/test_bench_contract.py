@@ -34,12 +34,22 @@ def _check_line(d, config):
     e2e = d["e2e"]
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    sys.path.insert(0, ROOT)
+    import bench
+    # the config dict is the one our arm prints for the same workload
+    assert d["config"] == bench.reference_config(config or "gdn_decode", d["n_gpus"], 0)
+    if config is None:  # the default run carries the prefill and KV attention lines too
+        for key, cfg, window in bench.SECONDARY:
+            sub = d[key]
+            assert sub["metric"] == bench.METRICS[cfg] and sub["value"] > 0 and sub["unit"] == "tokens/s"
+            assert sub["config"] == bench.reference_config(cfg, d["n_gpus"], window)
+            assert sub["cpu_baseline"]["value"] == sub["value"]
 
 
-@pytest.mark.parametrize("config", CONFIGS)
+@pytest.mark.parametrize("config", CONFIGS + [None])
 def test_reference_arm_prints_one_contract_line(config):
-    lines = _run([sys.executable, "bench.py", "--impl", "reference", "--config", config, "--steps", "1",
-                  "--warmup", "1"])
+    cfg_args = [] if config is None else ["--config", config]
+    lines = _run([sys.executable, "bench.py", "--impl", "reference", *cfg_args, "--steps", "1", "--warmup", "1"])
     assert len(lines) == 1
     _check_line(lines[0], config)
 

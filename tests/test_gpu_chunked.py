@@ -65,6 +65,19 @@ def test_full_head_shape_long_sequence():
     assert_close(st, rs, "state")
 
 
+@pytest.mark.parametrize("dtype,s0", [(torch.bfloat16, 0.0), (torch.float16, 0.01)])
+def test_long_prefill_full_sequence_matches_oracle(dtype, s0):
+    """One whole sequence of the long-prefill workload: 32768 tokens (512 chunks of state carry) with
+    all 32 value heads, seed 3, against the fp32 oracle.  bf16 inputs from a zero state (the
+    workload's own form), and fp16 inputs from a non-zero state (the gated-DeltaNet layer feeds the
+    kernel fp16 q/k/v)."""
+    q, k, v, g, beta, S0 = _case(1, 32768, 16, 32, 3, dtype=dtype, s0=s0)
+    o, st = _run(q, k, v, g, beta, S0)
+    ro, rs = og.chunk_gated_delta_rule(q, k, v, g, beta, 64, S0)
+    assert_close(o, ro, "out")
+    assert_close(st, rs, "state")
+
+
 def test_fp16_and_bf16_outputs():
     q, k, v, g, beta, S0 = _case(1, 256, 2, 4, 9, dtype=torch.float16, s0=0.01)
     ro, rs = og.chunk_gated_delta_rule(q, k, v, g, beta, 64, S0)

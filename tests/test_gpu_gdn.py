@@ -176,7 +176,7 @@ def test_gdn_layer_prefill_then_decode_matches_oracle():
         for step, (s, e) in enumerate([(0, 512)] + [(512 + i, 513 + i) for i in range(64)]):
             x = h[:, s:e]
             mixed, z, a, b = layer.in_proj_qkv(x), layer.in_proj_z(x), layer.in_proj_a(x), layer.in_proj_b(x)
-            o, normed = layer.core(mixed, z, a, b, conv_state, rec_state, use_precomputed_states=step > 0)
+            o, normed = layer.core(mixed, z, a, b, conv_state, rec_state, current_pos=0 if step == 0 else 512 + step - 1)
             if step == 0:
                 ro, rn, ref_conv, ref_state = og.gdn_layer_prefill(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), params,
                                                                    16, 32, 128, 128)
@@ -239,3 +239,27 @@ def test_prologue_and_gated_norm_read_projection_slices(T, use_state):
     n1 = gdn.gated_rmsnorm(o, zs.view(2, T, Hv, 128), nw, out_dtype=torch.bfloat16)
     n2 = gdn.gated_rmsnorm(o, zs.contiguous().view(2, T, Hv, 128), nw, out_dtype=torch.bfloat16)
     assert torch.equal(n1, n2)
+
+
+def test_layer_continues_a_prefill_from_its_states():
+    """``current_pos`` > 0 continues from the caller's states: a 512-token prefill split into calls at
+    positions 0 and 256 (chunk-aligned) gives bit for bit the core outputs, conv state and recurrent
+    state of one call; the position may be a one-element tensor, as the reference passes it."""
+    w, hidden = inputs.gdn_layer()
+    layer = gdn.GatedDeltaNet(dtype=torch.bfloat16, device=DEV)
+    with torch.no_grad():
+        layer.w_in.copy_(torch.cat([w["in_proj_qkv"], w["in_proj_z"], w["in_proj_b"], w["in_proj_a"]]))
+        layer.conv_weight.copy_(w["conv_w"])
+        layer.A_log.copy_(w["A_log"])
+        proj = F.linear(hidden[:, :512].to(DEV), layer.w_in)
+        c, v, H = layer.conv_dim, layer.value_dim, layer.num_v_heads
+        parts = lambda s, e: (proj[:, s:e, :c], proj[:, s:e, c:c + v], proj[:, s:e, c + v + H:],
+                              proj[:, s:e, c + v:c + v + H])
+        one = layer.new_states(1)
+        o1, n1 = layer.core(*parts(0, 512), *one, current_pos=0)
+        two = layer.new_states(1)
+        two[1].fill_(1.0)  # position 0 resets the recurrent state
+        oa, na = layer.core(*parts(0, 256), *two, current_pos=0)
+        ob, nb = layer.core(*parts(256, 512), *two, current_pos=torch.tensor([256], dtype=torch.int32))
+    assert torch.equal(torch.cat([oa, ob], 1), o1) and torch.equal(torch.cat([na, nb], 1), n1)
+    assert torch.equal(two[0], one[0]) and torch.equal(two[1], one[1])

@@ -41,6 +41,37 @@ def test_matches_reference_golden(gold, use_mask):
         assert_close(out.float(), c["out"], c["name"])
 
 
+@pytest.mark.parametrize("o_proj_form", ["conv2d", "weight"])
+def test_drop_in_module_returns_the_reference_projected_output(o_proj_form):
+    """The module built around the reference's own o_proj (a 1x1 Conv2d, or its weight) returns what
+    QwenAttention.forward_prefill / forward_regular return: o_proj(attention), [B, S, hidden]
+    (golden from the reference with a random o_proj), with the reference's own argument forms: the
+    additive causal mask and current_pos as a one-element tensor."""
+    fx = torch.load(os.path.join(GOLDEN, "kv_attention_oproj.pt"))
+    Hq, Hkv, hd, ctx, hidden = fx["Hq"], fx["Hkv"], fx["hd"], fx["ctx"], fx["hidden"]
+    conv = torch.nn.Conv2d(Hq * hd, hidden, 1, bias=False).to(DEV)
+    with torch.no_grad():
+        conv.weight.copy_(fx["o_proj_weight"])
+    att = attention.QwenAttentionB200(Hq, Hkv, hd, o_proj=conv if o_proj_form == "conv2d" else conv.weight)
+    for c in fx["cases"]:
+        S, pos = c["S"], c["pos"]
+        K = torch.zeros(Hkv, ctx, hd, dtype=torch.half)
+        V = torch.zeros(Hkv, ctx, hd, dtype=torch.half)
+        K[:, :pos + S] = c["K"]
+        V[:, :pos + S] = c["V"]
+        mask = ok.additive_mask(S, ctx, pos).half().to(DEV)
+        hs = torch.zeros(1, S, hidden, dtype=torch.half, device=DEV)
+        args = (hs, c["q"].to(DEV), (K.to(DEV), V.to(DEV)), mask)
+        if S == 1:
+            out = att.forward_regular(*args, torch.tensor([pos], dtype=torch.int32))
+        else:
+            out = att.forward_prefill(*args)
+        assert out.shape == (1, S, hidden)
+        assert_close(out.float(), c["out"], c["name"])
+        core = att.attention(c["q"].to(DEV), (K.to(DEV), V.to(DEV)), mask, pos)
+        assert torch.equal(att.project(core), out)
+
+
 def test_fused_cache_write_bit_exact_vs_reference():
     fx = torch.load(os.path.join(GOLDEN, "kv_cache_write.pt"))
     for w in fx["writes"]:

@@ -1,24 +1,186 @@
-"""The cfg4 hybrid stack, wired end to end on the device, layer by layer against the CPU oracle.
+"""The hybrid decoder stack at its full shape (24 layers: 18 gated-DeltaNet with H_qk 16 / H_v 32 /
+d 128 and 6 gated full attention with H_q 16 / H_kv 2 / hd 256; hidden 2048, SwiGLU 6144, vocab
+151936, context 4096, bf16, random N(0, 0.02) weights, seed 4) against the CPU oracle.
 
-A reduced width (hidden 512, 8 layers: 6 gated-DeltaNet + 2 gated full attention with the cfg2 head
-shape H_q 16 / H_kv 2 / hd 256, vocab 1000, ctx 512) keeps the fp32 oracle fast; the kernels are the
-same ones the full-size stack runs.  Each layer gets the device's own input (teacher forcing per
-layer), so errors do not compound: a 64-token prefill of 2 sequences, then 3 decode steps.
+Two kinds of check:
 
-Tolerances: every tensor the stack materialises is bf16, on both sides at the same points, so the two
-differ by single-ulp rounding flips (2^-8..2^-7 relative) wherever the fp32 values before rounding
-differ slightly (GEMM accumulation order, the core's fp16 q/k/v); compounded through a layer that is a
-relative L2 difference of a few 1e-3.  The mixer output is compared on its own (a wiring error there
-is an O(1) difference) as well as the layer output."""
+* Every library kernel on identical inputs, layer by layer (teacher forcing).  Each layer gets the
+  device's own input, and every op is fed the device's own tensors (its projection outputs, its
+  caches and recurrent states as they were before the op), so each comparison covers exactly one
+  op.  Ops with fp32 outputs (the gated-DeltaNet core output and recurrent state, the gated RMSNorm)
+  meet the parity bar: rel-L2 <= 1e-3 and max-abs <= 2e-3.  Conv states and untouched cache rows are
+  bit-exact.  Ops whose outputs are bf16 tensors (attention output, cache rows, RMSNorm, SwiGLU) are
+  compared with the fp32 oracle value before its bf16 rounding: such an output cannot come closer
+  than its own rounding (about 1.1e-3 relative L2), so the bar applies beyond that floor
+  (``assert_bf16_close``).  The torch GEMMs between the ops are not the library's and are not checked.
+* The greedy token ids of the whole stack: the device generates, the oracle is run over the
+  device's ids (teacher forcing) and its argmax at every position is compared with the device's
+  pick.  With random weights and a 151936-word vocabulary the top two logits are sometimes closer
+  than bf16 rounding, so the agreement rate is reported and held above 90%, not required to be 1.
+"""
 import pytest
 import torch
+import torch.nn.functional as F
 
+from oracle import gdn as og
 from oracle import stack as ost
-from tests.tolerance import assert_close
+from tests.tolerance import assert_close, errors
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-RTOL, ATOL = 1e-2, 6e-2  # relative L2, max abs: bf16 rounding flips (module docstring)
+SHARD_RTOL, SHARD_ATOL = 1e-2, 6e-2  # device against device, different GEMM shapes (see the test)
+
+
+def assert_bf16_close(got, want, what, rel_l2=1e-3, max_abs=2e-3):
+    """``got`` (bf16) against the fp32 oracle ``want``: within the bar beyond the error of rounding
+    ``want`` itself to bf16."""
+    want = want.float().cpu()
+    rel_f, abs_f = errors(want.bfloat16(), want)
+    rel, mx = errors(got, want)
+    assert torch.isfinite(got.float()).all(), f"{what}: non-finite values"
+    assert rel <= rel_f + rel_l2 and mx <= abs_f + max_abs, (
+        f"{what}: rel_l2={rel:.3e} (rounding floor {rel_f:.3e} + {rel_l2}) max_abs={mx:.3e} "
+        f"(floor {abs_f:.3e} + {max_abs})")
+
+
+_MODELS = {}
+
+
+def _full():
+    """The full-shape stack on the device and its fp32 host copy (built once per process)."""
+    if "dev" not in _MODELS:
+        from anemll_b200.stack import HybridStack, StackConfig
+        model = HybridStack(StackConfig(), device=DEV).init_weights(4)
+        _MODELS["dev"] = model
+        _MODELS["host"] = ost.host_model(model)
+    return _MODELS["dev"], _MODELS["host"]
+
+
+def _check_gdn(i, m, hm, cfg, h, state, pos, what):
+    """Layer i's gated-DeltaNet mixer: projection (torch), then the core kernels against the oracle
+    core on the same projection output and the same states.  Returns the mixer output."""
+    from anemll_b200 import gdn
+    B, T, _ = h.shape
+    proj = F.linear(h, m.w_in)
+    c, v = m.conv_dim, m.value_dim
+    mixed, z = proj[..., :c], proj[..., c:c + v]
+    b, a = proj[..., c + v:c + v + m.num_v_heads], proj[..., c + v + m.num_v_heads:]
+    conv0, rec0 = state[0].float().cpu(), state[1].cpu().clone()
+    o, normed = m.core(mixed, z, a, b, state[0], state[1], current_pos=pos)
+    params = dict(conv_w=hm.conv_weight.detach(), A_log=hm.A_log.detach(), dt_bias=hm.dt_bias.detach(),
+                  norm_w=hm.norm_weight.detach(), eps=m.eps)
+    args = (mixed.float().cpu(), z.float().cpu(), a.float().cpu(), b.float().cpu(), params, cfg.H_qk, cfg.H_v,
+            cfg.d_k, cfg.d_v)
+    if pos == 0:
+        ro, rn, rconv, rS = og.gdn_layer_prefill(*args)
+    else:
+        ro, rn, rconv, rS = og.gdn_layer_decode(*args, conv0, rec0)
+    assert_close(o, ro, f"{what} layer {i} gdn core out")
+    assert_close(state[1], rS, f"{what} layer {i} gdn recurrent state")
+    assert torch.equal(state[0].float().cpu(), rconv), f"{what} layer {i} conv state"
+    assert_bf16_close(normed, rn, f"{what} layer {i} gated norm (bf16 out)")
+    # the gated norm alone, fp32 out, on the device's own core output
+    zz = z.reshape(B, T, cfg.H_v, cfg.d_v)
+    n32 = gdn.gated_rmsnorm(o, zz, m.norm_weight, m.eps, out_dtype=torch.float32)
+    assert_close(n32, og.gated_rmsnorm(o.cpu(), zz.float().cpu(), hm.norm_weight.detach(), m.eps),
+                 f"{what} layer {i} gated norm (fp32 out)")
+    return F.linear(normed.reshape(B, T, -1), m.out_proj.weight)
+
+
+def _check_attention(i, m, hm, cfg, h, state, pos, cos, sin, what):
+    """Layer i's gated attention: fused q/k/v projection (torch), then the attention call with its
+    fused head norm, RoPE, cache write and gate against the oracle on the same projection output and
+    the same cache.  Returns the mixer output."""
+    from anemll_b200 import attention
+    B, T, _ = h.shape
+    qkv = F.linear(h, m.w_qkv)
+    kc0, vc0 = state[0].float().cpu(), state[1].float().cpu()
+    o = attention.kv_attention_qkv(qkv, m.q_norm, m.k_norm, cos, sin, cfg.eps, state[0], state[1], pos, cfg.H_q,
+                                   cfg.H_kv, cfg.head_dim)
+    assert o is not None, "the fused attention call declined a stack shape"
+    kc, vc = kc0.clone(), vc0.clone()
+    ro, rk = ost.attention_core(hm, cfg, qkv.float().cpu(), kc, vc, pos, cos[pos:pos + T].cpu(),
+                                sin[pos:pos + T].cpu(), with_k=True)
+    assert_bf16_close(o, ro, f"{what} layer {i} attention out")
+    new = slice(pos, pos + T)
+    assert_bf16_close(state[0][:, :, new], rk, f"{what} layer {i} new K rows")
+    assert torch.equal(state[1][:, :, new].float().cpu(), vc[:, :, new]), f"{what} layer {i} new V rows"
+    for dev_c, old in ((state[0], kc0), (state[1], vc0)):
+        assert torch.equal(dev_c[:, :, :pos].float().cpu(), old[:, :, :pos]), f"{what} layer {i} earlier rows"
+        assert torch.equal(dev_c[:, :, pos + T:].float().cpu(), old[:, :, pos + T:]), f"{what} layer {i} later rows"
+    return F.linear(o, m.o_proj.weight)
+
+
+def _check_layer(model, host, i, x, state, pos, what):
+    from anemll_b200.stack import rms_norm, silu_mul
+    cfg = model.cfg
+    h = rms_norm(x, model.norm1[i], cfg.eps)
+    assert_bf16_close(h, ost.rms_norm(x.float().cpu(), host.norm1[i].detach(), cfg.eps), f"{what} layer {i} rmsnorm")
+    if cfg.is_attention(i):
+        mix = _check_attention(i, model.mixers[i], host.mixers[i], cfg, h, state, pos, model.cos, model.sin, what)
+    else:
+        mix = _check_gdn(i, model.mixers[i], host.mixers[i], cfg, h, state, pos, what)
+    s, n2 = rms_norm(x, model.norm2[i], cfg.eps, residual=mix)
+    ref_s = ost.bf(x.float().cpu() + mix.float().cpu())
+    assert torch.equal(s.float().cpu(), ref_s), f"{what} layer {i} residual add"
+    assert_bf16_close(n2, ost.rms_norm(ref_s, host.norm2[i].detach(), cfg.eps), f"{what} layer {i} add + rmsnorm")
+    gu = F.linear(n2, model.gate_up[i].weight)
+    act = silu_mul(gu)
+    gate, up = gu.float().cpu().chunk(2, dim=-1)
+    assert_bf16_close(act, ost.bf(F.silu(gate)) * up, f"{what} layer {i} swiglu")
+    return s + F.linear(act, model.down[i].weight)
+
+
+@torch.no_grad()
+def test_every_kernel_matches_oracle_at_full_shape():
+    """Prefill of 2 x 64 tokens, then two decode steps, all 24 layers, every op on identical inputs."""
+    model, host = _full()
+    cfg = model.cfg
+    torch.manual_seed(4)
+    B, T = 2, 64
+    ids = torch.randint(0, cfg.vocab, (B, T)).to(DEV)
+    state = model.new_state(B)
+    x = model.embed(ids)
+    for i in range(cfg.n_layers):
+        x = _check_layer(model, host, i, x, state[i], 0, "prefill")
+    nxt = F.linear(_final_norm(model, x[:, -1]), model.lm_head.weight).argmax(-1)
+    for s in range(2):
+        x = model.embed(nxt[:, None])
+        for i in range(cfg.n_layers):
+            x = _check_layer(model, host, i, x, state[i], T + s, f"decode step {s}")
+        nxt = F.linear(_final_norm(model, x[:, -1]), model.lm_head.weight).argmax(-1)
+
+
+def _final_norm(model, x):
+    from anemll_b200.stack import rms_norm
+    return rms_norm(x.contiguous(), model.norm, model.cfg.eps)
+
+
+@torch.no_grad()
+def test_greedy_ids_agree_with_oracle_at_full_shape():
+    """4 sequences, a 64-token prompt and 16 greedy steps on the device (CUDA-graph decode); the
+    oracle runs the same 24 layers over the device's ids and picks its own argmax at every step."""
+    from anemll_b200.stack import GreedyDecoder
+    model, host = _full()
+    cfg = model.cfg
+    B, T, n = 4, 64, 16
+    prompt = torch.randint(0, cfg.vocab, (B, T), generator=torch.Generator().manual_seed(44))
+    ids = GreedyDecoder(model, B, graphs=True)(prompt.to(DEV), n).cpu()  # [B, n + 1]
+    state = ost.new_state(host, B)
+    agree, total = 0, 0
+    pos, x_ids = 0, prompt
+    for step in range(n + 1):
+        x = ost.bf(host.embed.weight.detach()[x_ids])
+        for i in range(cfg.n_layers):
+            x = ost.layer(host, i, x, state[i], pos)
+        logits = F.linear(ost.bf(ost.rms_norm(x[:, -1], host.norm.detach(), cfg.eps)), host.lm_head.weight.detach())
+        agree += int((logits.argmax(-1) == ids[:, step]).sum())
+        total += B
+        pos += x_ids.shape[1]
+        x_ids = ids[:, step:step + 1]  # teacher forcing: the device's pick feeds the next step
+    rate = agree / total
+    print(f"greedy id agreement with the oracle: {agree}/{total} = {rate:.3f}")
+    assert rate >= 0.9, f"greedy id agreement {rate:.3f}"
 
 
 def _small():
@@ -27,52 +189,13 @@ def _small():
     return HybridStack(cfg, device=DEV).init_weights(4)
 
 
-def test_stack_layers_match_oracle():
-    torch.manual_seed(0)
-    model = _small()
-    cfg = model.cfg
-    B, T = 2, 64
-    ids = torch.randint(0, cfg.vocab, (B, T))
-    state = model.new_state(B)
-    ostate = ost.new_state(model, B)
-    with torch.no_grad():
-        x = model.embed(ids.to(DEV))
-        for i in range(cfg.n_layers):
-            y, h = model.layer(i, x, state[i], 0, with_mixer=True)
-            ref, ref_h = ost.layer(model, i, x.float().cpu(), ostate[i], 0, with_mixer=True)
-            assert_close(h.float().cpu(), ref_h, f"prefill mixer {i}", rel_l2=RTOL, max_abs=ATOL)
-            assert_close(y.float().cpu(), ref, f"prefill layer {i}", rel_l2=RTOL, max_abs=ATOL)
-            x = y
-        nxt = model.lm_head(ost_norm(model, x[:, -1])).argmax(-1)
-        for s in range(3):
-            x = model.embed(nxt[:, None])
-            for i in range(cfg.n_layers):
-                y, h = model.layer(i, x, state[i], T + s, with_mixer=True)
-                ref, ref_h = ost.layer(model, i, x.float().cpu(), ostate[i], T + s, with_mixer=True)
-                assert_close(h.float().cpu(), ref_h, f"decode step {s} mixer {i}", rel_l2=RTOL, max_abs=ATOL)
-                assert_close(y.float().cpu(), ref, f"decode step {s} layer {i}", rel_l2=RTOL, max_abs=ATOL)
-                x = y
-            nxt = model.lm_head(ost_norm(model, x[:, -1])).argmax(-1)
-    for i, st in enumerate(state):  # caches: the rows written so far match, the rest is still zero
-        if cfg.is_attention(i):
-            for j in range(2):
-                assert_close(st[j][:, :, :T + 3].float().cpu(), ostate[i][j][:, :, :T + 3], f"cache {i}.{j}",
-                             rel_l2=RTOL, max_abs=ATOL)
-                assert not st[j][:, :, T + 3:].any()
-
-
-def ost_norm(model, x):
-    from anemll_b200.stack import rms_norm
-    return rms_norm(x, model.norm, model.cfg.eps)
-
-
 def test_generate_is_deterministic_and_shards_agree():
     """Greedy generation repeats token for token, and the CUDA-graph replay of the decode steps gives
     the eager run's tokens.  The multi-GPU split: every layer of two 2-sequence shards gives the
-    4-sequence run's output on the same input to bf16 rounding (prefill, then a decode step).  Whole
-    runs are not compared token for token: GEMM shapes change with the batch, the rounding flips
-    compound over the layers and the steps, and with random weights the top two logits of a
-    1000-word vocabulary are often within that distance, so greedy picks may differ."""
+    4-sequence run's output on the same input (prefill, then a decode step).  This compares the
+    device with itself: the torch GEMMs pick other kernels for the other batch shape, so their bf16
+    outputs differ by rounding flips that compound through a layer (hence the looser bar); the
+    library's own kernels give per-sequence results that do not depend on the batch."""
     from anemll_b200.stack import GreedyDecoder
     torch.manual_seed(1)
     model = _small()
@@ -85,15 +208,14 @@ def test_generate_is_deterministic_and_shards_agree():
     again = dec(ids, 6)  # replays
     assert torch.equal(first, full) and torch.equal(again, full)
     assert len(dec.graphs) == 6
-    # the split, layer by layer on the same inputs (the 4-sequence run's), prefill and one decode step
     sf, sa, sb = model.new_state(4), model.new_state(2), model.new_state(2)
     with torch.no_grad():
         for pos, x in ((0, model.embed(ids)), (32, model.embed(full[:, :1]))):
             for i in range(model.cfg.n_layers):
                 y = model.layer(i, x, sf[i], pos)
                 yh = torch.cat([model.layer(i, x[:2], sa[i], pos), model.layer(i, x[2:], sb[i], pos)])
-                assert_close(yh.float().cpu(), y.float().cpu(), f"shards at {pos}, layer {i}", rel_l2=RTOL,
-                             max_abs=ATOL)
+                assert_close(yh.float().cpu(), y.float().cpu(), f"shards at {pos}, layer {i}", rel_l2=SHARD_RTOL,
+                             max_abs=SHARD_ATOL)
                 x = y
 
 

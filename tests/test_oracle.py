@@ -92,6 +92,22 @@ def test_kv_attention_matches_reference(gold_kv):
         assert _rel(out, c["out"]) < 1e-5, c["name"]
 
 
+def test_kv_attention_with_o_proj_matches_reference():
+    """The oracle's attention followed by the fixture's o_proj weight reproduces the reference's
+    projected return value (``kv_attention_oproj.pt``)."""
+    fx = torch.load(os.path.join(GOLDEN, "kv_attention_oproj.pt"))
+    hd, ctx = fx["hd"], fx["ctx"]
+    w = fx["o_proj_weight"].reshape(fx["hidden"], -1)
+    for c in fx["cases"]:
+        S, pos = c["S"], c["pos"]
+        K = torch.zeros(1, fx["Hkv"], ctx, hd)
+        V = torch.zeros(1, fx["Hkv"], ctx, hd)
+        K[0, :, :pos + S] = c["K"].float()
+        V[0, :, :pos + S] = c["V"].float()
+        out = torch.nn.functional.linear(ok.attend(c["q"], K, V, ok.additive_mask(S, ctx, pos)), w)
+        assert _rel(out, c["out"]) < 1e-5, c["name"]
+
+
 def test_kv_cache_write_bit_exact(gold_write):
     for w in gold_write["writes"]:
         cache = w["before"].clone()
