@@ -32,15 +32,21 @@ SHARD_RTOL, SHARD_ATOL = 1e-2, 6e-2  # device against device, different GEMM sha
 
 
 def assert_bf16_close(got, want, what, rel_l2=1e-3, max_abs=2e-3):
-    """``got`` (bf16) against the fp32 oracle ``want``: within the bar beyond the error of rounding
-    ``want`` itself to bf16."""
+    """``got`` (bf16) against the fp32 oracle ``want``, within the bar beyond the rounding of the output
+    itself: rel-L2 at most the error of rounding ``want`` to bf16 plus ``rel_l2``; elementwise at most
+    one bf16 ulp of ``want`` plus ``max_abs`` (a value within the bar of the oracle may round to the
+    neighbouring bf16 number)."""
     want = want.float().cpu()
-    rel_f, abs_f = errors(want.bfloat16(), want)
-    rel, mx = errors(got, want)
-    assert torch.isfinite(got.float()).all(), f"{what}: non-finite values"
-    assert rel <= rel_f + rel_l2 and mx <= abs_f + max_abs, (
-        f"{what}: rel_l2={rel:.3e} (rounding floor {rel_f:.3e} + {rel_l2}) max_abs={mx:.3e} "
-        f"(floor {abs_f:.3e} + {max_abs})")
+    g = got.float().cpu()
+    assert torch.isfinite(g).all(), f"{what}: non-finite values"
+    rel_f, _ = errors(want.bfloat16(), want)
+    rel, _ = errors(g, want)
+    _, e = torch.frexp(want)
+    ulp = torch.ldexp(torch.ones_like(want), e - 8)  # |want| in [2^(e-1), 2^e): bf16 spacing 2^(e-8)
+    over = ((g - want).abs() - ulp - max_abs).max().item() if want.numel() else 0.0
+    assert rel <= rel_f + rel_l2 and over <= 0, (
+        f"{what}: rel_l2={rel:.3e} (rounding floor {rel_f:.3e} + {rel_l2}); worst element {over:.3e} beyond "
+        f"one ulp + {max_abs}")
 
 
 _MODELS = {}
@@ -78,12 +84,14 @@ def _check_gdn(i, m, hm, cfg, h, state, pos, what):
     assert_close(o, ro, f"{what} layer {i} gdn core out")
     assert_close(state[1], rS, f"{what} layer {i} gdn recurrent state")
     assert torch.equal(state[0].float().cpu(), rconv), f"{what} layer {i} conv state"
-    assert_bf16_close(normed, rn, f"{what} layer {i} gated norm (bf16 out)")
     # the gated norm alone, fp32 out, on the device's own core output
     zz = z.reshape(B, T, cfg.H_v, cfg.d_v)
     n32 = gdn.gated_rmsnorm(o, zz, m.norm_weight, m.eps, out_dtype=torch.float32)
-    assert_close(n32, og.gated_rmsnorm(o.cpu(), zz.float().cpu(), hm.norm_weight.detach(), m.eps),
-                 f"{what} layer {i} gated norm (fp32 out)")
+    rn_dev = og.gated_rmsnorm(o.cpu(), zz.float().cpu(), hm.norm_weight.detach(), m.eps)
+    assert_close(n32, rn_dev, f"{what} layer {i} gated norm (fp32 out)")
+    # the layer's bf16 output on the same input (against the oracle's own core output the norm would
+    # also scale the core's error by 1 / RMS of each row)
+    assert_bf16_close(normed, rn_dev, f"{what} layer {i} gated norm (bf16 out)")
     return F.linear(normed.reshape(B, T, -1), m.out_proj.weight)
 
 
@@ -158,29 +166,43 @@ def _final_norm(model, x):
 
 @torch.no_grad()
 def test_greedy_ids_agree_with_oracle_at_full_shape():
-    """4 sequences, a 64-token prompt and 16 greedy steps on the device (CUDA-graph decode); the
-    oracle runs the same 24 layers over the device's ids and picks its own argmax at every step."""
+    """4 sequences, a 64-token prompt and 16 greedy steps on the device (CUDA-graph decode).  The
+    device's logits at every step (eager, the same ids) pick the graph run's ids; the oracle runs the
+    same 24 layers over the device's ids (teacher forcing).  Reported: the id agreement rate and the
+    logits' relative L2 difference.  Required: every pick that differs from the oracle's argmax is a
+    near tie (the oracle's top logit beats the device's pick by no more than 4 standard deviations of
+    the device-oracle logit difference of that row), and the logits agree to the bf16 rounding of the
+    activations compounded over 24 layers (rel-L2 <= 0.1; about 5e-2 is seen).  Each kernel on its own
+    is held to the parity bar by the test above."""
     from anemll_b200.stack import GreedyDecoder
     model, host = _full()
     cfg = model.cfg
     B, T, n = 4, 64, 16
     prompt = torch.randint(0, cfg.vocab, (B, T), generator=torch.Generator().manual_seed(44))
     ids = GreedyDecoder(model, B, graphs=True)(prompt.to(DEV), n).cpu()  # [B, n + 1]
-    state = ost.new_state(host, B)
-    agree, total = 0, 0
+    dstate = model.new_state(B)
+    ostate = ost.new_state(host, B)
+    agree, total, worst_rel = 0, 0, 0.0
     pos, x_ids = 0, prompt
     for step in range(n + 1):
+        dl = model.forward_tokens(x_ids.to(DEV), dstate, pos).float().cpu()
+        assert torch.equal(dl.argmax(-1), ids[:, step]), f"step {step}: eager logits do not pick the graph run's ids"
         x = ost.bf(host.embed.weight.detach()[x_ids])
         for i in range(cfg.n_layers):
-            x = ost.layer(host, i, x, state[i], pos)
-        logits = F.linear(ost.bf(ost.rms_norm(x[:, -1], host.norm.detach(), cfg.eps)), host.lm_head.weight.detach())
-        agree += int((logits.argmax(-1) == ids[:, step]).sum())
+            x = ost.layer(host, i, x, ostate[i], pos)
+        ol = F.linear(ost.bf(ost.rms_norm(x[:, -1], host.norm.detach(), cfg.eps)), host.lm_head.weight.detach())
+        worst_rel = max(worst_rel, errors(dl, ol)[0])
+        sigma = (dl - ol).std(dim=-1)
+        pick = ids[:, step]
+        gap = ol.max(-1).values - ol.gather(-1, pick[:, None])[:, 0]
+        assert (gap <= 4 * sigma).all(), f"step {step}: a pick {gap.tolist()} below the oracle's top (sigma {sigma.tolist()})"
+        agree += int((ol.argmax(-1) == pick).sum())
         total += B
         pos += x_ids.shape[1]
         x_ids = ids[:, step:step + 1]  # teacher forcing: the device's pick feeds the next step
-    rate = agree / total
-    print(f"greedy id agreement with the oracle: {agree}/{total} = {rate:.3f}")
-    assert rate >= 0.9, f"greedy id agreement {rate:.3f}"
+    print(f"greedy ids: {agree}/{total} = {agree / total:.3f} agree with the oracle's argmax; "
+          f"logits rel-L2 up to {worst_rel:.3e}")
+    assert worst_rel <= 0.1, f"logits rel-L2 {worst_rel:.3e}"
 
 
 def _small():

@@ -62,26 +62,31 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls():
 
 def test_noalloc_matches_workspace_entry_point_on_prefill_chunks():
     """16-token chunks take the tcgen05 prefill path, whose partial rows sit at offsets set by its own
-    split count inside the scratch; two chunks in a row against the workspace entry point."""
+    split count inside the scratch; two chunks in a row against the workspace entry point, at a shape
+    whose scratch fits the built-in array (8 query heads on one kv head, hd 128, 1024-row cache)."""
     lib = _lib.load()
     torch.manual_seed(43)
-    S = 16
-    cache = torch.zeros(2, HKV, CTX, HD, dtype=torch.half)
-    cache[:, :, :2048] = torch.randn(2, HKV, 2048, HD).half()
+    S, hq, hkv, hd, ctx = 16, 8, 1, 128, 1024
+    cache = torch.zeros(2, hkv, ctx, hd, dtype=torch.half)
+    cache[:, :, :512] = torch.randn(2, hkv, 512, hd).half()
     cache_a, cache_b = cache.to(DEV), cache.clone().to(DEV)
-    # the workspace entry point is sized for any position (about 20 MB); at these positions the plan
-    # splits each key range about 17 ways, about 4.5 MB, which the built-in array holds
-    need = lib.anemll_kv_attention_workspace_size(1, S, HQ, HKV, HD, CTX)
+    need = lib.anemll_kv_attention_workspace_size(1, S, hq, hkv, hd, ctx)
+    assert 0 < need <= lib.anemll_kv_attention_noalloc_max_scratch()
     ws = torch.empty(need, dtype=torch.uint8, device=DEV)
-    for pos in (2048, 2048 + S):
-        q = torch.randn(1, HQ, S, HD, dtype=torch.half, device=DEV)
-        kn = torch.randn(1, HKV, S, HD, dtype=torch.half, device=DEV)
-        vn = torch.randn(1, HKV, S, HD, dtype=torch.half, device=DEV)
-        gate = torch.randn(1, S, HQ * HD, dtype=torch.half, device=DEV)
-        out_a = torch.empty(1, S, HQ * HD, dtype=torch.half, device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for pos in (512, 512 + S):
+        q = torch.randn(1, hq, S, hd, dtype=torch.half, device=DEV)
+        kn = torch.randn(1, hkv, S, hd, dtype=torch.half, device=DEV)
+        vn = torch.randn(1, hkv, S, hd, dtype=torch.half, device=DEV)
+        gate = torch.randn(1, S, hq * hd, dtype=torch.half, device=DEV)
+        out_a = torch.empty(1, S, hq * hd, dtype=torch.half, device=DEV)
         out_b = torch.full_like(out_a, float("nan"))
-        _lib.check(_call(lib, False, q, kn, vn, gate, cache_a[0], cache_a[1], out_a, pos, ws), "regular")
-        _lib.check(_call(lib, True, q, kn, vn, gate, cache_b[0], cache_b[1], out_b, pos), "noalloc")
+        for noalloc, cc, out in ((False, cache_a, out_a), (True, cache_b, out_b)):
+            args = (_p(q), _p(kn), _p(vn), _p(gate), _p(cc[0]), _p(cc[1]), 0, cc[0].stride(0), None, 0, 0, _p(out),
+                    _lib.F16, 1, S, hq, hkv, hd, ctx, pos, 0, 0)
+            rc = (lib.anemll_kv_attention_noalloc(*args, stream) if noalloc
+                  else lib.anemll_kv_attention(*args, _p(ws), ws.numel(), stream))
+            _lib.check(rc, "noalloc" if noalloc else "regular")
         torch.cuda.synchronize()
         assert_close(out_b.float(), out_a.float(), f"chunk at {pos}")
         assert torch.equal(cache_a, cache_b), "cache writes differ"
