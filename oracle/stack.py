@@ -45,7 +45,8 @@ def attention_core(m, cfg, qkv, kc, vc, pos, cos, sin, with_k=False):
     per-head RMSNorm of q and k, RoPE, the cache write into ``kc``/``vc`` [B, H_kv, ctx, hd] (fp32,
     updated in place), attention over the cache with the causal mask and the sigmoid gate.  Returns
     the gated output [B, T, H_q*hd] in fp32, before its bf16 rounding and ``o_proj`` (and with
-    ``with_k`` the new K rows [B, H_kv, T, hd] before their bf16 rounding)."""
+    ``with_k`` also the new K rows [B, H_kv, T, hd] before their bf16 rounding and the normed K rows
+    that entered RoPE, bf16-valued, in the same layout)."""
     B, T, _ = qkv.shape
     n_q, n_kv = cfg.H_q * 2 * cfg.head_dim, cfg.H_kv * cfg.head_dim
     qg = qkv[..., :n_q].reshape(B, T, cfg.H_q, 2 * cfg.head_dim)
@@ -59,7 +60,7 @@ def attention_core(m, cfg, qkv, kc, vc, pos, cos, sin, with_k=False):
     kc[:, :, pos:pos + T] = bf(k_f)
     vc[:, :, pos:pos + T] = v.transpose(1, 2)
     o = ok.attend(q, kc, vc, ok.additive_mask(T, cfg.ctx, pos), gate.reshape(B, T, -1))
-    return (o, k_f) if with_k else o
+    return (o, k_f, k) if with_k else o
 
 
 def attention_layer(m, cfg, h, kc, vc, pos, cos, sin):

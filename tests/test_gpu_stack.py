@@ -16,7 +16,8 @@ Two kinds of check:
 * The greedy token ids of the whole stack: the device generates, the oracle is run over the
   device's ids (teacher forcing) and its argmax at every position is compared with the device's
   pick.  With random weights and a 151936-word vocabulary the top two logits are sometimes closer
-  than bf16 rounding, so the agreement rate is reported and held above 90%, not required to be 1.
+  than bf16 rounding, so the agreement rate is reported (59 of 68 picks on a B200), and every pick
+  that differs must be a near tie of the oracle's logits.
 """
 import pytest
 import torch
@@ -31,18 +32,27 @@ DEV = "cuda"
 SHARD_RTOL, SHARD_ATOL = 1e-2, 6e-2  # device against device, different GEMM shapes (see the test)
 
 
-def assert_bf16_close(got, want, what, rel_l2=1e-3, max_abs=2e-3):
+def bf16_ulp(x):
+    """The spacing of bf16 numbers at |x|: 2^(e-8) for |x| in [2^(e-1), 2^e)."""
+    _, e = torch.frexp(x.float())
+    return torch.ldexp(torch.ones_like(x.float()), e - 8)
+
+
+def assert_bf16_close(got, want, what, rel_l2=1e-3, max_abs=2e-3, inner_ulp=None):
     """``got`` (bf16) against the fp32 oracle ``want``, within the bar beyond the rounding of the output
     itself: rel-L2 at most the error of rounding ``want`` to bf16 plus ``rel_l2``; elementwise at most
     one bf16 ulp of ``want`` plus ``max_abs`` (a value within the bar of the oracle may round to the
-    neighbouring bf16 number)."""
+    neighbouring bf16 number).  ``inner_ulp`` adds, per element, what one ulp of a bf16 tensor rounded
+    inside the op (before its last step) becomes in the output: such an intermediate may also round to
+    its neighbour when the device's fp32 value differs from the oracle's in the last bits."""
     want = want.float().cpu()
     g = got.float().cpu()
     assert torch.isfinite(g).all(), f"{what}: non-finite values"
     rel_f, _ = errors(want.bfloat16(), want)
     rel, _ = errors(g, want)
-    _, e = torch.frexp(want)
-    ulp = torch.ldexp(torch.ones_like(want), e - 8)  # |want| in [2^(e-1), 2^e): bf16 spacing 2^(e-8)
+    ulp = bf16_ulp(want)
+    if inner_ulp is not None:
+        ulp = ulp + inner_ulp.float().cpu()
     over = ((g - want).abs() - ulp - max_abs).max().item() if want.numel() else 0.0
     assert rel <= rel_f + rel_l2 and over <= 0, (
         f"{what}: rel_l2={rel:.3e} (rounding floor {rel_f:.3e} + {rel_l2}); worst element {over:.3e} beyond "
@@ -107,11 +117,17 @@ def _check_attention(i, m, hm, cfg, h, state, pos, cos, sin, what):
                                    cfg.H_kv, cfg.head_dim)
     assert o is not None, "the fused attention call declined a stack shape"
     kc, vc = kc0.clone(), vc0.clone()
-    ro, rk = ost.attention_core(hm, cfg, qkv.float().cpu(), kc, vc, pos, cos[pos:pos + T].cpu(),
-                                sin[pos:pos + T].cpu(), with_k=True)
+    c, sn = cos[pos:pos + T].cpu(), sin[pos:pos + T].cpu()
+    ro, rk, kn = ost.attention_core(hm, cfg, qkv.float().cpu(), kc, vc, pos, c, sn, with_k=True)
     assert_bf16_close(o, ro, f"{what} layer {i} attention out")
     new = slice(pos, pos + T)
-    assert_bf16_close(state[0][:, :, new], rk, f"{what} layer {i} new K rows")
+    # a new K row is RoPE of the normed row, which is rounded to bf16 first (as two framework ops
+    # would): out_j = kn_j cos_j + rot(kn)_j sin_j, so one ulp of kn moves out_j by |cos_j| ulp(kn_j)
+    # and one ulp of its rotation partner by |sin_j| ulp(rot(kn)_j)
+    h = cfg.head_dim // 2
+    partner = torch.cat([kn[..., h:], kn[..., :h]], dim=-1)
+    inner = c.float().abs() * bf16_ulp(kn) + sn.float().abs() * bf16_ulp(partner)
+    assert_bf16_close(state[0][:, :, new], rk, f"{what} layer {i} new K rows", inner_ulp=inner)
     assert torch.equal(state[1][:, :, new].float().cpu(), vc[:, :, new]), f"{what} layer {i} new V rows"
     for dev_c, old in ((state[0], kc0), (state[1], vc0)):
         assert torch.equal(dev_c[:, :, :pos].float().cpu(), old[:, :, :pos]), f"{what} layer {i} earlier rows"
