@@ -42,6 +42,12 @@
 //
 // Semantics: torch_chunk_gated_delta_rule of transformers 5.5.0
 // (modeling_qwen3_5.py:234-311); chunk (WY/UT) form of Yang et al. (2024).
+//
+// Gated form (anemll_gdn_chunked_prefill_gated): the layer's gated RMSNorm
+// (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190) runs in the epilogue.  A
+// CTA holds all d_v columns of its head, so the chunk's fp32 output tile is
+// staged in shared memory and four threads per token reduce its sum of squares
+// and write weight * o * rsqrt(mean(o^2) + eps) * silu(z) directly.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -105,6 +111,18 @@ struct TileMaps {
   CUtensorMap q, k, v;
 };
 
+// The gated RMSNorm's extra operands: z rows (token row b*T + t, z_ld elements apart, heads dense,
+// 16-byte aligned), the weight [d_v], eps, and an optional fp32 copy of the core output (NULL: not
+// written).
+template <typename TZ>
+struct GatedNorm {
+  const TZ* z;
+  long long z_ld;
+  const float* w;
+  float eps;
+  float* core_out;
+};
+
 __device__ int g_chunked_error = 0;
 
 // byte offset of 16-byte chunk `ch` (0..7) of row `r` inside a 128-byte-row swizzled block
@@ -164,11 +182,11 @@ __device__ __forceinline__ float pick_lane(const float* r, int lane) {
   return d;
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, bool GATED>
 __global__ void __launch_bounds__(NT, 2)
 gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restrict__ g, const float* __restrict__ beta,
                    float* __restrict__ state, TOut* __restrict__ out, int T, int Hqk, int Hv, float scale,
-                   int l2norm) {
+                   int l2norm, const GatedNorm<TOut> gn) {
   constexpr bool kBF = std::is_same<TIn, __nv_bfloat16>::value;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -705,7 +723,60 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
         of[q4 * 4 + 2] = f.z;
         of[q4 * 4 + 3] = f.w;
       }
-      if constexpr (sizeof(TOut) == 2) {
+      if constexpr (GATED) {
+        // fp32 [token][d_v] staging in R1 (free once the state update has read the decayed Vn); the
+        // low three bits of each row's 16-byte chunk index are XORed with the chunk's 32-column
+        // quarter and the token's parity, so neither the column writes nor the row reads conflict
+        float* ost = reinterpret_cast<float*>(sm + OFF_R1);
+        const int cw = row >> 2;
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int tok = 32 * hf + t;
+          ost[tok * D + ((cw ^ (((cw >> 3) & 3) ^ ((tok & 1) << 2))) << 2) + (row & 3)] = fmaf(of[t], o1[t], o2[t]);
+        }
+        __syncthreads();
+        // thread (token, quarter): 32 columns of one token; the token's four threads are adjacent lanes
+        const int tok = tid >> 2, qq = tid & 3;
+        const int swz = qq ^ ((tok & 1) << 2);
+        float x[32];
+        float ss = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const float4 f = ld4(ost + tok * D + (((8 * qq + kk) ^ swz) << 2));
+          x[4 * kk] = f.x;
+          x[4 * kk + 1] = f.y;
+          x[4 * kk + 2] = f.z;
+          x[4 * kk + 3] = f.w;
+          ss += f.x * f.x + f.y * f.y + f.z * f.z + f.w * f.w;
+        }
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        const float rn = rsqrtf(ss / (float)D + gn.eps);
+        if (tok < nvalid) {
+          const size_t trow = (size_t)b * T + t0 + tok;
+          const size_t obase = (trow * Hv + hv) * D + 32 * qq;
+          if (gn.core_out) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              *reinterpret_cast<float4*>(gn.core_out + obase + 4 * kk) =
+                  make_float4(x[4 * kk], x[4 * kk + 1], x[4 * kk + 2], x[4 * kk + 3]);
+          }
+          const TOut* zp = gn.z + (long long)trow * gn.z_ld + (long long)hv * D + 32 * qq;
+          const float* wp = gn.w + 32 * qq;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float zf[8], y[8];
+            load8(zp + 8 * j, zf);
+            const float4 wa = __ldg(reinterpret_cast<const float4*>(wp + 8 * j));
+            const float4 wb = __ldg(reinterpret_cast<const float4*>(wp + 8 * j + 4));
+            const float wf[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              y[e] = wf[e] * x[8 * j + e] * rn * __fdividef(zf[e], 1.0f + __expf(-zf[e]));
+            store8(out + obase + 8 * j, y);
+          }
+        }
+      } else if constexpr (sizeof(TOut) == 2) {
         TOut* ost = reinterpret_cast<TOut*>(sm + OFF_OST);  // [token][d_v] staging
 #pragma unroll
         for (int t = 0; t < 32; ++t) ost[(32 * hf + t) * D + row] = from_f32<TOut>(fmaf(of[t], o1[t], o2[t]));
@@ -780,19 +851,20 @@ int encode_rows_map(CUtensorMap* m, const void* base, int heads, long long token
   return ANEMLL_OK;
 }
 
-template <typename TIn, typename TOut>
+template <typename TIn, typename TOut, bool GATED>
 int launch_chunked(const void* q, const void* k, const void* v, const float* g, const float* beta, float* state,
-                   void* out, int B, int T, int Hqk, int Hv, float scale, int l2norm, cudaStream_t st) {
+                   void* out, int B, int T, int Hqk, int Hv, float scale, int l2norm, const GatedNorm<TOut>& gn,
+                   cudaStream_t st) {
   TileMaps maps;
   const long long tokens = (long long)B * T;
   int rc = encode_rows_map(&maps.q, q, Hqk, tokens);
   if (!rc) rc = encode_rows_map(&maps.k, k, Hqk, tokens);
   if (!rc) rc = encode_rows_map(&maps.v, v, Hv, tokens);
   if (rc) return rc;
-  auto kern = gdn_chunked_kernel<TIn, TOut>;
+  auto kern = gdn_chunked_kernel<TIn, TOut, GATED>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  kern<<<B * Hv, NT, SMEM_BYTES, st>>>(maps, g, beta, state, (TOut*)out, T, Hqk, Hv, scale, l2norm);
-  return launch_status("gdn_chunked_prefill");
+  kern<<<B * Hv, NT, SMEM_BYTES, st>>>(maps, g, beta, state, (TOut*)out, T, Hqk, Hv, scale, l2norm, gn);
+  return launch_status(GATED ? "gdn_chunked_prefill_gated" : "gdn_chunked_prefill");
 }
 
 }  // namespace
@@ -822,7 +894,46 @@ extern "C" int anemll_gdn_chunked_prefill(const void* q, const void* k, const vo
   cudaStream_t st = (cudaStream_t)stream;
   return ANEMLL_DISPATCH_HALF(qkv_dtype, TIn, [&] {
     return ANEMLL_DISPATCH_DTYPE(out_dtype, TOut, [&] {
-      return launch_chunked<TIn, TOut>(q, k, v, g, beta, state, out, B, T, H_qk, H_v, scale, qk_l2norm, st);
+      const GatedNorm<TOut> none{nullptr, 0, nullptr, 0.f, nullptr};
+      return launch_chunked<TIn, TOut, false>(q, k, v, g, beta, state, out, B, T, H_qk, H_v, scale, qk_l2norm, none,
+                                              st);
+    });
+  });
+}
+
+extern "C" int anemll_gdn_chunked_prefill_gated(const void* q, const void* k, const void* v, int qkv_dtype,
+                                                const float* g, const float* beta, float* state,
+                                                const void* z, int64_t z_row_stride, const float* norm_weight,
+                                                float eps, void* out, int out_dtype, float* core_out,
+                                                int B, int T, int H_qk, int H_v, int d_k, int d_v,
+                                                int chunk_size, float scale, int qk_l2norm, void* stream) {
+  ANEMLL_REQUIRE(state && (T == 0 || (q && k && v && g && beta && z && norm_weight && out)), ANEMLL_EINVAL,
+                 "gdn_chunked_prefill_gated: null pointer");
+  ANEMLL_REQUIRE(B > 0 && T >= 0 && H_qk > 0 && H_v > 0 && H_v % H_qk == 0, ANEMLL_EINVAL,
+                 "gdn_chunked_prefill_gated: bad sizes B=%d T=%d H_qk=%d H_v=%d", B, T, H_qk, H_v);
+  ANEMLL_REQUIRE(d_k == D && d_v == D, ANEMLL_EUNSUPPORTED, "gdn_chunked_prefill_gated: d_k and d_v must be 128");
+  ANEMLL_REQUIRE(chunk_size == C, ANEMLL_EUNSUPPORTED, "gdn_chunked_prefill_gated: chunk_size must be 64");
+  ANEMLL_REQUIRE(qkv_dtype == ANEMLL_F16 || qkv_dtype == ANEMLL_BF16, ANEMLL_EUNSUPPORTED,
+                 "gdn_chunked_prefill_gated: q/k/v must be f16 or bf16");
+  ANEMLL_REQUIRE(out_dtype == ANEMLL_F16 || out_dtype == ANEMLL_BF16, ANEMLL_EUNSUPPORTED,
+                 "gdn_chunked_prefill_gated: out (and z) must be f16 or bf16");
+  if (z_row_stride == 0) z_row_stride = (int64_t)H_v * d_v;
+  ANEMLL_REQUIRE(z_row_stride >= (int64_t)H_v * d_v, ANEMLL_EINVAL,
+                 "gdn_chunked_prefill_gated: z row stride shorter than H_v * d_v");
+  if (T == 0) return ANEMLL_OK;
+  ANEMLL_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(v, 16) && aligned(g, 4) && aligned(beta, 4) &&
+                     aligned(out, 16) && aligned(z, 16) && (z_row_stride * 2) % 16 == 0 && aligned(norm_weight, 16) &&
+                     (core_out == nullptr || aligned(core_out, 16)),
+                 ANEMLL_EALIGN,
+                 "gdn_chunked_prefill_gated: q/k/v, out, z (and its row stride), the weight and core_out must be "
+                 "16-byte aligned");
+  if (scale <= 0.f) scale = 1.0f / sqrtf((float)d_k);
+  cudaStream_t st = (cudaStream_t)stream;
+  return ANEMLL_DISPATCH_HALF(qkv_dtype, TIn, [&] {
+    return ANEMLL_DISPATCH_HALF(out_dtype, TOut, [&] {
+      const GatedNorm<TOut> gn{(const TOut*)z, (long long)z_row_stride, norm_weight, eps, core_out};
+      return launch_chunked<TIn, TOut, true>(q, k, v, g, beta, state, out, B, T, H_qk, H_v, scale, qk_l2norm, gn,
+                                             st);
     });
   });
 }

@@ -30,6 +30,7 @@ __all__ = [
     "recurrent_gated_delta_rule_",
     "chunk_gated_delta_rule",
     "chunk_gated_delta_rule_",
+    "gated_delta_rule_norm_",
     "chunked_device_error",
     "gdn_prologue",
     "gated_rmsnorm",
@@ -122,6 +123,72 @@ def chunk_gated_delta_rule_(query, key, value, g, beta, state, scale=None, use_q
         float(scale) if scale is not None else 0.0, int(bool(use_qk_l2norm_in_kernel)),
         _lib.stream_ptr(query.device))
     _lib.check(rc, "anemll_gdn_chunked_prefill")
+    return out
+
+
+def _z_rows(z, B, T, H, d):
+    """``z`` [B, T, H, d] as (tensor, token row stride in elements): dense heads with a uniform token
+    stride (a column slice of a wider projection output is read in place), else a contiguous copy."""
+    if z.is_contiguous():
+        return z, H * d
+    if z.dim() == 4 and z.stride(-1) == 1 and z.stride(-2) == d:
+        ld = z.stride(1) if T > 1 else z.stride(0)
+        if B == 1 or T == 1 or z.stride(0) == ld * T:
+            return z, ld
+    return z.contiguous(), H * d
+
+
+def gated_delta_rule_norm_(query, key, value, g, beta, state, z, norm_weight, eps=1e-6, chunked=True,
+                           chunk_size=64, scale=None, use_qk_l2norm_in_kernel=False, out=None, out_dtype=None,
+                           core_out=None):
+    """The delta rule with the layer's gated RMSNorm fused into its epilogue: returns
+    ``norm_weight * o * rsqrt(mean(o^2) + eps) * silu(z)`` [B, T, H_v, d_v] (``out_dtype``, default
+    ``z.dtype``: fp16 or bf16), where ``o`` is the core output of :func:`chunk_gated_delta_rule_`
+    (``chunked``) or :func:`recurrent_gated_delta_rule_`.  ``state`` is updated in place; ``core_out``
+    (fp32 [B, T, H_v, d_v], optional) also receives ``o``.  ``z`` [B, T, H_v, d_v] may be a column
+    slice of the layer's fused projection output.  Replaces the core call and ``self.norm`` of
+    ``Qwen3_5GatedDeltaNet.forward`` (modeling_qwen3_5.py:497-523, 175-190)."""
+    _need_cuda(query, key, value, g, beta, state, z, norm_weight, core_out)
+    for n, t in (("query", query), ("key", key), ("value", value), ("g", g), ("beta", beta), ("state", state)):
+        _need_contig(n, t)
+    if g.dtype != torch.float32 or beta.dtype != torch.float32 or state.dtype != torch.float32:
+        raise TypeError("g, beta and state must be float32")
+    if query.dtype != key.dtype or key.dtype != value.dtype:
+        raise TypeError("query, key and value must share a dtype")
+    B, T, H_qk, d_k = query.shape
+    H_v, d_v = value.shape[2], value.shape[3]
+    if key.shape != query.shape or value.shape[:2] != (B, T) or tuple(state.shape) != (B, H_v, d_k, d_v):
+        raise ValueError("shape mismatch between query/key/value/state")
+    if tuple(g.shape) != (B, T, H_v) or tuple(beta.shape) != (B, T, H_v):
+        raise ValueError("g and beta must be [B, T, H_v]")
+    if tuple(z.shape) != (B, T, H_v, d_v) or tuple(norm_weight.shape) != (d_v,):
+        raise ValueError("z must be [B, T, H_v, d_v] and norm_weight [d_v]")
+    out_dtype = out_dtype or z.dtype
+    if out_dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("the gated output is fp16 or bf16")
+    if z.dtype != out_dtype:
+        z = z.to(out_dtype)
+    z, z_ld = _z_rows(z, B, T, H_v, d_v)
+    if chunked and (z_ld * z.element_size()) % 16:
+        z, z_ld = z.contiguous(), H_v * d_v
+    w = norm_weight.float().contiguous()
+    if out is None:
+        out = torch.empty(B, T, H_v, d_v, dtype=out_dtype, device=query.device)
+    if core_out is not None and (core_out.dtype != torch.float32 or tuple(core_out.shape) != (B, T, H_v, d_v)
+                                 or not core_out.is_contiguous()):
+        raise ValueError("core_out must be a contiguous fp32 [B, T, H_v, d_v] tensor")
+    lib = _lib.load()
+    args = (_lib.ptr(query), _lib.ptr(key), _lib.ptr(value), _lib.dtype_code(query.dtype), _lib.ptr(g), _lib.ptr(beta),
+            _lib.ptr(state), _lib.ptr(z), int(z_ld), _lib.ptr(w), float(eps), _lib.ptr(out), _lib.dtype_code(out.dtype),
+            _lib.ptr(core_out), B, T, H_qk, H_v, d_k, d_v)
+    tail = (float(scale) if scale is not None else 0.0, int(bool(use_qk_l2norm_in_kernel)),
+            _lib.stream_ptr(query.device))
+    if chunked:
+        rc = lib.anemll_gdn_chunked_prefill_gated(*args, int(chunk_size), *tail)
+        _lib.check(rc, "anemll_gdn_chunked_prefill_gated")
+    else:
+        rc = lib.anemll_gdn_recurrent_gated(*args, *tail)
+        _lib.check(rc, "anemll_gdn_recurrent_gated")
     return out
 
 
@@ -300,9 +367,11 @@ class GatedDeltaNet(nn.Module):
 
     CHUNKED_MIN_TOKENS = 16  # calls with at least this many tokens run the chunked prefill kernel
 
-    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos=0):
-        """Everything between the input and output projections (the hot path).  Returns the core
-        output (fp32) and the gated-normed output (activation dtype)."""
+    def core(self, mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos=0, return_core=False):
+        """Everything between the input and output projections (the hot path): the prologue, then the
+        chunked or recurrent kernel with the gated RMSNorm in its epilogue.  Returns the gated-normed
+        output (activation dtype), or with ``return_core`` the pair (fp32 core output, normed output)
+        from the same launch."""
         B, T, _ = mixed_qkv.shape
         cont = _position(current_pos) > 0
         if not cont:
@@ -311,14 +380,14 @@ class GatedDeltaNet(nn.Module):
                                         self.num_k_heads,
                                         self.num_v_heads, self.head_k_dim, self.head_v_dim,
                                         use_state=cont, out_dtype=self.core_dtype)
-        if T >= self.CHUNKED_MIN_TOKENS:
-            o = chunk_gated_delta_rule_(q, k, v, g, beta, recurrent_state, chunk_size=self.chunk_size,
-                                        out_dtype=torch.float32)
-        else:
-            o = recurrent_gated_delta_rule_(q, k, v, g, beta, recurrent_state, out_dtype=torch.float32)
-        normed = gated_rmsnorm(o, z.reshape(B, T, self.num_v_heads, self.head_v_dim), self.norm_weight,
-                               self.eps, out_dtype=mixed_qkv.dtype)
-        return o, normed
+        o = None
+        if return_core:
+            o = torch.empty(B, T, self.num_v_heads, self.head_v_dim, dtype=torch.float32, device=mixed_qkv.device)
+        normed = gated_delta_rule_norm_(q, k, v, g, beta, recurrent_state,
+                                        z.reshape(B, T, self.num_v_heads, self.head_v_dim), self.norm_weight,
+                                        self.eps, chunked=T >= self.CHUNKED_MIN_TOKENS, chunk_size=self.chunk_size,
+                                        out_dtype=mixed_qkv.dtype, core_out=o)
+        return (o, normed) if return_core else normed
 
     def forward(self, hidden_states, current_pos, conv_state, recurrent_state):
         B, T, _ = hidden_states.shape
@@ -326,7 +395,7 @@ class GatedDeltaNet(nn.Module):
         c, v = self.conv_dim, self.value_dim
         mixed_qkv, z = proj[..., :c], proj[..., c:c + v]
         b, a = proj[..., c + v:c + v + self.num_v_heads], proj[..., c + v + self.num_v_heads:]
-        _, normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos)
+        normed = self.core(mixed_qkv, z, a, b, conv_state, recurrent_state, current_pos)
         return F.linear(normed.reshape(B, T, self.value_dim), self.out_proj.weight)
 
 

@@ -12,6 +12,9 @@ operator                               replaces
 beta, state, scale, use_qk_l2norm)``   ``modeling_qwen3_5.py:234-311``); ``state`` updated
 ``gdn_recurrent(q, k, v, g, beta,      ``torch_recurrent_gated_delta_rule`` (314-353)
 state, scale, use_qk_l2norm)``
+``gdn_gated_delta_rule_norm(q, k, v,   the core call and ``self.norm`` (``Qwen3_5RMSNormGated``)
+g, beta, state, z, norm_weight, eps,   of ``Qwen3_5GatedDeltaNet.forward`` (497-523, 175-190):
+chunked, scale, use_qk_l2norm)``       either kernel above with the gated RMSNorm in its epilogue
 ``gdn_prologue(mixed_qkv, conv_weight, the conv/split/l2-norm/gate part of
 conv_state, a, b, A_log, dt_bias,      ``Qwen3_5GatedDeltaNet.forward`` (453-496);
 H_qk, H_v, d_k, d_v, use_state)``      ``conv_state`` updated
@@ -29,7 +32,7 @@ import torch
 
 from . import attention, gdn
 
-__all__ = ["gdn_chunked_prefill", "gdn_recurrent", "gdn_prologue", "kv_attention"]
+__all__ = ["gdn_chunked_prefill", "gdn_recurrent", "gdn_gated_delta_rule_norm", "gdn_prologue", "kv_attention"]
 
 
 @torch.library.custom_op("anemll_b200::gdn_chunked_prefill", mutates_args=("state",), device_types="cuda")
@@ -44,6 +47,15 @@ def gdn_recurrent(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Te
                   state: torch.Tensor, scale: float = 0.0, use_qk_l2norm: bool = False) -> torch.Tensor:
     return gdn.recurrent_gated_delta_rule_(q, k, v, g, beta, state, scale=scale if scale > 0 else None,
                                            use_qk_l2norm_in_kernel=use_qk_l2norm)
+
+
+@torch.library.custom_op("anemll_b200::gdn_gated_delta_rule_norm", mutates_args=("state",), device_types="cuda")
+def gdn_gated_delta_rule_norm(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                              beta: torch.Tensor, state: torch.Tensor, z: torch.Tensor, norm_weight: torch.Tensor,
+                              eps: float = 1e-6, chunked: bool = True, scale: float = 0.0,
+                              use_qk_l2norm: bool = False) -> torch.Tensor:
+    return gdn.gated_delta_rule_norm_(q, k, v, g, beta, state, z, norm_weight, eps, chunked=chunked,
+                                      scale=scale if scale > 0 else None, use_qk_l2norm_in_kernel=use_qk_l2norm)
 
 
 @torch.library.custom_op("anemll_b200::gdn_prologue", mutates_args=("conv_state",), device_types="cuda")

@@ -176,7 +176,8 @@ def test_gdn_layer_prefill_then_decode_matches_oracle():
         for step, (s, e) in enumerate([(0, 512)] + [(512 + i, 513 + i) for i in range(64)]):
             x = h[:, s:e]
             mixed, z, a, b = layer.in_proj_qkv(x), layer.in_proj_z(x), layer.in_proj_a(x), layer.in_proj_b(x)
-            o, normed = layer.core(mixed, z, a, b, conv_state, rec_state, current_pos=0 if step == 0 else 512 + step - 1)
+            o, normed = layer.core(mixed, z, a, b, conv_state, rec_state,
+                                   current_pos=0 if step == 0 else 512 + step - 1, return_core=True)
             if step == 0:
                 ro, rn, ref_conv, ref_state = og.gdn_layer_prefill(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), params,
                                                                    16, 32, 128, 128)
@@ -256,10 +257,11 @@ def test_layer_continues_a_prefill_from_its_states():
         parts = lambda s, e: (proj[:, s:e, :c], proj[:, s:e, c:c + v], proj[:, s:e, c + v + H:],
                               proj[:, s:e, c + v:c + v + H])
         one = layer.new_states(1)
-        o1, n1 = layer.core(*parts(0, 512), *one, current_pos=0)
+        o1, n1 = layer.core(*parts(0, 512), *one, current_pos=0, return_core=True)
         two = layer.new_states(1)
         two[1].fill_(1.0)  # position 0 resets the recurrent state
-        oa, na = layer.core(*parts(0, 256), *two, current_pos=0)
-        ob, nb = layer.core(*parts(256, 512), *two, current_pos=torch.tensor([256], dtype=torch.int32))
+        oa, na = layer.core(*parts(0, 256), *two, current_pos=0, return_core=True)
+        ob, nb = layer.core(*parts(256, 512), *two, current_pos=torch.tensor([256], dtype=torch.int32),
+                            return_core=True)
     assert torch.equal(torch.cat([oa, ob], 1), o1) and torch.equal(torch.cat([na, nb], 1), n1)
     assert torch.equal(two[0], one[0]) and torch.equal(two[1], one[1])

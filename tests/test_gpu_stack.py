@@ -82,7 +82,7 @@ def _check_gdn(i, m, hm, cfg, h, state, pos, what):
     mixed, z = proj[..., :c], proj[..., c:c + v]
     b, a = proj[..., c + v:c + v + m.num_v_heads], proj[..., c + v + m.num_v_heads:]
     conv0, rec0 = state[0].float().cpu(), state[1].cpu().clone()
-    o, normed = m.core(mixed, z, a, b, state[0], state[1], current_pos=pos)
+    o, normed = m.core(mixed, z, a, b, state[0], state[1], current_pos=pos, return_core=True)
     params = dict(conv_w=hm.conv_weight.detach(), A_log=hm.A_log.detach(), dt_bias=hm.dt_bias.detach(),
                   norm_w=hm.norm_weight.detach(), eps=m.eps)
     args = (mixed.float().cpu(), z.float().cpu(), a.float().cpu(), b.float().cpu(), params, cfg.H_qk, cfg.H_v,
