@@ -270,10 +270,12 @@ def bench_gdn_decode(args, ws, rank, local):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / pk["hbm_gbs"], "peak_source": how,
                      "algorithmic_bytes_per_launch": decode_bytes_per_step(),
-                     # ncu DRAM bytes (read + write) of one launch; the write-back of part of a step's
-                     # state is deferred into the next launch, so a lone launch shows less than it moves
-                     # in steady state
-                     "traffic": traffic_from_profiles("gdn_recurrent_decode")},
+                     # ncu DRAM bytes (read + write) per launch in steady state (consecutive launches,
+                     # caches not flushed: each launch's window carries the write-back of the previous
+                     # launch's dirty state lines), and the fraction of the peak those bytes reach
+                     "traffic": traffic_from_profiles("gdn_recurrent_decode"),
+                     "dram_frac": dram_frac(traffic_from_profiles("gdn_recurrent_decode"), per_launch_s,
+                                            pk["hbm_gbs"])},
         "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": args.steps,
@@ -1101,6 +1103,12 @@ def _cpu_stack_model(cfg):
                     n = min(base.numel(), flat.numel() - i)
                     flat[i:i + n].copy_(base[:n] * (5.0 if name.endswith("conv_weight") else 1.0))
     return model
+
+
+def dram_frac(traffic, per_launch_s, peak_gbs):
+    """Measured DRAM bytes of one launch over its device time, as a fraction of the HBM peak (None
+    without a capture)."""
+    return None if traffic is None else traffic / per_launch_s / 1e9 / peak_gbs
 
 
 def traffic_from_profiles(name):
