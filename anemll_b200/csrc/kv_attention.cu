@@ -347,30 +347,35 @@ kv_attn_kernel(KvParams p) {
 // issued before the weights are known, so the kernel waits on a single memory round trip.  The
 // warp sums meet in shared memory.
 // PER = splits per warp (1, 2, 4, 8 or 16), the smallest that covers n_splits, keeps the registers
-// (and so the CTAs per SM) in step with the split count.
+// (and so the CTAs per SM) in step with the split count.  NCG > 1 splits each row's columns over NCG
+// CTAs (blockIdx.z): decode-shaped calls have few rows, and one CTA pulling every split's whole row
+// waits on its own SM's load rate, so a few CTAs per row share the reads.
 constexpr int CB_WARPS = 8;
 constexpr int CB_MAX_SPLITS = 128;
 
-template <typename T, int HD, int PER>
+template <typename T, int HD, int PER, int NCG = 1>
 __global__ void __launch_bounds__(CB_WARPS * 32)
 kv_combine_kernel(KvParams p) {
   static_assert(PER <= CB_MAX_SPLITS / CB_WARPS, "split count above the combine's limit");
+  static_assert(HD % (32 * NCG) == 0 && (HD / NCG / 32) % 2 == 0, "column groups of 64 or more");
   griddep_wait();
   griddep_launch_dependents();
-  constexpr int VPT = HD / 32;  // columns per lane
+  constexpr int CW = HD / NCG;  // columns of this CTA
+  constexpr int VPT = CW / 32;  // columns per lane
   const int G = p.Hq / p.Hkv;
   const int R = p.S * G;
   const int r = blockIdx.x;
   const int bh = blockIdx.y;
+  const int c0 = (int)blockIdx.z * CW;
   const int b = bh / p.Hkv, kvh = bh % p.Hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float s_w[CB_MAX_SPLITS];
   __shared__ float s_red[CB_WARPS];
-  __shared__ __align__(16) float s_acc[CB_WARPS][HD];
+  __shared__ __align__(16) float s_acc[CB_WARPS][CW];
   const int ns = p.n_splits;
   const long long row0 = (long long)bh * ns * R + r;  // row id of split 0; split i adds i * R
   const long long step = (long long)R * HD;
-  const float* po = p.ws_o + row0 * HD + lane * VPT;
+  const float* po = p.ws_o + row0 * HD + c0 + lane * VPT;
   float v[PER][VPT];
 #pragma unroll
   for (int k = 0; k < PER; ++k) {
@@ -420,13 +425,13 @@ kv_combine_kernel(KvParams p) {
 #pragma unroll
   for (int w = 0; w < CB_WARPS; ++w) L += s_red[w];
   const int s = r / G, hq = kvh * G + r % G;
-  for (int d = tid; d < HD; d += CB_WARPS * 32) {
+  for (int d = tid; d < CW; d += CB_WARPS * 32) {
     float a = 0.f;
 #pragma unroll
     for (int w = 0; w < CB_WARPS; ++w) a += s_acc[w][d];
-    const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + d;
+    const long long o = ((long long)b * p.S + s) * p.Hq * HD + (long long)hq * HD + c0 + d;
     float val = a / L;
-    if (p.gate) val *= sigmoid_fast(to_f32(reinterpret_cast<const T*>(p.gate)[gate_index(p, b, s, hq, d)]));
+    if (p.gate) val *= sigmoid_fast(to_f32(reinterpret_cast<const T*>(p.gate)[gate_index(p, b, s, hq, c0 + d)]));
     reinterpret_cast<T*>(p.out)[o] = from_f32<T>(val);
   }
 }
@@ -456,16 +461,24 @@ int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, 
   return launch_status(what);
 }
 
+template <typename T, int HD, int NCG>
+int launch_combine_ncg(const KvParams& q, cudaStream_t st) {
+  const int R = q.S * (q.Hq / q.Hkv);
+  const dim3 grid(R, q.B * q.Hkv, NCG), block(CB_WARPS * 32);
+  const int per = (q.n_splits + CB_WARPS - 1) / CB_WARPS;
+  if (per <= 1) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 1, NCG>, grid, block, 0, st, q);
+  if (per <= 2) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 2, NCG>, grid, block, 0, st, q);
+  if (per <= 4) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 4, NCG>, grid, block, 0, st, q);
+  if (per <= 8) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 8, NCG>, grid, block, 0, st, q);
+  return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 16, NCG>, grid, block, 0, st, q);
+}
+
+// Rows x (sequence, kv head) below one CTA per SM: split the columns into 64-wide groups.
 template <typename T, int HD>
 int launch_combine(const KvParams& q, cudaStream_t st) {
-  const int R = q.S * (q.Hq / q.Hkv);
-  const dim3 grid(R, q.B * q.Hkv), block(CB_WARPS * 32);
-  const int per = (q.n_splits + CB_WARPS - 1) / CB_WARPS;
-  if (per <= 1) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 1>, grid, block, 0, st, q);
-  if (per <= 2) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 2>, grid, block, 0, st, q);
-  if (per <= 4) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 4>, grid, block, 0, st, q);
-  if (per <= 8) return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 8>, grid, block, 0, st, q);
-  return launch_pdl("kv_combine", kv_combine_kernel<T, HD, 16>, grid, block, 0, st, q);
+  const long rows = (long)q.S * (q.Hq / q.Hkv) * q.B * q.Hkv;
+  if (HD >= 128 && rows < 148) return launch_combine_ncg<T, HD, HD / 64>(q, st);
+  return launch_combine_ncg<T, HD, 1>(q, st);
 }
 
 struct Plan {
