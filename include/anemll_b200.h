@@ -115,6 +115,18 @@ int anemll_gdn_chunked_prefill_gated(const void* q, const void* k, const void* v
                                      int chunk_size, float scale, int qk_l2norm, void* stream);
 
 /*
+ * Which kernel runs the chunked prefill (and its gated form): 0 (default)
+ * chooses by the number of (sequence, value head) chains: one chain per SM
+ * with the next chunk's state-independent work pipelined under the current
+ * chunk's state chain while the chains fit one wave of SMs, two chains per
+ * SM beyond that; 1 always the pipelined kernel; 2 always the two-chain
+ * kernel.  Both give the same results bit for bit.  Returns the previous
+ * mode; other values only query it.  No counterpart in the reference (a
+ * choice between this build's kernels).
+ */
+int anemll_gdn_chunked_mode(int mode);
+
+/*
  * Device-side status of the chunked kernel: non-zero if a bounded wait on the
  * tensor core ran out (the kernel then stopped early and its outputs are
  * invalid).  Synchronous; reset != 0 clears the flag.  Returns -1 on a CUDA

@@ -127,3 +127,34 @@ def test_empty_and_invalid():
     with pytest.raises(RuntimeError, match="f16 or bf16"):
         gdn.chunk_gated_delta_rule_(q, q, torch.zeros(1, 4, 2, 128, device=DEV), torch.zeros(1, 4, 2, device=DEV),
                                     torch.zeros(1, 4, 2, device=DEV), st)
+
+
+@pytest.mark.parametrize("B,T,Hqk,Hv,l2,dtype", [(2, 300, 2, 4, False, torch.bfloat16), (1, 130, 2, 4, True, torch.float16),
+                                                 (1, 2048, 16, 32, False, torch.bfloat16)])
+def test_pipelined_and_two_chain_kernels_agree_bitwise(B, T, Hqk, Hv, l2, dtype):
+    """The one-chain-per-SM kernel (the next chunk's state-independent work pipelined under the current
+    chunk's state chain) and the two-chains-per-SM kernel run the same arithmetic: outputs and final
+    states are equal bit for bit, in the plain and the gated form, with ragged last chunks and the
+    in-kernel l2 norm."""
+    from anemll_b200 import _lib
+    lib = _lib.load()
+    q, k, v, g, beta, S0 = _case(B, T, Hqk, Hv, seed=T, dtype=dtype, s0=0.01)
+    if l2:
+        q, k = (2.0 * q.float()).to(dtype), (0.5 * k.float()).to(dtype)
+    z = torch.randn(B, T, Hv, 128).to(dtype).to(DEV)
+    w = (1.0 + 0.1 * torch.randn(128)).to(DEV)
+    prev = lib.anemll_gdn_chunked_mode(0)
+    try:
+        res = {}
+        for mode in (1, 2):
+            lib.anemll_gdn_chunked_mode(mode)
+            o, st = _run(q, k, v, g, beta, S0, l2=l2)
+            s2 = S0.to(DEV).contiguous()
+            y = gdn.gated_delta_rule_norm_(q.to(DEV), k.to(DEV), v.to(DEV), g.to(DEV), beta.to(DEV), s2, z, w,
+                                           chunked=True, use_qk_l2norm_in_kernel=l2)
+            _no_device_error()
+            res[mode] = (o, st, y, s2)
+    finally:
+        lib.anemll_gdn_chunked_mode(prev)
+    for a, b_ in zip(res[1], res[2]):
+        assert torch.equal(a, b_)
