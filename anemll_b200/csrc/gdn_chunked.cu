@@ -819,17 +819,17 @@ gdn_chunked_kernel(const __grid_constant__ TileMaps maps, const float* __restric
 // ------------------------------------------------------------------------------------------------
 // Pipelined form: one chain per SM, 512 threads in two warp groups, and the next chunk's
 // state-independent work (D1, P/A, T, U/W) under the current chunk's state chain.
-//   intra group (warps 0-7):  chunk c + 1: D1, gates, P/A readout, T, U/W products
-//   state group (warps 8-15): chunk c:     S and W readouts, Vn/O1, Vn readout, O2 and the state
-//                                          update, output
+//   intra group (warps 0-7):  chunk c + 1: D1, gates, P/A readout, T
+//   state group (warps 8-15): chunk c:     U/W products, S and W readouts, Vn/O1, Vn readout, O2 and
+//                                          the state update, output
 // TMEM (512 columns): S^T 0-127, U|W of even chunks 128-255, of odd chunks 256-383, D1 384-511.
 // Shared memory: the q/k tiles, P and the state factors (dec rk, the O1 factor, gamma) are
 // double-buffered by chunk parity; T1/T2, A/T (fp16) and A's diagonal blocks belong to the intra
 // group, the W^T and S^T copies -> Vn and the decayed Vn -> output staging to the state group.
-// Hand-offs (mbarriers): chunk c's U|W, P and factors ready (intra -> state: the commit of its U/W
-// products and a plain arrive after P and the factors are written, so the intra group does not wait
-// for the products); U|W, P and factors of chunk c free again (state -> intra, before chunk c + 2
-// reuses them).  The v tiles are double-buffered too.  The state group requests
+// Hand-offs (mbarriers): chunk c's T1/T2, P, factors and v tile ready (intra -> state, which issues
+// the U/W products itself and reads S^T under them); chunk c's U/W products done (their commit: the
+// intra group waits for it before it rewrites T1/T2 for chunk c + 1); U|W, P and factors of chunk c
+// free again (state -> intra, before chunk c + 2 reuses them).  The v tiles are double-buffered too.  The state group requests
 // chunk c + 2's q/k tile as soon as its state update has read k.  The arithmetic is the two-CTA
 // kernel's, phase for phase, so both give the same results bit for bit.
 constexpr int PT = 512;
@@ -888,7 +888,7 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
   float* sGq = misc + PM2_GQ;
   float* sGa = misc + PM2_GA;
   float* sAd = reinterpret_cast<float*>(sm + PP_AD);
-  __shared__ uint64_t qkbar[2], vbar[2], mbarI, mbarS, iready[2], sfree[2];
+  __shared__ uint64_t qkbar[2], vbar[2], mbarI, mbarS, iready[2], uwdone[2], sfree[2];
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag, qk_issued, qk_done, v_issued, v_done, uw_issued;
 
@@ -940,8 +940,10 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
     tc::mbar_init(&vbar[1], 1);
     tc::mbar_init(&mbarI, 1);
     tc::mbar_init(&mbarS, 1);
-    tc::mbar_init(&iready[0], 2);  // the U/W commit and the arrive after P and the factors
-    tc::mbar_init(&iready[1], 2);
+    tc::mbar_init(&iready[0], 1);
+    tc::mbar_init(&iready[1], 1);
+    tc::mbar_init(&uwdone[0], 1);
+    tc::mbar_init(&uwdone[1], 1);
     tc::mbar_init(&sfree[0], 1);
     tc::mbar_init(&sfree[1], 1);
     tc::fence_mbar_init();
@@ -1019,14 +1021,6 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
       if (ti == 0) qk_done = c;
       cp_async_wait<0>();
       if (c + 1 < nchunks) issue_gb(c + 1);
-      // chunk c - 1's U/W products have read T1/T2 and their v tile: request chunk c + 1's v there
-      if (c >= 1) {
-        if (!group_and(1, tc::mbar_wait(tc::smem_u32(&iready[buf ^ 1]), (uint32_t)(((c - 1) >> 1) & 1)))) {
-          fail();
-          break;
-        }
-        if (ti == 0 && c + 1 < nchunks) issue_v(c + 1);
-      }
       // U|W, P and the factors of this parity are free once chunk c - 2's state chain has read them
       if (c >= 2 && !group_and(1, tc::mbar_wait(tc::smem_u32(&sfree[buf]), (uint32_t)(((c - 2) >> 1) & 1)))) {
         fail();
@@ -1148,6 +1142,15 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
       }
       group_sync(1);
 
+      // chunk c - 1's U/W products (the state group issues them) have read T1/T2 and their v tile:
+      // request chunk c + 1's v there
+      if (c >= 1) {
+        if (!group_and(1, tc::mbar_wait(tc::smem_u32(&uwdone[buf ^ 1]), (uint32_t)(((c - 1) >> 1) & 1)))) {
+          fail();
+          break;
+        }
+        if (ti == 0 && c + 1 < nchunks) issue_v(c + 1);
+      }
       // ---------------- T = (I + A)^-1 -> T1 = T diag(beta), T2 = T diag(beta e^G rk), hi|lo ----------------
       // (1) threads 0-63: diagonal 16x16 blocks, thread (blk, j) solves column j by right-looking
       //     substitution and writes it to T (fp16) and T1, T2 (hi|lo)
@@ -1292,29 +1295,8 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
         break;
       }
       if (ti == 0) v_done = c;
-      sync_smem_for_mma();
-      // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T (hi and lo parts) ----------------
-      // T1, T2 are lower triangular: k-step s (tokens j in [16 s, 16 s + 16)) only reaches output
-      // tokens i >= 16 s, so it runs with N = 64 - 16 s on B rows and D columns from 16 s
-      if (ti == 0) {
-#pragma unroll
-        for (int part = 0; part < 2; ++part) {
-#pragma unroll
-          for (int s = 0; s < 4; ++s) {
-            const uint32_t id = tc::idesc_f16(128, 64 - 16 * s, true, false, false, kBF);
-            const uint64_t av = tc::sdesc_sw128(sbase + PP_V + buf * 2 * T64_BLK + s * 2048, T64_BLK, 1024);
-            const uint64_t b1 = tc::sdesc_sw128(sbase + (part ? PP_T1L : PP_T1H) + s * 2048 + s * 32, 16, 1024);
-            tc::mma_f16(tmem + col_u + 16 * s, av, b1, id, part > 0 || s > 0);
-            const uint64_t ak = tc::sdesc_sw128(sbase + (PP_QK + buf * 2 * QK_BLK) + 64 * 128 + s * 2048, QK_BLK, 1024);
-            const uint64_t b2 = tc::sdesc_sw128(sbase + (part ? PP_T2L : PP_T2H) + s * 2048 + s * 32, 16, 1024);
-            tc::mma_f16(tmem + col_u + 64 + 16 * s, ak, b2, id, part > 0 || s > 0);
-          }
-        }
-        tc::commit(tc::smem_u32(&iready[buf]));  // one of the chunk-ready barrier's two arrivals
-        uw_issued = c;
-      }
-
-      // chunk c's P and factors are ready for the state group (its U|W once the commit above arrives)
+      tc::fence_async_smem();  // T1/T2 and P are operands of the state group's products
+      // chunk c's T1/T2, P, factors and v tile are ready for the state group
       tc::fence_before();
       group_sync(1);
       if (ti == 0) mbar_arrive(tc::smem_u32(&iready[buf]));
@@ -1334,33 +1316,57 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
         break;
       }
       tc::fence_after();
-      // ---------------- S^T -> the S^T copy (S^T *= gamma in TMEM) and the W^T readout (MN-major operand) ----------------
+      // ---------------- U^T = V^T T1^T ; W^T = K^T T2^T (hi and lo parts) ----------------
+      // T1, T2 are lower triangular: k-step s (tokens j in [16 s, 16 s + 16)) only reaches output
+      // tokens i >= 16 s, so it runs with N = 64 - 16 s on B rows and D columns from 16 s
+      if (ti == 0) {
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+            const uint32_t id = tc::idesc_f16(128, 64 - 16 * s, true, false, false, kBF);
+            const uint64_t av = tc::sdesc_sw128(sbase + PP_V + buf * 2 * T64_BLK + s * 2048, T64_BLK, 1024);
+            const uint64_t b1 = tc::sdesc_sw128(sbase + (part ? PP_T1L : PP_T1H) + s * 2048 + s * 32, 16, 1024);
+            tc::mma_f16(tmem + col_u + 16 * s, av, b1, id, part > 0 || s > 0);
+            const uint64_t ak = tc::sdesc_sw128(sbase + (PP_QK + buf * 2 * QK_BLK) + 64 * 128 + s * 2048, QK_BLK, 1024);
+            const uint64_t b2 = tc::sdesc_sw128(sbase + (part ? PP_T2L : PP_T2H) + s * 2048 + s * 32, 16, 1024);
+            tc::mma_f16(tmem + col_u + 64 + 16 * s, ak, b2, id, part > 0 || s > 0);
+          }
+        }
+        tc::commit(tc::smem_u32(&uwdone[buf]));
+        uw_issued = c;
+      }
+
+      // ---------------- meanwhile: S^T -> the S^T copy (S^T *= gamma in TMEM) ----------------
       {
         const float gamma = misc[PM2_GAM + buf];
-        float s32[32], r0[32];
-        tc::tmem_ld32(lane_addr + PCOL_S + 32 * hf, s32);
-        tc::tmem_wait_ld();
+        float s32[32];
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          tc::tmem_ld32(lane_addr + PCOL_S + 64 * hh + 32 * hf, s32);
+          tc::tmem_wait_ld();
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
-          *reinterpret_cast<uint4*>(sm + PP_SB0 + sw(row, 4 * hf + cb)) = pack8<TIn>(s32 + cb * 8);
+          for (int cb = 0; cb < 4; ++cb)
+            *reinterpret_cast<uint4*>(sm + (hh ? PP_SB1 : PP_SB0) + sw(row, 4 * hf + cb)) = pack8<TIn>(s32 + cb * 8);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) s32[e] *= gamma;
-        tc::tmem_st32(lane_addr + PCOL_S + 32 * hf, s32);
+          for (int e = 0; e < 32; ++e) s32[e] *= gamma;
+          tc::tmem_st32(lane_addr + PCOL_S + 64 * hh + 32 * hf, s32);
+        }
         tc::tmem_wait_st();
+      }
+      // ---------------- W^T readout (MN-major operand) once the U/W products are done ----------------
+      if (!group_and(2, tc::mbar_wait(tc::smem_u32(&uwdone[buf]), (uint32_t)((c >> 1) & 1)))) {
+        fail();
+        break;
+      }
+      tc::fence_after();
+      {
+        float r0[32];
         tc::tmem_ld32(lane_addr + col_u + 64 + 32 * hf, r0);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb)
           *reinterpret_cast<uint4*>(sm + PP_W + sw(row, 4 * hf + cb)) = pack8<TIn>(r0 + cb * 8);
-        tc::tmem_ld32(lane_addr + PCOL_S + 64 + 32 * hf, s32);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int cb = 0; cb < 4; ++cb)
-          *reinterpret_cast<uint4*>(sm + PP_SB1 + sw(row, 4 * hf + cb)) = pack8<TIn>(s32 + cb * 8);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s32[e] *= gamma;
-        tc::tmem_st32(lane_addr + PCOL_S + 64 + 32 * hf, s32);
-        tc::tmem_wait_st();
       }
       sync_smem_for_mma();
 
@@ -1533,7 +1539,7 @@ gdn_chunked_pipe_kernel(const __grid_constant__ TileMaps maps, const float* __re
       tc::mbar_wait(tc::smem_u32(&vbar[cc & 1]), (uint32_t)((cc >> 1) & 1));
     // U/W products of a stopped run complete before TMEM is released
     if (abort_flag && uw_issued >= 0)
-      tc::mbar_wait(tc::smem_u32(&iready[uw_issued & 1]), (uint32_t)((uw_issued >> 1) & 1));
+      tc::mbar_wait(tc::smem_u32(&uwdone[uw_issued & 1]), (uint32_t)((uw_issued >> 1) & 1));
   }
   // ---- final state (state group) ----
   if (!intra && !abort_flag) {
