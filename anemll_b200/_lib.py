@@ -29,9 +29,6 @@ _SIGS = {
                                     _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp], _c_int),
     "anemll_gdn_chunked_error": ([_c_int], _c_int),
     "anemll_gdn_chunked_mode": ([_c_int], _c_int),
-    "anemll_gdn_recurrent_gated": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_i64, _vp, _c_float, _vp, _c_int,
-                                    _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _vp],
-                                   _c_int),
     "anemll_gdn_chunked_prefill_gated": ([_vp, _vp, _vp, _c_int, _vp, _vp, _vp, _vp, _c_i64, _vp, _c_float, _vp,
                                           _c_int, _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                           _c_float, _c_int, _vp], _c_int),

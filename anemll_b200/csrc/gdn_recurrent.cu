@@ -15,16 +15,6 @@
 //   S     = e^g S + k delta^T
 // Semantics follow torch_recurrent_gated_delta_rule (transformers 5.5.0,
 // modeling_qwen3_5.py:314-353).
-//
-// Gated form (anemll_gdn_recurrent_gated): the layer's gated RMSNorm
-// (Qwen3_5RMSNormGated, modeling_qwen3_5.py:175-190) is applied to o before it
-// leaves the SM.  Its sum of squares runs over all d_v columns of a head, which
-// are spread over the head's d_v / DVT CTAs, so those CTAs are launched as one
-// thread-block cluster: each publishes its slice's partial sum in shared memory
-// and, after a cluster barrier, reads the others' through distributed shared
-// memory (the same sum, in the same order, on every CTA).
-#include <cooperative_groups.h>
-
 #include "common.cuh"
 
 namespace anemll {
@@ -32,23 +22,12 @@ namespace {
 
 constexpr int DK = 128;
 
-// The gated RMSNorm's extra operands: z rows (token row b*T + t, z_ld elements apart, heads dense),
-// the weight [d_v], eps, and an optional fp32 copy of the core output o (NULL: not written).
-template <typename TZ>
-struct GatedNorm {
-  const TZ* z;
-  long long z_ld;
-  const float* w;
-  float eps;
-  float* core_out;
-};
-
-template <typename TIn, typename TOut, int DVT, int NT, bool GATED>
+template <typename TIn, typename TOut, int DVT, int NT>
 __global__ void __launch_bounds__(NT)
 gdn_recurrent_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const TIn* __restrict__ v,
                      const float* __restrict__ g, const float* __restrict__ beta,
                      float* __restrict__ state, TOut* __restrict__ out,
-                     int T, int Hqk, int Hv, int dv, float scale, int l2norm, const GatedNorm<TOut> gn) {
+                     int T, int Hqk, int Hv, int dv, float scale, int l2norm) {
   constexpr int CG = DVT / 4;   // float4 column groups per row
   constexpr int RG = NT / CG;   // row groups
   constexpr int RPT = DK / RG;  // rows per thread
@@ -80,7 +59,6 @@ gdn_recurrent_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const
   __shared__ float sk[2][DK];
   __shared__ float red[2][2][NWARP][DVT];
   __shared__ float scal[2][4];
-  __shared__ float ssq[2];  // gated form: this slice's partial sum of squares of o, by token parity
 
   for (int t = 0; t < T; ++t) {
     const int p = t & 1;
@@ -157,35 +135,7 @@ gdn_recurrent_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const
       delta[c] = bt * (vv[c] - dec * a);
       o[c] = dec * bb + delta[c] * kq;
     }
-    if constexpr (GATED) {
-      // this CTA's partial sum of squares of o (threads rg == 0 hold the slice's columns, in warp 0),
-      // then the whole row's sum from every CTA of the cluster (the head's slices, in rank order)
-      if (warp == 0) {
-        float part = rg == 0 ? o[0] * o[0] + o[1] * o[1] + o[2] * o[2] + o[3] * o[3] : 0.f;
-        part = warp_sum(part);
-        if (lane == 0) ssq[p] = part;
-      }
-      cooperative_groups::cluster_group cluster = cooperative_groups::this_cluster();
-      cluster.sync();
-      if (rg == 0) {
-        float tot = 0.f;
-        const int nslices = (int)cluster.num_blocks();
-        for (int r = 0; r < nslices; ++r) tot += *cluster.map_shared_rank(&ssq[p], r);
-        const float rn = rsqrtf(tot / (float)dv + gn.eps);
-        const TOut* zt = gn.z + (long long)tok * gn.z_ld + (long long)hv * dv + col0;
-        TOut* ot = out + (tok * Hv + hv) * dv + col0;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float zc = to_f32(zt[c]);
-          ot[c] = from_f32<TOut>(gn.w[col0 + c] * o[c] * rn * __fdividef(zc, 1.0f + __expf(-zc)));
-        }
-        if (gn.core_out) {
-          float* co = gn.core_out + (tok * Hv + hv) * dv + col0;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) co[c] = o[c];
-        }
-      }
-    } else if (rg == 0) {
+    if (rg == 0) {
       TOut* ot = out + (tok * Hv + hv) * dv + col0;
 #pragma unroll
       for (int c = 0; c < 4; ++c) ot[c] = from_f32<TOut>(o[c]);
@@ -206,8 +156,6 @@ gdn_recurrent_kernel(const TIn* __restrict__ q, const TIn* __restrict__ k, const
     const int r = rg + i * RG;
     *reinterpret_cast<float4*>(S + (size_t)r * dv + col0) = s[i];
   }
-  // gated form: no CTA leaves while another may still read its partial sums
-  if constexpr (GATED) cooperative_groups::this_cluster().sync();
 }
 
 template <typename TIn, typename TOut>
@@ -217,55 +165,16 @@ int launch_recurrent(const void* q, const void* k, const void* v, const float* g
   // Narrow slices when there are few (b, h) pairs so the grid still covers the SMs.
   const long pairs = (long)B * Hv;
   const bool narrow = pairs * (dv / 32) < 2 * 148 && (dv % 16) == 0;
-  const GatedNorm<TOut> none{nullptr, 0, nullptr, 0.f, nullptr};
   if (narrow) {
     dim3 grid(dv / 16, Hv, B);
-    gdn_recurrent_kernel<TIn, TOut, 16, 128, false><<<grid, 128, 0, st>>>(
-        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm,
-        none);
+    gdn_recurrent_kernel<TIn, TOut, 16, 128><<<grid, 128, 0, st>>>(
+        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm);
   } else {
     dim3 grid(dv / 32, Hv, B);
-    gdn_recurrent_kernel<TIn, TOut, 32, 128, false><<<grid, 128, 0, st>>>(
-        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm,
-        none);
+    gdn_recurrent_kernel<TIn, TOut, 32, 128><<<grid, 128, 0, st>>>(
+        (const TIn*)q, (const TIn*)k, (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm);
   }
   return launch_status("gdn_recurrent");
-}
-
-// Gated form: one cluster per (sequence, value head), its dv / DVT slices (at most 8, the portable
-// cluster size).
-template <typename TIn, typename TOut, int DVT>
-int launch_recurrent_gated_dvt(const void* q, const void* k, const void* v, const float* g, const float* beta,
-                               float* state, void* out, int B, int T, int Hqk, int Hv, int dv, float scale,
-                               int l2norm, const GatedNorm<TOut>& gn, cudaStream_t st) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(dv / DVT, Hv, B);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = dv / DVT;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, gdn_recurrent_kernel<TIn, TOut, DVT, 128, true>, (const TIn*)q, (const TIn*)k,
-                     (const TIn*)v, g, beta, state, (TOut*)out, T, Hqk, Hv, dv, scale, l2norm, gn);
-  return launch_status("gdn_recurrent_gated");
-}
-
-template <typename TIn, typename TOut>
-int launch_recurrent_gated(const void* q, const void* k, const void* v, const float* g, const float* beta,
-                           float* state, void* out, int B, int T, int Hqk, int Hv, int dv, float scale, int l2norm,
-                           const GatedNorm<TOut>& gn, cudaStream_t st) {
-  const long pairs = (long)B * Hv;
-  const bool narrow = pairs * (dv / 32) < 2 * 148 && dv / 16 <= 8;
-  if (narrow)
-    return launch_recurrent_gated_dvt<TIn, TOut, 16>(q, k, v, g, beta, state, out, B, T, Hqk, Hv, dv, scale, l2norm,
-                                                     gn, st);
-  return launch_recurrent_gated_dvt<TIn, TOut, 32>(q, k, v, g, beta, state, out, B, T, Hqk, Hv, dv, scale, l2norm,
-                                                   gn, st);
 }
 
 }  // namespace
@@ -293,39 +202,6 @@ extern "C" int anemll_gdn_recurrent(const void* q, const void* k, const void* v,
   return ANEMLL_DISPATCH_DTYPE(qkv_dtype, TIn, [&] {
     return ANEMLL_DISPATCH_DTYPE(out_dtype, TOut, [&] {
       return launch_recurrent<TIn, TOut>(q, k, v, g, beta, state, out, B, T, H_qk, H_v, d_v, scale, qk_l2norm, st);
-    });
-  });
-}
-
-extern "C" int anemll_gdn_recurrent_gated(const void* q, const void* k, const void* v, int qkv_dtype,
-                                          const float* g, const float* beta, float* state,
-                                          const void* z, int64_t z_row_stride, const float* norm_weight, float eps,
-                                          void* out, int out_dtype, float* core_out,
-                                          int B, int T, int H_qk, int H_v, int d_k, int d_v,
-                                          float scale, int qk_l2norm, void* stream) {
-  ANEMLL_REQUIRE(state && (T == 0 || (q && k && v && g && beta && z && norm_weight && out)), ANEMLL_EINVAL,
-                 "gdn_recurrent_gated: null pointer");
-  ANEMLL_REQUIRE(B > 0 && T >= 0 && H_qk > 0 && H_v > 0, ANEMLL_EINVAL,
-                 "gdn_recurrent_gated: bad sizes B=%d T=%d H_qk=%d H_v=%d", B, T, H_qk, H_v);
-  ANEMLL_REQUIRE(H_v % H_qk == 0, ANEMLL_EINVAL, "gdn_recurrent_gated: H_v (%d) must be a multiple of H_qk (%d)",
-                 H_v, H_qk);
-  ANEMLL_REQUIRE(d_k == DK, ANEMLL_EUNSUPPORTED, "gdn_recurrent_gated: d_k must be 128 (got %d)", d_k);
-  ANEMLL_REQUIRE(d_v > 0 && d_v % 32 == 0 && d_v <= 256, ANEMLL_EUNSUPPORTED,
-                 "gdn_recurrent_gated: d_v must be a multiple of 32 up to 256 (got %d)", d_v);
-  ANEMLL_REQUIRE(dtype_ok(qkv_dtype) && (out_dtype == ANEMLL_F16 || out_dtype == ANEMLL_BF16), ANEMLL_EUNSUPPORTED,
-                 "gdn_recurrent_gated: q/k/v f32, f16 or bf16; out (and z) f16 or bf16");
-  if (z_row_stride == 0) z_row_stride = (int64_t)H_v * d_v;
-  ANEMLL_REQUIRE(z_row_stride >= (int64_t)H_v * d_v, ANEMLL_EINVAL,
-                 "gdn_recurrent_gated: z row stride shorter than H_v * d_v");
-  ANEMLL_REQUIRE(aligned(state, 16), ANEMLL_EALIGN, "gdn_recurrent_gated: state must be 16-byte aligned");
-  if (T == 0) return ANEMLL_OK;
-  if (scale <= 0.f) scale = 1.0f / sqrtf((float)d_k);
-  cudaStream_t st = (cudaStream_t)stream;
-  return ANEMLL_DISPATCH_DTYPE(qkv_dtype, TIn, [&] {
-    return ANEMLL_DISPATCH_HALF(out_dtype, TOut, [&] {
-      const GatedNorm<TOut> gn{(const TOut*)z, (long long)z_row_stride, norm_weight, eps, core_out};
-      return launch_recurrent_gated<TIn, TOut>(q, k, v, g, beta, state, out, B, T, H_qk, H_v, d_v, scale, qk_l2norm,
-                                               gn, st);
     });
   });
 }

@@ -141,12 +141,15 @@ def _z_rows(z, B, T, H, d):
 def gated_delta_rule_norm_(query, key, value, g, beta, state, z, norm_weight, eps=1e-6, chunked=True,
                            chunk_size=64, scale=None, use_qk_l2norm_in_kernel=False, out=None, out_dtype=None,
                            core_out=None):
-    """The delta rule with the layer's gated RMSNorm fused into its epilogue: returns
+    """The delta rule followed by the layer's gated RMSNorm: returns
     ``norm_weight * o * rsqrt(mean(o^2) + eps) * silu(z)`` [B, T, H_v, d_v] (``out_dtype``, default
     ``z.dtype``: fp16 or bf16), where ``o`` is the core output of :func:`chunk_gated_delta_rule_`
-    (``chunked``) or :func:`recurrent_gated_delta_rule_`.  ``state`` is updated in place; ``core_out``
-    (fp32 [B, T, H_v, d_v], optional) also receives ``o``.  ``z`` [B, T, H_v, d_v] may be a column
-    slice of the layer's fused projection output.  Replaces the core call and ``self.norm`` of
+    (``chunked``) or :func:`recurrent_gated_delta_rule_`.  The chunked prefill applies the norm in its
+    epilogue, so ``o`` never goes through HBM; the recurrent form runs the recurrent kernel and then
+    :func:`gated_rmsnorm` (fused recurrent forms measured slower: the norm's sum over d_v spans the
+    CTAs that split a head's state).  ``state`` is updated in place; ``core_out`` (fp32
+    [B, T, H_v, d_v], optional) also receives ``o``.  ``z`` [B, T, H_v, d_v] may be a column slice of
+    the layer's fused projection output.  Replaces the core call and ``self.norm`` of
     ``Qwen3_5GatedDeltaNet.forward`` (modeling_qwen3_5.py:497-523, 175-190)."""
     _need_cuda(query, key, value, g, beta, state, z, norm_weight, core_out)
     for n, t in (("query", query), ("key", key), ("value", value), ("g", g), ("beta", beta), ("state", state)):
@@ -168,6 +171,11 @@ def gated_delta_rule_norm_(query, key, value, g, beta, state, z, norm_weight, ep
         raise TypeError("the gated output is fp16 or bf16")
     if z.dtype != out_dtype:
         z = z.to(out_dtype)
+    if not chunked:
+        o = core_out if core_out is not None else torch.empty(B, T, H_v, d_v, dtype=torch.float32,
+                                                              device=query.device)
+        recurrent_gated_delta_rule_(query, key, value, g, beta, state, scale, use_qk_l2norm_in_kernel, out=o)
+        return gated_rmsnorm(o, z, norm_weight, eps, out_dtype=out_dtype, out=out)
     z, z_ld = _z_rows(z, B, T, H_v, d_v)
     if chunked and (z_ld * z.element_size()) % 16:
         z, z_ld = z.contiguous(), H_v * d_v
@@ -183,12 +191,8 @@ def gated_delta_rule_norm_(query, key, value, g, beta, state, z, norm_weight, ep
             _lib.ptr(core_out), B, T, H_qk, H_v, d_k, d_v)
     tail = (float(scale) if scale is not None else 0.0, int(bool(use_qk_l2norm_in_kernel)),
             _lib.stream_ptr(query.device))
-    if chunked:
-        rc = lib.anemll_gdn_chunked_prefill_gated(*args, int(chunk_size), *tail)
-        _lib.check(rc, "anemll_gdn_chunked_prefill_gated")
-    else:
-        rc = lib.anemll_gdn_recurrent_gated(*args, *tail)
-        _lib.check(rc, "anemll_gdn_recurrent_gated")
+    rc = lib.anemll_gdn_chunked_prefill_gated(*args, int(chunk_size), *tail)
+    _lib.check(rc, "anemll_gdn_chunked_prefill_gated")
     return out
 
 
@@ -285,7 +289,7 @@ def gdn_prologue(mixed_qkv, conv_weight, conv_state, a, b, A_log, dt_bias, num_k
     return q, k, v, g, beta
 
 
-def gated_rmsnorm(x, z, weight, eps=1e-6, out_dtype=None):
+def gated_rmsnorm(x, z, weight, eps=1e-6, out_dtype=None, out=None):
     """``weight * x * rsqrt(mean(x^2)+eps) * silu(z)`` over the last dim.  ``z`` may be a column slice
     of a wider projection output: [B, T, H, d] with dense heads and a uniform token stride."""
     _need_cuda(x, z, weight)
@@ -304,7 +308,10 @@ def gated_rmsnorm(x, z, weight, eps=1e-6, out_dtype=None):
         if not ok:
             z, z_heads, z_ld = z.contiguous(), 0, 0
     w = weight.float().contiguous()
-    out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    elif out.shape != x.shape or not out.is_contiguous():
+        raise ValueError("gated_rmsnorm: out must be a contiguous tensor of x's shape")
     rc = _lib.load().anemll_gated_rmsnorm(_lib.ptr(x), _lib.dtype_code(x.dtype), _lib.ptr(z), _lib.dtype_code(z.dtype),
                                           _lib.ptr(w), _lib.ptr(out), _lib.dtype_code(out.dtype), x.numel() // d, d,
                                           float(eps), z_heads, z_ld, _lib.stream_ptr(x.device))

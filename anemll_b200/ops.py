@@ -14,7 +14,8 @@ beta, state, scale, use_qk_l2norm)``   ``modeling_qwen3_5.py:234-311``); ``state
 state, scale, use_qk_l2norm)``
 ``gdn_gated_delta_rule_norm(q, k, v,   the core call and ``self.norm`` (``Qwen3_5RMSNormGated``)
 g, beta, state, z, norm_weight, eps,   of ``Qwen3_5GatedDeltaNet.forward`` (497-523, 175-190):
-chunked, scale, use_qk_l2norm)``       either kernel above with the gated RMSNorm in its epilogue
+chunked, scale, use_qk_l2norm)``       the chunked prefill with the norm in its epilogue, or the
+                                       recurrent kernel followed by the norm kernel
 ``gdn_prologue(mixed_qkv, conv_weight, the conv/split/l2-norm/gate part of
 conv_state, a, b, A_log, dt_bias,      ``Qwen3_5GatedDeltaNet.forward`` (453-496);
 H_qk, H_v, d_k, d_v, use_state)``      ``conv_state`` updated

@@ -87,26 +87,20 @@ int anemll_gdn_chunked_prefill(const void* q, const void* k, const void* v, int 
                                int chunk_size, float scale, int qk_l2norm, void* stream);
 
 /*
- * The two delta-rule kernels above with the layer's gated RMSNorm in their
- * epilogue: out = norm_weight * o * rsqrt(mean(o^2) + eps) * silu(z) over d_v,
- * o being the core output the plain call would return.  Replaces the core call
- * together with self.norm (Qwen3_5RMSNormGated) in Qwen3_5GatedDeltaNet.forward
+ * The chunked prefill with the layer's gated RMSNorm in its epilogue:
+ * out = norm_weight * o * rsqrt(mean(o^2) + eps) * silu(z) over d_v, o being
+ * the core output the plain call would return.  Replaces the core call together
+ * with self.norm (Qwen3_5RMSNormGated) in Qwen3_5GatedDeltaNet.forward
  * (transformers 5.5.0 modeling_qwen3_5.py:497-523, the norm 175-190), so that o
  * never travels through HBM.  z [B, T, H_v, d_v] has the output's dtype
  * (ANEMLL_F16 or ANEMLL_BF16) with dense heads and token rows z_row_stride
- * elements apart (0: H_v * d_v), so it may be a column slice of the layer's
- * fused projection output; norm_weight [d_v] fp32.  core_out (fp32
- * [B, T, H_v, d_v], or NULL) also receives o.  Other arguments as above.
- * The recurrent form launches the d_v / 32 (or / 16) CTAs of a head as one
- * thread-block cluster (d_v <= 256); the chunked form needs 16-byte aligned
- * out, z rows, norm_weight and core_out.
+ * elements apart (0: H_v * d_v; 16-byte aligned), so it may be a column slice
+ * of the layer's fused projection output; norm_weight [d_v] fp32 (16-byte
+ * aligned).  core_out (fp32 [B, T, H_v, d_v], 16-byte aligned, or NULL) also
+ * receives o.  Other arguments as anemll_gdn_chunked_prefill.  (Decode keeps the
+ * recurrent kernel and anemll_gated_rmsnorm: the fused recurrent forms measured
+ * slower.)
  */
-int anemll_gdn_recurrent_gated(const void* q, const void* k, const void* v, int qkv_dtype,
-                               const float* g, const float* beta, float* state,
-                               const void* z, int64_t z_row_stride, const float* norm_weight, float eps,
-                               void* out, int out_dtype, float* core_out,
-                               int B, int T, int H_qk, int H_v, int d_k, int d_v,
-                               float scale, int qk_l2norm, void* stream);
 int anemll_gdn_chunked_prefill_gated(const void* q, const void* k, const void* v, int qkv_dtype,
                                      const float* g, const float* beta, float* state,
                                      const void* z, int64_t z_row_stride, const float* norm_weight, float eps,

@@ -48,16 +48,15 @@ def test_recurrent_rejects_null_and_head_ratio():
     assert lib.anemll_gdn_recurrent(p, p, p, 2, p, p, p, p, 2, 1, 1, 3, 4, 128, 128, 0.0, 1, None) < 0
 
 
-def test_gated_forms_reject_bad_arguments():
+def test_gated_prefill_rejects_bad_arguments():
     lib = _lib.load()
     p = ctypes.c_void_p(16)
     # the gated output (and z) is fp16 or bf16
-    rc = lib.anemll_gdn_recurrent_gated(p, p, p, 2, p, p, p, p, 0, p, 1e-6, p, 0, None, 1, 1, 1, 2, 128, 128, 0.0, 0,
-                                        None)
+    rc = lib.anemll_gdn_chunked_prefill_gated(p, p, p, 2, p, p, p, p, 0, p, 1e-6, p, 0, None, 1, 64, 1, 2, 128, 128,
+                                              64, 0.0, 0, None)
     assert rc < 0 and b"out" in lib.anemll_last_error()
-    # a head's slices must fit one cluster
-    rc = lib.anemll_gdn_recurrent_gated(p, p, p, 2, p, p, p, p, 0, p, 1e-6, p, 2, None, 1, 1, 1, 2, 128, 512, 0.0, 0,
-                                        None)
+    rc = lib.anemll_gdn_chunked_prefill_gated(p, p, p, 2, p, p, p, p, 0, p, 1e-6, p, 2, None, 1, 64, 1, 2, 128, 256,
+                                              64, 0.0, 0, None)
     assert rc < 0 and b"d_v" in lib.anemll_last_error()
     # z rows shorter than H_v * d_v
     rc = lib.anemll_gdn_chunked_prefill_gated(p, p, p, 2, p, p, p, p, 64, p, 1e-6, p, 2, None, 1, 64, 1, 2, 128, 128,

@@ -1,6 +1,6 @@
-"""The delta-rule kernels with the gated RMSNorm in their epilogue (``gated_delta_rule_norm_``,
-``anemll_gdn_chunked_prefill_gated`` / ``anemll_gdn_recurrent_gated``) against the unfused calls
-and the CPU oracle.
+"""The delta rule followed by the layer's gated RMSNorm (``gated_delta_rule_norm_``: the chunked
+prefill with the norm in its epilogue, ``anemll_gdn_chunked_prefill_gated``, and the recurrent kernel
+followed by ``anemll_gated_rmsnorm``) against the unfused calls and the CPU oracle.
 
 * The core output the fused launch also writes (``core_out``) and the updated state are bit for bit
   those of the plain kernel: the epilogue only adds the norm.
@@ -11,9 +11,9 @@ and the CPU oracle.
   of the sum of squares: every element within one ulp of the output type.
 * z read in place as a column slice of a wider projection output gives the contiguous result.
 
-Shapes cover the chunked kernel with a ragged last chunk, the recurrent kernel with the narrow
-(16-column slices, clusters of 8) and the wide (32-column slices, clusters of 4) grids, one and
-several tokens per launch.
+Shapes cover the chunked kernels (the pipelined one-chain-per-SM kernel at these chain counts) with
+a ragged last chunk, and the recurrent path with its narrow (16-column) and wide (32-column) slice
+grids, one and several tokens per launch.
 """
 import pytest
 import torch
@@ -54,9 +54,9 @@ def _inputs(B, T, Hqk, Hv, seed, dtype=torch.bfloat16, wide_z=True):
 CASES = [  # (B, T, H_qk, H_v, chunked)
     (2, 200, 2, 4, True),     # two full chunks and a ragged one
     (1, 64, 16, 32, True),    # the full head shape, one chunk
-    (2, 1, 2, 4, False),      # narrow recurrent grid: clusters of 8
+    (2, 1, 2, 4, False),      # narrow recurrent grid (16-column slices)
     (3, 5, 2, 4, False),      # several tokens per launch
-    (4, 1, 16, 32, False),    # wide grid: clusters of 4
+    (4, 1, 16, 32, False),    # wide grid (32-column slices)
 ]
 
 
