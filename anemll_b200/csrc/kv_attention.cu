@@ -549,16 +549,26 @@ size_t workspace_bytes_for(int n_splits, int B, int S, int Hq, int Hkv, int hd) 
 // 16 tokens, rows head-major: row = head * 16 + token) and one key split; K/V
 // blocks of 64 keys arrive by TMA (double-buffered) straight from the cache.
 // Per block: S = Q K^T into TMEM (tcgen05, M=128 N=64 K=hd), an online softmax
-// on CUDA cores (thread = row) writes fp16 P to shared memory, O += P V on the
-// tensor core into TMEM (M=128 N=hd K=64).  The running max is kept stale until
-// it grows by more than 2^8, so O in TMEM is rescaled only then.  The new cache
-// rows are copied from k_new / v_new into the landed K/V tiles of every CTA whose
-// blocks hold them, and row-tile-0 CTAs store them into the cache.  Partials use
-// the same workspace format and combine kernel as the mma.sync path.
+// on CUDA cores writes fp16 P to shared memory, O += P V on the tensor core
+// into TMEM (M=128 N=hd K=64).  Two threads share each row (256 threads: warps
+// w and w + 4 read TMEM lane quarter w), each taking half of the row's score
+// columns, half of O's columns in a rescale and half of the epilogue; the two
+// halves meet once per block, on the row maximum.  The running max is kept
+// stale until it grows by more than 2^8, so O in TMEM is rescaled only then.
+// The new cache rows are copied from k_new / v_new into the landed K/V tiles of
+// every CTA whose blocks hold them, and row-tile-0 CTAs store them into the
+// cache.  Partials use the same workspace format and combine kernel as the
+// mma.sync path; they leave the CTA as one 128-row fp32 tile, staged in shared
+// memory and written by TMA stores.
 constexpr int TC_KB = 64;  // keys per block
+constexpr int TC_NT = 256;  // threads: two per query row
 
 struct KvTcMaps {
   CUtensorMap q, k, v;
+  // split partials of the tcgen05 prefill path (n_splits > 1), fp32, as {column, token, head, block =
+  // (sequence, kv head, split)}: a {32, 16, 8, 1} box is one 32-column slice of a 128-row tile in the
+  // kernel's head-major row order, stored into the workspace's token-major rows (row = token G + head)
+  CUtensorMap o;
 };
 
 __device__ int g_kv_tc_error = 0;
@@ -566,7 +576,7 @@ __device__ int g_kv_tc_error = 0;
 __device__ __forceinline__ uint32_t swz128(int r, int ch) { return (uint32_t)(r * 128 + ((ch ^ (r & 7)) << 4)); }
 
 template <typename T, int HD>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(TC_NT, 1)
 kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   griddep_wait();
   constexpr int NKB = HD / 64;                 // 64-element column blocks of a row
@@ -577,12 +587,15 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   constexpr int OFF_V = OFF_K + 2 * NKB * KV_BLK;
   constexpr int OFF_P = OFF_V + 2 * NKB * KV_BLK;
   constexpr uint32_t COL_SB = 0, COL_O = 256;  // S: two 64-column buffers; O: HD columns
+  constexpr int SLICES = HD / 32;              // 32-column slices of an O row
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t mbar, qbar, kvbar[2];
   __shared__ uint32_t tmem_slot;
+  __shared__ float s_half[2][128];  // per row: each half's block maximum, then its running sum
 
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & 127, half = tid >> 7;  // query row (TMEM lane) and which half of its columns
   const int G = p.Hq / p.Hkv;  // == 8
   const int bh = blockIdx.z, b = bh / p.Hkv, kvh = bh % p.Hkv;
   const int tile = blockIdx.x, split = blockIdx.y;
@@ -599,7 +612,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   const uint32_t bar = tc::smem_u32(&mbar), qb = tc::smem_u32(&qbar), kvb0 = tc::smem_u32(&kvbar[0]);
 
   // this thread's row: head g, token s
-  const int g = tid >> 4, s = tile * 16 + (tid & 15);
+  const int g = row >> 4, s = tile * 16 + (row & 15);
   const bool row_valid = s < p.S;
   const int qpos = p.pos + s;
   int lo = 0;
@@ -639,7 +652,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   if (tid == 0) {
     tc::mbar_arrive_expect_tx(qb, (uint32_t)(NKB * Q_BLK));
 #pragma unroll
@@ -659,13 +672,13 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   float* f_w = reinterpret_cast<float*>(sm + OFF_P);
   static_assert(16 * FLD * 4 <= NKB * KV_BLK && HD * 4 <= 128 * 128, "staged tables fit the idle buffers");
   if (p.fused) {
-    for (int i = tid; i < 2 * 16 * (HD / 4); i += 128) {
+    for (int i = tid; i < 2 * 16 * (HD / 4); i += TC_NT) {
       const int tb = i / (16 * (HD / 4)), rem = i % (16 * (HD / 4)), st = rem / (HD / 4), c4 = rem % (HD / 4);
       if (tile * 16 + st < p.S)
         cp_async16((tb ? f_sin : f_cos) + st * FLD + c4 * 4,
                    (tb ? p.sin_t : p.cos_t) + (long long)(p.pos + tile * 16 + st) * HD + c4 * 4);
     }
-    for (int i = tid; i < HD / 4; i += 128) cp_async16(f_w + i * 4, p.qnw + i * 4);
+    for (int i = tid; i < HD / 4; i += TC_NT) cp_async16(f_w + i * 4, p.qnw + i * 4);
     cp_async_commit();
   }
   bool ok = __syncthreads_and(tc::mbar_wait(qb, 0));
@@ -674,15 +687,15 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     __syncthreads();
   }
   if (p.fused && ok) {
-    // head norm + RoPE of this thread's query row, in place in the swizzled tile (thread tid owns
-    // row tid: head tid / 16, token tile * 16 + tid % 16); same arithmetic as head_norm_rope_warp
-    const int srow = tile * 16 + (tid & 15);
-    if (srow < p.S) {
+    // head norm + RoPE of the query rows, in place in the swizzled tile (the first half's thread
+    // owns row `row`: head row / 16, token tile * 16 + row % 16); same arithmetic as
+    // head_norm_rope_warp
+    if (half == 0 && row_valid) {
       constexpr int EPL = HD / 32, PPC = 8 / EPL;  // elements per partial, partials per 8-element chunk
       float part[32];
 #pragma unroll
       for (int k = 0; k < HD / 8; ++k) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sm + OFF_Q + (k >> 3) * Q_BLK + swz128(tid, k & 7));
+        const uint4 u = *reinterpret_cast<const uint4*>(sm + OFF_Q + (k >> 3) * Q_BLK + swz128(row, k & 7));
         const T* h = reinterpret_cast<const T*>(&u);
 #pragma unroll
         for (int q2 = 0; q2 < PPC; ++q2) {
@@ -696,13 +709,13 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         }
       }
       const float rn = head_norm_scale(part, HD, p.eps);
-      const float* cr = f_cos + (tid & 15) * FLD;
-      const float* sr = f_sin + (tid & 15) * FLD;
+      const float* cr = f_cos + (row & 15) * FLD;
+      const float* sr = f_sin + (row & 15) * FLD;
 #pragma unroll 1
       for (int k = 0; k < HD / 16; ++k) {  // chunk k of the first half with chunk k + HD/16
         const int k2 = k + HD / 16;
-        uint8_t* pl = sm + OFF_Q + (k >> 3) * Q_BLK + swz128(tid, k & 7);
-        uint8_t* ph = sm + OFF_Q + (k2 >> 3) * Q_BLK + swz128(tid, k2 & 7);
+        uint8_t* pl = sm + OFF_Q + (k >> 3) * Q_BLK + swz128(row, k & 7);
+        uint8_t* ph = sm + OFF_Q + (k2 >> 3) * Q_BLK + swz128(row, k2 & 7);
         uint4 ul = *reinterpret_cast<const uint4*>(pl), uh = *reinterpret_cast<const uint4*>(ph);
         T* hl = reinterpret_cast<T*>(&ul);
         T* hh = reinterpret_cast<T*>(&uh);
@@ -725,7 +738,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     __syncthreads();
   }
   uint32_t phase = 0;
-  float m_run = -INFINITY, l_run = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // l_run: this half's share of the row sum
   int pending = nblk > 0 ? 0 : -1;  // K/V block requested and not yet waited for
 
 #pragma unroll 1
@@ -749,11 +762,11 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       // four vectors per thread in flight at a time (loads first, then stores)
       constexpr int PU = 4;
       const int n_items = (j1 - j0) * (HD / 8);
-      for (int i0 = tid; i0 < n_items; i0 += PU * 128) {
+      for (int i0 = tid; i0 < n_items; i0 += PU * TC_NT) {
         uint4 kv[PU], vv[PU];
 #pragma unroll
         for (int u = 0; u < PU; ++u) {
-          const int i = i0 + u * 128;
+          const int i = i0 + u * TC_NT;
           if (i < n_items) {
             const int jj = j0 + i / (HD / 8), ch = i % (HD / 8);
             kv[u] = *reinterpret_cast<const uint4*>(kn + (long long)(jj - p.pos) * HD + ch * 8);
@@ -762,7 +775,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         }
 #pragma unroll
         for (int u = 0; u < PU; ++u) {
-          const int i = i0 + u * 128;
+          const int i = i0 + u * TC_NT;
           if (i < n_items) {
             const int jj = j0 + i / (HD / 8), ch = i % (HD / 8), r = jj - key0;
             *reinterpret_cast<uint4*>(sm + OFF_K + (buf * NKB + (ch >> 3)) * KV_BLK + swz128(r, ch & 7)) = kv[u];
@@ -794,25 +807,24 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     phase ^= 1u;
     if (!ok) break;
     tc::fence_after();
-    // online softmax (base 2) of this row's 64 scores
-    float x[64];
-    tc::tmem_ld32(lane_addr + COL_SB + buf * 64, x);
-    tc::tmem_ld32(lane_addr + COL_SB + buf * 64 + 32, x + 32);
+    // online softmax (base 2): this thread's 32 of the row's 64 scores
+    float x[32];
+    tc::tmem_ld32(lane_addr + COL_SB + buf * 64 + half * 32, x);
     tc::tmem_wait_ld();
     float mb = -INFINITY;
     if (!p.mask) {
-      // keys visible to this row form one interval of the block: [vlo, vhi]
-      const int vlo = max(lo, key0) - key0;
-      const int vhi = row_valid ? min(qpos, k_end - 1) - key0 : -1;
+      // keys visible to this row form one interval of the block: [vlo, vhi] (block columns)
+      const int vlo = max(lo, key0) - key0 - half * 32;
+      const int vhi = (row_valid ? min(qpos, k_end - 1) - key0 : -1) - half * 32;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
+      for (int e = 0; e < 32; ++e) {
         x[e] = (e >= vlo && e <= vhi) ? x[e] * p.scale_log2 : -INFINITY;
         mb = fmaxf(mb, x[e]);
       }
     } else {
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
-        const int kj = key0 + e;
+      for (int e = 0; e < 32; ++e) {
+        const int kj = key0 + half * 32 + e;
         float v = x[e] * p.scale_log2;
         bool vis = row_valid && kj < k_end;
         if (vis) {
@@ -827,6 +839,10 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
         mb = fmaxf(mb, x[e]);
       }
     }
+    // the row's block maximum over both halves (the halves then take the same rescale decisions)
+    s_half[half][row] = mb;
+    __syncthreads();
+    mb = fmaxf(s_half[0][row], s_half[1][row]);
     float alpha = 1.f;
     bool rescale = false;
     if (mb > m_run + 8.f) {  // also true when m_run is still -inf
@@ -839,7 +855,7 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     const float base = m_run == -INFINITY ? 0.f : m_run;
     float ls = 0.f;
 #pragma unroll
-    for (int cb = 0; cb < 8; ++cb) {
+    for (int cb = 0; cb < 4; ++cb) {
       float p8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
@@ -850,14 +866,14 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
       T* h = reinterpret_cast<T*>(&u);
 #pragma unroll
       for (int e = 0; e < 8; ++e) h[e] = from_f32<T>(p8[e]);
-      *reinterpret_cast<uint4*>(sm + OFF_P + swz128(tid, cb)) = u;
+      *reinterpret_cast<uint4*>(sm + OFF_P + swz128(row, half * 4 + cb)) = u;
     }
     l_run = l_run * alpha + ls;
     if (key0 + TC_KB > k_end) {
       // V rows past the split end (unwritten cache rows, possibly not finite) are zeroed, so that
       // their zero weights give exact zeros in P V
       const int nz = key0 + TC_KB - k_end;
-      for (int i = tid; i < nz * NKB * 8; i += 128) {
+      for (int i = tid; i < nz * NKB * 8; i += TC_NT) {
         const int r = TC_KB - nz + i / (NKB * 8), c = (i / 8) % NKB, u = i % 8;
         *reinterpret_cast<uint4*>(sm + OFF_V + (buf * NKB + c) * KV_BLK + r * 128 + u * 16) =
             make_uint4(0, 0, 0, 0);
@@ -865,13 +881,14 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
     }
     if (__any_sync(0xffffffffu, rescale)) {  // warp-collective TMEM access; alpha = 1 on other lanes
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+      for (int c = 0; c < SLICES / 2; ++c) {  // this half's columns of O
         float o[32];
-        tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+        const uint32_t col = COL_O + (uint32_t)(half * (HD / 2) + c * 32);
+        tc::tmem_ld32(lane_addr + col, o);
         tc::tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; ++e) o[e] *= alpha;
-        tc::tmem_st32(lane_addr + COL_O + c * 32, o);
+        tc::tmem_st32(lane_addr + col, o);
       }
       tc::tmem_wait_st();
     }
@@ -898,73 +915,102 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
   if (pending >= 0 && !ok) tc::mbar_wait(kvb0 + 8u * (pending & 1), (uint32_t)((pending >> 1) & 1));
   griddep_launch_dependents();
 
-  // ---- epilogue: O rows leave through shared memory (the P tile) in 32-column slices, so
-  //      that global stores are whole 128-byte row segments ----
   if (ok) {
     const int R = p.S * G;
-    float* stage = reinterpret_cast<float*>(sm + OFF_P);  // [128 rows][32 floats], float4 index swizzled
-    const float scale_row = p.n_splits == 1 ? (nblk > 0 && l_run > 0.f ? 1.f / l_run : 0.f) : 1.f;
-    if (p.n_splits > 1 && row_valid) {
-      const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)s * G + g;
-      p.ws_ml[row_id * 2 + 0] = m_run;
-      p.ws_ml[row_id * 2 + 1] = l_run;
-    }
-    // the tile's gate rows are copied into shared memory in one go (the Q and K regions are free:
-    // every MMA has completed), so that no store of the slices below waits on a global load
-    const bool gated = p.n_splits == 1 && p.gate != nullptr;
-    constexpr int GLD = HD + 8;  // staged gate row stride (elements): 16-byte units, banks spread
-    T* gs = reinterpret_cast<T*>(sm + OFF_Q);
-    static_assert(128 * GLD * (int)sizeof(T) <= OFF_V - OFF_Q, "the gate tile fits in the Q and K regions");
-    if (gated) {
-      for (int i = tid; i < 128 * (HD / 8); i += 128) {
-        const int r = i / (HD / 8), ch = i % (HD / 8);
-        const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
-        if (rs < p.S)
-          cp_async16(gs + r * GLD + ch * 8, reinterpret_cast<const T*>(p.gate) + gate_index(p, b, rs, hq, ch * 8));
+    s_half[half][row] = l_run;  // (every block's reads of s_half are done: barriers since)
+    __syncthreads();
+    const float l_row = s_half[0][row] + s_half[1][row];
+    if (p.n_splits > 1) {
+      // ---- partial: the unnormalised 128-row O tile is staged in shared memory in 32-column
+      //      slices [slice][128 rows][32 floats] with the 128-byte swizzle (the Q and K regions:
+      //      every MMA has completed) and leaves by TMA stores; tokens past S are not written ----
+      if (half == 0 && row_valid) {
+        const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)s * G + g;
+        p.ws_ml[row_id * 2 + 0] = m_run;
+        p.ws_ml[row_id * 2 + 1] = l_row;
       }
-      cp_async_commit();
-      cp_async_wait<0>();
-      __syncthreads();
-    }
+      static_assert(SLICES * 128 * 128 <= OFF_V - OFF_Q, "the staged O tile fits in the Q and K regions");
 #pragma unroll 1
-    for (int c = 0; c < HD / 32; ++c) {
-      float o[32];
-      if (nblk > 0) {  // uniform across the CTA: every lane takes part in the warp-wide TMEM load
-        tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
-        tc::tmem_wait_ld();
-      } else {
+      for (int c0 = 0; c0 < SLICES / 2; ++c0) {
+        const int c = half * (SLICES / 2) + c0;
+        float o[32];
+        if (nblk > 0) {  // uniform across the CTA: every lane takes part in the warp-wide TMEM load
+          tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) o[e] = 0.f;
-      }
-#pragma unroll
-      for (int c4 = 0; c4 < 8; ++c4)
-        *reinterpret_cast<float4*>(stage + tid * 32 + ((c4 ^ (tid & 7)) << 2)) =
-            make_float4(o[c4 * 4] * scale_row, o[c4 * 4 + 1] * scale_row, o[c4 * 4 + 2] * scale_row,
-                        o[c4 * 4 + 3] * scale_row);
-      __syncthreads();
-      if (p.n_splits > 1) {
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int idx = tid + it * 128, r = idx >> 3, c4 = idx & 7;
-          const int rs = tile * 16 + (r & 15), rg = r >> 4;
-          if (rs < p.S) {
-            const long long row_id = ((long long)bh * p.n_splits + split) * R + (long long)rs * G + rg;
-            *reinterpret_cast<float4*>(p.ws_o + row_id * HD + c * 32 + c4 * 4) =
-                *reinterpret_cast<const float4*>(stage + r * 32 + ((c4 ^ (r & 7)) << 2));
-          }
+          for (int e = 0; e < 32; ++e) o[e] = 0.f;
         }
-      } else {
+        uint8_t* dst = sm + OFF_Q + c * (128 * 128);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4)
+          *reinterpret_cast<float4*>(dst + swz128(row, c4)) =
+              make_float4(o[c4 * 4], o[c4 * 4 + 1], o[c4 * 4 + 2], o[c4 * 4 + 3]);
+      }
+      tc::fence_async_smem();  // generic writes before the TMA engine reads the tile
+      __syncthreads();
+      if (tid == 0) {
+#pragma unroll 1
+        for (int c = 0; c < SLICES; ++c)
+          tc::tma_store_4d(&maps.o, sbase + OFF_Q + c * (128 * 128), c * 32, tile * 16, 0, bh * p.n_splits + split);
+        tc::bulk_commit();
+        tc::bulk_wait_all();
+      }
+    } else {
+      // ---- final rows: O / l, gated, through shared memory in 32-column slices (the two halves
+      //      stage slices 2 c2 and 2 c2 + 1 side by side), so that global stores are whole 64-byte
+      //      row segments ----
+      const float scale_row = nblk > 0 && l_row > 0.f ? 1.f / l_row : 0.f;
+      // the tile's gate rows are copied into shared memory in one go (the Q and K regions are free:
+      // every MMA has completed), so that no store of the slices below waits on a global load
+      const bool gated = p.gate != nullptr;
+      constexpr int GLD = HD + 8;  // staged gate row stride (elements): 16-byte units, banks spread
+      T* gs = reinterpret_cast<T*>(sm + OFF_Q);
+      static_assert(128 * GLD * (int)sizeof(T) <= OFF_V - OFF_Q, "the gate tile fits in the Q and K regions");
+      if (gated) {
+        for (int i = tid; i < 128 * (HD / 8); i += TC_NT) {
+          const int r = i / (HD / 8), ch = i % (HD / 8);
+          const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
+          if (rs < p.S)
+            cp_async16(gs + r * GLD + ch * 8, reinterpret_cast<const T*>(p.gate) + gate_index(p, b, rs, hq, ch * 8));
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+      }
+#pragma unroll 1
+      for (int c2 = 0; c2 < SLICES / 2; ++c2) {
+        {
+          const int c = 2 * c2 + half;
+          float o[32];
+          if (nblk > 0) {
+            tc::tmem_ld32(lane_addr + COL_O + c * 32, o);
+            tc::tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0.f;
+          }
+          float* stage = reinterpret_cast<float*>(sm + (half ? OFF_V : OFF_P));  // [128][32], float4 swizzled
+#pragma unroll
+          for (int c4 = 0; c4 < 8; ++c4)
+            *reinterpret_cast<float4*>(stage + row * 32 + ((c4 ^ (row & 7)) << 2)) =
+                make_float4(o[c4 * 4] * scale_row, o[c4 * 4 + 1] * scale_row, o[c4 * 4 + 2] * scale_row,
+                            o[c4 * 4 + 3] * scale_row);
+        }
+        __syncthreads();
 #pragma unroll
         for (int it = 0; it < 4; ++it) {
-          const int idx = tid + it * 128, r = idx >> 2, c8 = idx & 3;
+          const int idx = tid + it * TC_NT, sl = idx >> 9, r = (idx >> 2) & 127, c8 = idx & 3;
+          const int col = (2 * c2 + sl) * 32 + c8 * 8;
           const int rs = tile * 16 + (r & 15), hq = kvh * G + (r >> 4);
-          const long long off = ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD + c * 32 + c8 * 8;
+          const long long off = ((long long)b * p.S + rs) * p.Hq * HD + (long long)hq * HD + col;
           if (rs < p.S) {
+            const float* stage = reinterpret_cast<const float*>(sm + (sl ? OFF_V : OFF_P));
             const float4 a = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8) ^ (r & 7)) << 2));
             const float4 bq = *reinterpret_cast<const float4*>(stage + r * 32 + (((2 * c8 + 1) ^ (r & 7)) << 2));
             float v[8] = {a.x, a.y, a.z, a.w, bq.x, bq.y, bq.z, bq.w};
             if (gated) {
-              const uint4 gu = *reinterpret_cast<const uint4*>(gs + r * GLD + c * 32 + c8 * 8);
+              const uint4 gu = *reinterpret_cast<const uint4*>(gs + r * GLD + col);
               const T* gh = reinterpret_cast<const T*>(&gu);
 #pragma unroll
               for (int e = 0; e < 8; ++e) v[e] *= sigmoid_fast(to_f32(gh[e]));
@@ -976,8 +1022,8 @@ kv_attn_tc_kernel(const __grid_constant__ KvTcMaps maps, KvParams p) {
             *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.out) + off) = u;
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
   // the other warps' epilogue reads of TMEM must finish before the allocation is released
@@ -1393,11 +1439,11 @@ PFN_cuTensorMapEncodeTiled_v12000 kv_map_encoder() {
 }
 
 int kv_encode(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
-              const cuuint32_t* box) {
+              const cuuint32_t* box, CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT16) {
   auto enc = kv_map_encoder();
   ANEMLL_REQUIRE(enc, ANEMLL_EUNSUPPORTED, "kv_attention: cuTensorMapEncodeTiled unavailable");
   const cuuint32_t es[4] = {1, 1, 1, 1};
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
+  const CUresult r = enc(m, dt, (cuuint32_t)rank, const_cast<void*>(base), dims, strides,
                          box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   ANEMLL_REQUIRE(r == CUDA_SUCCESS, ANEMLL_EINVAL, "kv_attention: tensor map encoding failed (%d)", (int)r);
@@ -1577,6 +1623,14 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
       rc = kv_encode(&maps.q, p.q, 3, dq, sq, bq);
     }
     if (!rc) rc = kv_cache_maps(maps, p, HD);
+    if (!rc && n_splits > 1) {  // partials {column, token, head, (sequence, kv head, split)}, fp32
+      const int G = p.Hq / p.Hkv;
+      const cuuint64_t dm[4] = {(cuuint64_t)HD, (cuuint64_t)p.S, (cuuint64_t)G,
+                                (cuuint64_t)p.B * p.Hkv * n_splits};
+      const cuuint64_t sm4[3] = {(cuuint64_t)G * HD * 4, (cuuint64_t)HD * 4, (cuuint64_t)p.S * G * HD * 4};
+      const cuuint32_t bm[4] = {32, 16, 8, 1};
+      rc = kv_encode(&maps.o, q.ws_o, 4, dm, sm4, bm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32);
+    }
     if (rc) return rc;
   }
   constexpr int NKB = HD / 64;
@@ -1584,7 +1638,7 @@ int launch_kv_tc(KvParams& p, const Plan& pl0, cudaStream_t st) {
   auto kern = kv_attn_tc_kernel<T, HD>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(row_tiles, n_splits, p.B * p.Hkv);
-  int rc = launch_pdl("kv_attention_tc", kern, grid, dim3(128), smem, st, maps, q);
+  int rc = launch_pdl("kv_attention_tc", kern, grid, dim3(TC_NT), smem, st, maps, q);
   if (rc) return rc;
   if (n_splits > 1) {
     rc = launch_combine<T, HD>(q, st);

@@ -219,15 +219,15 @@ def bench_gdn_decode(args, ws, rank, local):
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(ms, ws, dev)
 
-    # end to end through the public op with host buffers: H2D of the step's
-    # inputs from pinned memory, the kernel, D2H of the step's output
+    # End to end through the public op with host buffers.  Serial form: every step copies its five
+    # inputs from pinned memory, runs the op and reads its output back, all on one stream.
     hq, hk, hv, hg, hb = (w[n].pin_memory() for n in ("q", "k", "v", "g", "beta"))
     dq, dk_, dv_, dg, db = (torch.empty_like(x[0], device=dev) for x in (hq, hk, hv, hg, hb))
     hout = torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16).pin_memory()
     h2d = sum(x[0].numel() * x.element_size() for x in (hq, hk, hv, hg, hb))
     d2h = hout.numel() * hout.element_size()
 
-    def e2e_step(i):
+    def e2e_serial_step(i):
         t = i % DECODE_STEPS
         dq.copy_(hq[t], non_blocking=True)
         dk_.copy_(hk[t], non_blocking=True)
@@ -237,17 +237,70 @@ def bench_gdn_decode(args, ws, rank, local):
         gdn.recurrent_gated_delta_rule_(dq, dk_, dv_, dg, db, states[i & 1], out=out)
         hout.copy_(out, non_blocking=True)
 
-    for i in range(args.warmup):
-        e2e_step(i)
-    torch.cuda.synchronize(dev)
-    barrier(ws)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), ws, dev)
+    def timed_e2e(step_fn, streams=()):
+        for i in range(args.warmup):
+            step_fn(i)
+        torch.cuda.synchronize(dev)
+        barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s2 in streams:  # the copy streams start with the timed region ...
+            s2.wait_event(e0)
+        for i in range(args.steps):
+            step_fn(i)
+        for s2 in streams:  # ... and it ends after their last copy
+            stream.wait_stream(s2)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return max_over_ranks(e0.elapsed_time(e1), ws, dev)
+
+    e2e_serial_ms = timed_e2e(e2e_serial_step)
+
+    # Pipelined form (the headline e2e): a serving loop that keeps the kernel busy.  Each step's
+    # inputs sit in one pinned host buffer and go to the device in one copy on a copy stream, a
+    # step ahead of the kernel; the output comes back on a third stream while the next step
+    # computes.  Device input and output buffers are double-buffered, guarded by events.
+    names = ("q", "k", "v", "g", "beta")
+    sizes = [w[n][0].numel() * w[n].element_size() for n in names]
+    offs, o = [], 0
+    for sz in sizes:
+        offs.append(o)
+        o += (sz + 255) // 256 * 256
+    step_bytes = o
+    hin = torch.empty(DECODE_STEPS, step_bytes, dtype=torch.uint8).pin_memory()
+    for t in range(DECODE_STEPS):
+        for n, off, sz in zip(names, offs, sizes):
+            hin[t, off:off + sz].copy_(w[n][t].contiguous().view(-1).view(torch.uint8))
+    din = [torch.empty(step_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
+    views = [tuple(din[b][off:off + sz].view(w[n].dtype).view(w[n][0].shape) for n, off, sz in zip(names, offs, sizes))
+             for b in range(2)]
+    douts = [torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    houts = torch.empty(2, DECODE_B, 1, H_V, DV, dtype=torch.bfloat16).pin_memory()
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_k = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def e2e_step(i):
+        b = i & 1
+        if i >= 2:
+            s_in.wait_event(ev_k[b])  # kernel i - 2 is done with din[b]
+        with torch.cuda.stream(s_in):
+            din[b].copy_(hin[i % DECODE_STEPS], non_blocking=True)
+        ev_in[b].record(s_in)
+        stream.wait_event(ev_in[b])
+        if i >= 2:
+            stream.wait_event(ev_out[b])  # step i - 2's output has been read back from douts[b]
+        gdn.recurrent_gated_delta_rule_(*views[b], states[i & 1], out=douts[b])
+        ev_k[b].record(stream)
+        s_out.wait_event(ev_k[b])
+        with torch.cuda.stream(s_out):
+            houts[b].copy_(douts[b], non_blocking=True)
+        ev_out[b].record(s_out)
+
+    e2e_ms = timed_e2e(e2e_step, (s_in, s_out))
+    if not torch.equal(houts[(args.steps - 1) & 1].to(dev), douts[(args.steps - 1) & 1]):
+        raise RuntimeError("e2e: the last step's output read back does not match the device copy")
 
     pk, how = peaks()
     per_launch_s = ms / 1e3 / args.steps
@@ -276,8 +329,13 @@ def bench_gdn_decode(args, ws, rank, local):
                      "traffic": traffic_from_profiles("gdn_recurrent_decode"),
                      "dram_frac": dram_frac(traffic_from_profiles("gdn_recurrent_decode"), per_launch_s,
                                             pk["hbm_gbs"])},
-        "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": step_bytes,
+                "d2h_bytes_per_step": d2h,
+                "form": "pipelined: one H2D copy of the step's packed inputs on a copy stream a step ahead, "
+                        "the public op, the output's D2H on a third stream (double-buffered, events)"},
+        "e2e_serial": {"value": ws * args.steps / (e2e_serial_ms / 1e3), "unit": "steps/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "form": "five H2D copies, the public op and the D2H copy on one stream"},
         "gpu_launches": args.steps,
     }
     res["clocks"] = clk.summary()
