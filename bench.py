@@ -10,9 +10,11 @@ its own batch of 64 sequences; no collective on the data path.
                   [--config gdn_decode|gdn_prefill|kv_attention|gdn_layer|cache_ops|stack]
 
 Without ``--config`` the decode line also carries, as secondary lines, the
-chunked prefill (8 x 32768 tokens, the tensor-core kernel) and the KV-cache
-attention pass (causal and with a 512-token window), each with its own
-roofline, e2e leg and CPU baseline.  ``--config X`` prints X's line alone.
+chunked prefill (8 x 32768 tokens, the tensor-core kernel), the KV-cache
+attention pass (causal and with a 512-token window), the gated delta-rule layer
+(512-token prefill + 64 decode steps) and the 24-layer hybrid stack (128 x
+(1024 + 256) tokens), each with its own roofline, e2e leg and CPU baseline.
+``--config X`` prints X's line alone.
 
 ``--impl reference`` times the CPU oracle of the same path on the host cores
 (the reference has no GPU implementation of this path), rank 0 only.
@@ -665,6 +667,40 @@ def bench_kv_attention(args, ws, rank, local):
 
 # ------------------------------------------------------------- GDN layer ----
 LAYER_PREFILL, LAYER_DECODE, HIDDEN = 512, 64, 2048
+
+
+def layer_config(ws):
+    return {"workload": "gdn_layer", "batch_per_gpu": 1, "prefill": LAYER_PREFILL, "decode_steps": LAYER_DECODE,
+            "hidden": HIDDEN, "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV, "chunk": CHUNK,
+            "l2": "flushed (256 MB write) before the prefill and before the decode steps of every timed pass",
+            "parallelism": f"weak, {ws} independent sequences"}
+
+
+CACHE_NL, CACHE_H, CACHE_SW, CACHE_HD = 18, 1, 512, 256
+
+
+def cache_ops_config(ws):
+    return {"workload": "kv_cache_ops", "local_layers": CACHE_NL, "window": CACHE_SW, "H_kv": CACHE_H,
+            "head_dim": CACHE_HD, "mask_tokens": 64, "resize": "36x1x1024x256 -> 4096 rows, position 1000",
+            "calls_per_step": 4 * CACHE_NL + 1,
+            "l2": "flushed (256 MB write) before every timed step",
+            "parallelism": f"weak, {ws} replicas"}
+
+
+def stack_config(ws, seqs=None, prefill=None, decode=None):
+    from anemll_b200.stack import StackConfig
+    cfg = StackConfig()
+    seqs = STACK_B if seqs is None else seqs
+    prefill = STACK_PREFILL if prefill is None else prefill
+    decode = STACK_DECODE if decode is None else decode
+    n_att = sum(cfg.is_attention(i) for i in range(cfg.n_layers))
+    return {"workload": "hybrid_stack", "sequences": seqs, "sequences_per_gpu": seqs // ws,
+            "prefill": prefill, "decode_steps": decode, "layers": cfg.n_layers,
+            "attention_layers": n_att, "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab,
+            "ctx": cfg.ctx, "gdn": f"H_qk {cfg.H_qk}, H_v {cfg.H_v}, d {cfg.d_k}",
+            "attention": f"H_q {cfg.H_q}, H_kv {cfg.H_kv}, hd {cfg.head_dim}",
+            "l2": "flushed (256 MB write) before every timed pass; weights and states exceed L2",
+            "parallelism": f"sequences split over {ws} GPUs, NCCL all-gather of next-token ids"}
 LAYER_PROJ = 2 * H_QK * DK + 2 * H_V * DV + 2 * H_V  # in_proj_qkv | in_proj_z | in_proj_b | in_proj_a rows
 
 
@@ -795,10 +831,7 @@ def bench_gdn_layer(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "bf16 activations and weights, f32 state",
         "data": "synthetic (seeded; hidden ~N(0,1), weights ~N(0,0.02), conv ~N(0,0.1), A_log ~U(0, log 16))",
-        "config": {"workload": "gdn_layer", "batch_per_gpu": 1, "prefill": LAYER_PREFILL, "decode_steps": LAYER_DECODE,
-                   "hidden": HIDDEN, "H_qk": H_QK, "H_v": H_V, "d_k": DK, "d_v": DV, "chunk": CHUNK,
-                   "l2": "flushed (256 MB write) before the prefill and before the decode steps of every timed pass",
-                   "parallelism": f"weak, {ws} independent sequences"},
+        "config": layer_config(ws),
         "prefill_ms": pre_ms / args.steps,
         "decode_us_per_step": dec_ms / args.steps / LAYER_DECODE * 1e3,
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
@@ -826,7 +859,7 @@ def bench_cache_ops(args, ws, rank, local):
     from anemll_b200 import _lib as lib, cache_ops
     dev = torch.device("cuda", local)
     g = torch.Generator().manual_seed(6 + rank)
-    nl, H, sw, hd = 18, 1, 512, 256
+    nl, H, sw, hd = CACHE_NL, CACHE_H, CACHE_SW, CACHE_HD
     kv = torch.randn(2 * nl, H, sw, hd, generator=g).half().to(dev)
     key = torch.randn(1, H, 1, hd, generator=g).half().to(dev)
     val = torch.randn(1, H, 1, hd, generator=g).half().to(dev)
@@ -917,11 +950,7 @@ def bench_cache_ops(args, ws, rank, local):
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": "kv_cache_ops", "local_layers": nl, "window": sw, "H_kv": H, "head_dim": hd,
-                   "mask_tokens": 64, "resize": "36x1x1024x256 -> 4096 rows, position 1000",
-                   "calls_per_step": 2 * nl + 2 * nl + 1,
-                   "l2": "flushed (256 MB write) before every timed step",
-                   "parallelism": f"weak, {ws} replicas"},
+        "config": cache_ops_config(ws),
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": gbs / pk["hbm_gbs"], "peak_source": how, "algorithmic_bytes_per_step": bytes_step,
                      "traffic": None,
@@ -1058,13 +1087,7 @@ def bench_stack(args, ws, rank, local):
         "dtype": "bf16 activations and weights, f32 GDN states",
         "data": "synthetic (uniform random prompt ids, seed 4; weights ~N(0,0.02), conv ~N(0,0.1), "
                 "A_log ~U(0, log 16))",
-        "config": {"workload": "hybrid_stack", "sequences": STACK_B, "sequences_per_gpu": B,
-                   "prefill": STACK_PREFILL, "decode_steps": STACK_DECODE, "layers": cfg.n_layers,
-                   "attention_layers": n_att, "hidden": cfg.hidden, "ffn": cfg.ffn, "vocab": cfg.vocab,
-                   "ctx": cfg.ctx, "gdn": f"H_qk {cfg.H_qk}, H_v {cfg.H_v}, d {cfg.d_k}",
-                   "attention": f"H_q {cfg.H_q}, H_kv {cfg.H_kv}, hd {cfg.head_dim}",
-                   "l2": "flushed (256 MB write) before every timed pass; weights and states exceed L2",
-                   "parallelism": f"sequences split over {ws} GPUs, NCCL all-gather of next-token ids"},
+        "config": stack_config(ws, STACK_B, STACK_PREFILL, STACK_DECODE),
         "prefill_tokens_per_s": STACK_B * STACK_PREFILL * args.steps / (pre_max / 1e3),
         "decode_steps_per_s": STACK_DECODE * args.steps / (dec_max / 1e3),
         "prefill_ms": pre_max / args.steps,
@@ -1311,7 +1334,11 @@ def reference_config(config, ws, window):
         return prefill_config(ws)
     if config == "kv_attention":
         return kv_config(ws, window)
-    return {"workload": {"gdn_layer": "gdn_layer", "cache_ops": "kv_cache_ops", "stack": "hybrid_stack"}[config]}
+    if config == "gdn_layer":
+        return layer_config(ws)
+    if config == "cache_ops":
+        return cache_ops_config(ws)
+    return stack_config(ws)
 
 
 def reference_line(config, args, ws, threads, window=0):
@@ -1357,8 +1384,8 @@ def reference_arm(args, ws, rank):
 
 # the secondary lines of the default run: (key, config, window, steps, warmup)
 SECONDARY = (("prefill", "gdn_prefill", 0), ("kv_attention", "kv_attention", 0),
-             ("kv_attention_window", "kv_attention", 512))
-SECONDARY_STEPS = {"gdn_prefill": (20, 5), "kv_attention": (50, 5)}
+             ("kv_attention_window", "kv_attention", 512), ("layer", "gdn_layer", 0), ("stack", "stack", 0))
+SECONDARY_STEPS = {"gdn_prefill": (20, 5), "kv_attention": (50, 5), "gdn_layer": (50, 5), "stack": (3, 3)}
 
 
 def cpu_baseline_for(config, args, threads, window=0):
