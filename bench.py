@@ -145,6 +145,23 @@ DECODE_B, DECODE_STEPS = 64, 256
 H_QK, H_V, DK, DV = 16, 32, 128, 128
 
 
+def cudart():
+    """The CUDA runtime that torch has loaded, for the e2e legs' stream-ordered copies and events:
+    cudaMemcpyAsync, cudaEventRecord and cudaStreamWaitEvent called directly (one C call each)."""
+    import ctypes
+    rt = ctypes.CDLL("libcudart.so.12")
+    vp, sz, ci = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int
+    rt.cudaMemcpyAsync.argtypes = [vp, vp, sz, ci, vp]
+    rt.cudaEventRecord.argtypes = [vp, vp]
+    rt.cudaStreamWaitEvent.argtypes = [vp, vp, ctypes.c_uint]
+    rt.cudaEventCreateWithFlags.argtypes = [ctypes.POINTER(vp), ctypes.c_uint]
+    rt.cudaEventDestroy.argtypes = [vp]
+    for f in ("cudaMemcpyAsync", "cudaEventRecord", "cudaStreamWaitEvent", "cudaEventCreateWithFlags",
+              "cudaEventDestroy"):
+        getattr(rt, f).restype = ci
+    return rt
+
+
 def decode_bytes_per_step(B=DECODE_B):
     state = 2 * B * H_V * DK * DV * 4
     qk = 2 * B * H_QK * DK * 2
@@ -258,10 +275,12 @@ def bench_gdn_decode(args, ws, rank, local):
 
     e2e_serial_ms = timed_e2e(e2e_serial_step)
 
-    # Pipelined form (the headline e2e): a serving loop that keeps the kernel busy.  Each step's
-    # inputs sit in one pinned host buffer and go to the device in one copy on a copy stream, a
-    # step ahead of the kernel; the output comes back on a third stream while the next step
-    # computes.  Device input and output buffers are double-buffered, guarded by events.
+    # Pipelined form (the headline e2e): a serving loop that keeps the kernel busy, driving the C-ABI
+    # entry point (anemll_gdn_recurrent) and the CUDA runtime directly, so that the host issues a step
+    # in a few microseconds.  Each step's inputs sit in one pinned host buffer and go to the device in
+    # one copy on a copy stream, a step ahead of the kernel; the output comes back on a third stream
+    # while the next step computes.  Device input and output buffers are double-buffered, guarded by
+    # events.
     names = ("q", "k", "v", "g", "beta")
     sizes = [w[n][0].numel() * w[n].element_size() for n in names]
     offs, o = [], 0
@@ -274,35 +293,61 @@ def bench_gdn_decode(args, ws, rank, local):
         for n, off, sz in zip(names, offs, sizes):
             hin[t, off:off + sz].copy_(w[n][t].contiguous().view(-1).view(torch.uint8))
     din = [torch.empty(step_bytes, dtype=torch.uint8, device=dev) for _ in range(2)]
-    views = [tuple(din[b][off:off + sz].view(w[n].dtype).view(w[n][0].shape) for n, off, sz in zip(names, offs, sizes))
-             for b in range(2)]
+    vptrs = [tuple(din[b].data_ptr() + off for off in offs) for b in range(2)]
     douts = [torch.empty(DECODE_B, 1, H_V, DV, dtype=torch.bfloat16, device=dev) for _ in range(2)]
     houts = torch.empty(2, DECODE_B, 1, H_V, DV, dtype=torch.bfloat16).pin_memory()
+    hin_p = [hin[t].data_ptr() for t in range(DECODE_STEPS)]
+    din_p, dout_p, hout_p = [x.data_ptr() for x in din], [x.data_ptr() for x in douts], [houts[b].data_ptr()
+                                                                                          for b in range(2)]
     s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_k = [torch.cuda.Event() for _ in range(2)]
-    ev_out = [torch.cuda.Event() for _ in range(2)]
+    rt = cudart()
+    h_in, h_out, h_cmp = s_in.cuda_stream, s_out.cuda_stream, stream.cuda_stream
+
+    def new_event():
+        import ctypes
+        ev = ctypes.c_void_p()
+        if rt.cudaEventCreateWithFlags(ctypes.byref(ev), 2):  # cudaEventDisableTiming
+            raise RuntimeError("cudaEventCreateWithFlags failed")
+        return ev.value
+
+    ev_in, ev_k, ev_out = ([new_event() for _ in range(2)] for _ in range(3))
+
+    def cu(rc, what):
+        if rc:
+            raise RuntimeError(f"e2e: {what} failed (CUDA error {rc})")
 
     def e2e_step(i):
         b = i & 1
         if i >= 2:
-            s_in.wait_event(ev_k[b])  # kernel i - 2 is done with din[b]
-        with torch.cuda.stream(s_in):
-            din[b].copy_(hin[i % DECODE_STEPS], non_blocking=True)
-        ev_in[b].record(s_in)
-        stream.wait_event(ev_in[b])
+            cu(rt.cudaStreamWaitEvent(h_in, ev_k[b], 0), "cudaStreamWaitEvent")  # kernel i - 2 read din[b]
+        cu(rt.cudaMemcpyAsync(din_p[b], hin_p[i % DECODE_STEPS], step_bytes, 1, h_in), "cudaMemcpyAsync")
+        cu(rt.cudaEventRecord(ev_in[b], h_in), "cudaEventRecord")
+        cu(rt.cudaStreamWaitEvent(h_cmp, ev_in[b], 0), "cudaStreamWaitEvent")
         if i >= 2:
-            stream.wait_event(ev_out[b])  # step i - 2's output has been read back from douts[b]
-        gdn.recurrent_gated_delta_rule_(*views[b], states[i & 1], out=douts[b])
-        ev_k[b].record(stream)
-        s_out.wait_event(ev_k[b])
-        with torch.cuda.stream(s_out):
-            houts[b].copy_(douts[b], non_blocking=True)
-        ev_out[b].record(s_out)
+            cu(rt.cudaStreamWaitEvent(h_cmp, ev_out[b], 0), "cudaStreamWaitEvent")  # step i - 2 read douts[b]
+        pq, pk, pv, pg, pb = vptrs[b]
+        rc = lib.anemll_gdn_recurrent(pq, pk, pv, _lib.BF16, pg, pb, sptrs[i & 1], dout_p[b], _lib.BF16,
+                                      DECODE_B, 1, H_QK, H_V, DK, DV, 0.0, 0, h_cmp)
+        if rc:
+            _lib.check(rc, "anemll_gdn_recurrent")
+        cu(rt.cudaEventRecord(ev_k[b], h_cmp), "cudaEventRecord")
+        cu(rt.cudaStreamWaitEvent(h_out, ev_k[b], 0), "cudaStreamWaitEvent")
+        cu(rt.cudaMemcpyAsync(hout_p[b], dout_p[b], d2h, 2, h_out), "cudaMemcpyAsync")
+        cu(rt.cudaEventRecord(ev_out[b], h_out), "cudaEventRecord")
 
     e2e_ms = timed_e2e(e2e_step, (s_in, s_out))
     if not torch.equal(houts[(args.steps - 1) & 1].to(dev), douts[(args.steps - 1) & 1]):
         raise RuntimeError("e2e: the last step's output read back does not match the device copy")
+    # the same copies without the kernel: how long a step's H2D and D2H take on their own (they hide
+    # under the neighbouring steps' kernels when the pipelined leg approaches the device-timed value)
+    def copy_step(i):
+        b = i & 1
+        cu(rt.cudaMemcpyAsync(din_p[b], hin_p[i % DECODE_STEPS], step_bytes, 1, h_cmp), "cudaMemcpyAsync")
+        cu(rt.cudaMemcpyAsync(hout_p[b], dout_p[b], d2h, 2, h_cmp), "cudaMemcpyAsync")
+
+    copies_ms = timed_e2e(copy_step)
+    for ev in ev_in + ev_k + ev_out:
+        rt.cudaEventDestroy(ev)
 
     pk, how = peaks()
     per_launch_s = ms / 1e3 / args.steps
@@ -334,7 +379,9 @@ def bench_gdn_decode(args, ws, rank, local):
         "e2e": {"value": ws * args.steps / (e2e_ms / 1e3), "unit": "steps/s", "h2d_bytes_per_step": step_bytes,
                 "d2h_bytes_per_step": d2h,
                 "form": "pipelined: one H2D copy of the step's packed inputs on a copy stream a step ahead, "
-                        "the public op, the output's D2H on a third stream (double-buffered, events)"},
+                        "the C-ABI call anemll_gdn_recurrent, the output's D2H on a third stream "
+                        "(double-buffered, events; copies and events through the CUDA runtime)",
+                "copies_alone_us_per_step": copies_ms / args.steps * 1e3},
         "e2e_serial": {"value": ws * args.steps / (e2e_serial_ms / 1e3), "unit": "steps/s",
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                        "form": "five H2D copies, the public op and the D2H copy on one stream"},
