@@ -196,6 +196,34 @@ def test_decode_kernels_match_oracle(hd, dt):
     assert attention.kv_device_error() == 0
 
 
+@pytest.mark.parametrize("hd", [128, 256])
+def test_tcgen05_partial_query_tiles_with_key_splits(hd):
+    """Prefill chunks on the tcgen05 path whose last 16-token query tile is partial (S = 20, 33, 100,
+    130), at positions that give every tile several key splits: the split partials leave each CTA by
+    TMA stores that must stop at the chunk's last token (later tokens would land in the next split's
+    rows), and the combine merges them.  New rows patched into the tiles (S < 128) and pre-written
+    by the copy kernel (S >= 128); causal and a 300-token window; cache bit-exact."""
+    torch.manual_seed(31 + hd)
+    Hq, Hkv, ctx = 16, 2, 4096
+    for S, pos, window in [(20, 2500, 0), (33, 1800, 0), (100, 3000, 300), (130, 2047, 0), (20, 3900, 300)]:
+        kc = torch.randn(Hkv, ctx, hd).half()
+        vc = torch.randn(Hkv, ctx, hd).half()
+        q = torch.randn(1, Hq, S, hd).half()
+        kn = torch.randn(1, Hkv, S, hd).half()
+        vn = torch.randn(1, Hkv, S, hd).half()
+        gate = torch.randn(1, S, Hq * hd).half()
+        kr, vr = kc.float().clone(), vc.float().clone()
+        kr[:, pos:pos + S] = kn[0].float()
+        vr[:, pos:pos + S] = vn[0].float()
+        ref = ok.attend(q, kr.unsqueeze(0), vr.unsqueeze(0), ok.additive_mask(S, ctx, pos, window), gate)
+        kd, vd = kc.to(DEV), vc.to(DEV)
+        out = attention.kv_attention(q.to(DEV), kd, vd, pos, k_new=kn.to(DEV), v_new=vn.to(DEV), gate=gate.to(DEV),
+                                     window=window)
+        assert_close(out.float().cpu(), ref, f"hd {hd} S {S} pos {pos} window {window}")
+        assert torch.equal(kd.cpu().float(), kr) and torch.equal(vd.cpu().float(), vr)
+    assert attention.kv_device_error() == 0
+
+
 def test_unwritten_cache_rows_are_never_read():
     """Cache rows past the visible range may hold anything, NaN included: prefill chunks (tcgen05
     path), decode steps (TMA decode kernel) and the generic kernel read none of them."""
