@@ -1184,10 +1184,14 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
   for (; c < nch; ++c) {
     const int st = c % NS;
     // the barrier also means every warp is done with chunk c - 1, whose stage is then refilled
-    // (NS >= 2 whenever a refill happens, so that stage is not the one waited for here)
+    // (with NS >= 2 that stage is not the one waited for here; with one stage the refill comes first)
+    if (NS == 1 && c >= 1) {  // one stage: every warp is done with chunk c - 1, refill it with chunk c
+      __syncthreads();
+      if (tid == 0) issue(c);
+    }
     ok = __syncthreads_and(tc::mbar_wait(full0 + 8u * st, (uint32_t)((c / NS) & 1)));
     if (!ok) break;
-    if (tid == 0 && c >= 1 && c - 1 + NS < nch) issue(c - 1 + NS);
+    if (tid == 0 && NS >= 2 && c >= 1 && c - 1 + NS < nch) issue(c - 1 + NS);
     uint8_t* Kt = sm + L::OFF_ST + st * L::STAGE;
     uint8_t* Vt = Kt + NKB * L::KV_BLK;
     const int key0 = k_begin + c * DC_KC;
@@ -1356,8 +1360,9 @@ kv_decode_kernel(const __grid_constant__ KvTcMaps maps, KvParams p, int n_stages
     atomicExch(&g_kv_tc_error, 1);
     // chunks issued and not consumed, [c, issued_end), may still be landing: wait for them
     // (bounded) before the CTA exits.  Chunks [0, NS) are issued up front and iteration
-    // c' >= 1 issues chunk c' - 1 + NS, so issued_end = min(nch, max(NS, c - 1 + NS)).
-    const int issued_end = min(nch, c == 0 ? NS : c - 1 + NS);
+    // c' >= 1 issues chunk c' - 1 + NS, so issued_end = min(nch, max(NS, c - 1 + NS)); with one
+    // stage iteration c issues chunk c itself, before its wait.
+    const int issued_end = NS == 1 ? min(nch, c + 1) : min(nch, c == 0 ? NS : c - 1 + NS);
     for (int x = c; x < issued_end; ++x) tc::mbar_wait(full0 + 8u * (x % NS), (uint32_t)((x / NS) & 1));
     return;  // block-uniform: ok came from __syncthreads_and
   }
@@ -1487,7 +1492,12 @@ int launch_kv_dec(KvParams& p, const Plan& pl0, cudaStream_t st) {
   const int cps = (nchunks + want - 1) / want;  // chunks per split
   const int ks = cps * DC_KC;
   const int n_splits = max(1, (Lk + ks - 1) / ks);
-  const int stages = min(cps, L::MAX_STAGES);
+  // One K/V stage when the grid holds two CTAs per SM at hd 256: two resident CTAs (eight warps)
+  // hide each other's loads better than one CTA with a second stage (batch 128: 80 -> 70 us a call).
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool two_per_sm = HD == 256 && (long)n_splits * base >= 2L * sms;
+  const int stages = two_per_sm ? 1 : min(cps, L::MAX_STAGES);
   KvParams q = p;
   q.n_splits = n_splits;
   q.ks = ks;
