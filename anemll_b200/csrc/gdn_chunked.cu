@@ -27,7 +27,7 @@
 // products as two accumulating MMAs; S^T and W^T are single-precision-of-the-
 // input-type operands; the Vn P^T product runs in fp16.  A CPU emulation of
 // every rounding point gives output rel-L2 ~3e-4 and state rel-L2 ~3e-6
-// against an fp64 recurrence (bf16 inputs, cfg0 distributions).
+// against an fp64 recurrence (bf16 inputs, the layer's input and gate distributions).
 //
 // Occupancy: two CTAs per SM (256 threads, 256 TMEM columns and ~112 KB of
 // shared memory each).  Warps w and w + 4 share TMEM lane quarter w and split

@@ -1,4 +1,4 @@
-"""The cfg4 hybrid decoder stack on one GPU (or one shard of sequences per rank).
+"""The 24-layer hybrid decoder stack on one GPU (or one shard of sequences per rank).
 
 Embedding -> 24 layers -> final RMSNorm -> LM head -> in-model argmax (greedy next token).  Layer i
 is a full-attention layer iff (i + 1) % 4 == 0 (18 gated-DeltaNet layers, 6 attention layers), each

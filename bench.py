@@ -770,7 +770,7 @@ def _load_layer(layer, w):
 
 
 def bench_gdn_layer(args, ws, rank, local):
-    """One Qwen3.5 gated delta-rule layer through the drop-in module (cfg0 shape).
+    """One Qwen3.5 gated delta-rule layer through the drop-in module.
 
     B=1 per rank, a 512-token prefill then 64 decode steps, hidden 2048, bf16,
     random-init weights.  The input/output projections are torch GEMMs.  The
@@ -1193,7 +1193,7 @@ def cpu_prefill_sample(threads, T=2048):
 
 
 def cpu_kv_sample(threads, window, n_chunks=4, n_dec=8):
-    """Oracle KV attention calls (cfg2 shape) on the host; returns tokens/s."""
+    """Oracle KV attention calls (H_q 16, H_kv 2, hd 256, ctx 4096) on the host; returns tokens/s."""
     from anemll_b200 import inputs
     from oracle import kv_attention as ok
     torch.set_num_threads(threads)

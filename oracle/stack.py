@@ -1,4 +1,4 @@
-"""CPU oracle of the cfg4 hybrid stack's layers (test infrastructure only).
+"""CPU oracle of the 24-layer hybrid stack's layers (test infrastructure only).
 
 Each layer is restated in fp32 from its weights (copied from the device model), rounding to bf16
 exactly where the device path materialises bf16 tensors (GEMM outputs, norms, rotary outputs,

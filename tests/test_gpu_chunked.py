@@ -104,7 +104,7 @@ def test_split_at_chunk_boundary_is_bit_exact():
 
 
 def test_chunked_agrees_with_recurrent_kernel_at_full_prefill_shape():
-    """cfg3 head shape on the device only (no CPU oracle): B=8 sequences of 8192
+    """The long-prefill head shape on the device only (no CPU oracle): B=8 sequences of 8192
     tokens, chunked vs token-recurrent kernel, both against each other."""
     w = inputs.gdn_prefill_device(B=8, T=8192)
     s_c = torch.zeros(8, 32, 128, 128, device=DEV)

@@ -85,7 +85,7 @@ def test_fused_cache_write_bit_exact_vs_reference():
 
 
 @pytest.mark.parametrize("window", [0, 512])
-def test_cfg2_chunked_prefill_and_decode(window):
+def test_chunked_prefill_and_decode_over_a_4096_cache(window):
     """H_q=16, H_kv=2, hd=256, ctx 4096, fp16: 31 x 64-token chunks at 2048..4031, then
     64 decode steps at 4032..4095, causal and 512-token sliding window; every
     output within tolerance, the final cache bit-exact."""
